@@ -1,0 +1,198 @@
+/*
+ * lora_b200.h -- C ABI of the B200 (sm_100a) LoRA-linear kernels.
+ *
+ * Computes the LoRA linear  y = x.W^T + bias + sum_a s_a (x.A_a^T).B_a^T  and
+ * its pieces, behind plain pointers and sizes so that any host language can
+ * bind it (ctypes, cgo, JNI, N-API).  Storage layouts follow PyTorch / PEFT:
+ *   W    = nn.Linear.weight   [N, K] row-major
+ *   A    = lora_A.weight      [R, K] row-major
+ *   B    = lora_B.weight      [N, R] row-major
+ * Row strides ("ld*") are in elements; the innermost stride is always 1.
+ *
+ * Conventions shared by every entry point:
+ *   - all tensor pointers are device pointers on the current CUDA device;
+ *   - `stream` is a cudaStream_t (NULL = legacy default stream); every launch
+ *     goes on it and no entry point synchronises the host;
+ *   - the return value is a lora_status; no exception crosses the ABI;
+ *   - dtype is LORA_F16 or LORA_BF16 for activations and weights; some
+ *     intermediate z buffers may be LORA_F32 where stated.
+ *
+ * Each declaration names the reference function (lishenghui/probe,
+ * loraforge_kernels/, file:line) whose GPU work it replaces.
+ */
+#ifndef LORA_B200_H
+#define LORA_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define LORA_API __attribute__((visibility("default")))
+#else
+#define LORA_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum lora_status {
+  LORA_OK = 0,
+  LORA_ERR_SHAPE = 1,       /* inconsistent or unsupported sizes            */
+  LORA_ERR_ALIGN = 2,       /* pointer / stride alignment not met           */
+  LORA_ERR_DTYPE = 3,       /* unsupported dtype combination                */
+  LORA_ERR_DEVICE = 4,      /* no usable sm_100 device                      */
+  LORA_ERR_INDEX = 5,       /* adapter id / offset out of range             */
+  LORA_ERR_CUDA = 6,        /* a CUDA runtime / driver call failed          */
+  LORA_ERR_TIMEOUT = 7,     /* a bounded device wait ran out                */
+  LORA_ERR_WORKSPACE = 8,   /* workspace missing or too small               */
+  LORA_ERR_UNSUPPORTED = 9, /* valid request this build does not implement  */
+  LORA_ERR_ARG = 10         /* NULL pointer or invalid argument             */
+};
+
+enum lora_dtype { LORA_F16 = 0, LORA_BF16 = 1, LORA_F32 = 2 };
+
+/* Layout of a LoRA up-projection B as seen by the expand kernels. */
+enum lora_b_layout {
+  LORA_B_PEFT = 0,      /* B[n * ldb + j]  : lora_B.weight [N, R]            */
+  LORA_B_RANK_MAJOR = 1 /* B[j * ldb + n]  : flat table [sum R, N]           */
+};
+
+/* ABI version of this library (bumped on any signature change). */
+LORA_API int lora_b200_abi_version(void);
+
+/* Human-readable name of a lora_status value. */
+LORA_API const char* lora_b200_status_string(int status);
+
+/* Reads and clears the device-side error word of `device` (a bounded wait
+ * that ran out, or an adapter id out of range seen on the device).  Waits for
+ * the device to finish its queued work.  *code = 0 when nothing was recorded.
+ * No reference counterpart: the reference's Triton kernels have no device
+ * error channel. */
+LORA_API int lora_b200_device_error(int device, int* code);
+
+/* ---------------------------------------------------------------------------
+ * Dense fused LoRA GEMM on tcgen05 tensor cores (TMA -> smem -> TMEM).
+ *
+ *   out[M,N] = alpha * ( x[M,K] . w[N,K]^T  +  z[M,R] . bw[N,R]^T ) + bias[N]
+ *
+ * The second product is the LoRA expand folded in as an extra K-slice
+ * ("K-concat"): z = s * x . A^T comes from lora_shrink, bw is lora_B.weight
+ * zero-padded to width ldbw.  R = 0 (z, bw NULL) gives a plain linear.
+ * Requirements: 16-byte aligned pointers; ldx, ldw multiples of 8 and >= K;
+ * K a multiple of 8; when R > 0, ldz and ldbw >= roundup(R, 64), multiples of
+ * 8, and columns [R, roundup(R,64)) of z and bw are zero.  bias may be NULL.
+ * Replaces: _fused_lora_gemm_kernel / fused_gemm (fused_linear.py:229-317),
+ * _kconcat (fused_linear.py:676-677), the cuBLAS GEMM of _concat / _hybrid
+ * (fused_linear.py:362-373) and cutlass_gemm (csrc/cutlass_gemm_gate.cu:91-106).
+ * ------------------------------------------------------------------------- */
+LORA_API int lora_gemm(const void* x, int64_t ldx, const void* w, int64_t ldw, const void* z, int64_t ldz,
+              const void* bw, int64_t ldbw, const void* bias, void* out, int64_t ldo, int64_t M,
+              int64_t N, int64_t K, int64_t R, float alpha, int dtype, void* stream);
+
+/* ---------------------------------------------------------------------------
+ * Split-K rank shrink  z[M, z_width] = scale * x[M,K] . a[R,K]^T
+ * Columns [R, z_width) of z are written with zeros.  z_dtype may be LORA_F32
+ * or the input dtype.  split_k slices of K run in separate CTAs; their fp32
+ * partials are summed in a fixed order by the last CTA to finish (no float
+ * atomics: the result is deterministic).  split_k == 0 picks a value.
+ * Workspace: lora_shrink_workspace_size() bytes, zero-filled before its first
+ * use; the kernel leaves its counters at zero again on return, so the same
+ * workspace can be reused (and captured in a CUDA graph) without re-zeroing.
+ * Calls that share one workspace must not overlap on the GPU.
+ * Replaces: _splitk_shrink_kernel + torch sum / splitk_lora_shrink
+ * (splitk_lora.py:22-63,104-126), _splitk_shrink_partial / _splitk_shrink_atomic
+ * (splitk_shrink.py:34-141), the x.A^T half of the fused_lora / tiled_lora /
+ * classed_* / grouped_lora kernels (fused_lora.py:10-200) and build_ext's shrink
+ * (fused_linear.py:662-673).
+ * ------------------------------------------------------------------------- */
+LORA_API size_t lora_shrink_workspace_size(int64_t M, int64_t R, int split_k);
+LORA_API int lora_shrink_pick_split_k(int64_t M, int64_t K, int64_t R);
+LORA_API int lora_shrink(const void* x, int64_t ldx, const void* a, int64_t lda, void* z, int64_t ldz,
+                int z_dtype, int64_t z_width, int64_t M, int64_t K, int64_t R, float scale,
+                int dtype, int split_k, void* workspace, size_t workspace_bytes, void* stream);
+
+/* ---------------------------------------------------------------------------
+ * Expand + add   out[M,N] = y[M,N] + scale * z[M,R] . B^T + bias[N]
+ * y may be NULL (treated as zero) and may not alias out.  z is f32 or the
+ * input dtype (rounded to the input dtype before the tensor-core product).
+ * b_layout selects LORA_B_PEFT ([N,R]) or LORA_B_RANK_MAJOR ([R,N]).
+ * Replaces: _expand_add_kernel / expand_add (fused_linear.py:112-200),
+ * _persistent_expand_add_kernel (splitk_lora.py:66-153) and the expand half of
+ * the fused_lora / tiled_lora / classed_* / grouped_lora kernels
+ * (fused_lora.py:10-200).
+ * ------------------------------------------------------------------------- */
+LORA_API int lora_expand_add(const void* y, int64_t ldy, const void* z, int64_t ldz, int z_dtype,
+                    const void* b, int64_t ldb, int b_layout, const void* bias, void* out,
+                    int64_t ldo, int64_t M, int64_t N, int64_t R, float scale, int dtype,
+                    void* stream);
+
+/* ---------------------------------------------------------------------------
+ * Decode linear (small M): out[M,N] = x . w^T + scale * z . b^T + bias
+ * Streams w once with split-K over CTAs; z ([M,R], input dtype or f32) comes
+ * from lora_shrink and may be NULL when R == 0.  b is lora_B.weight [N,R].
+ * M <= 64.  Workspace: lora_decode_workspace_size() bytes, zero-filled before
+ * first use (self-resetting counters, as for lora_shrink).
+ * Replaces: _decode_linear_kernel / build_decode_linear / decode_lora_linear
+ * (decode_linear.py:13-100).
+ * ------------------------------------------------------------------------- */
+LORA_API size_t lora_decode_workspace_size(int64_t M, int64_t N, int split_k);
+LORA_API int lora_decode_pick_split_k(int64_t M, int64_t N, int64_t K);
+LORA_API int lora_decode_linear(const void* x, int64_t ldx, const void* w, int64_t ldw, const void* z,
+                       int64_t ldz, int z_dtype, const void* b, int64_t ldb, const void* bias,
+                       void* out, int64_t ldo, int64_t M, int64_t N, int64_t K, int64_t R,
+                       float scale, int dtype, int split_k, void* workspace,
+                       size_t workspace_bytes, void* stream);
+
+/* ---------------------------------------------------------------------------
+ * Segmented multi-adapter LoRA (SGMV / BGMV).
+ *
+ * Adapter tables: a_flat rows (offsets[a] .. offsets[a]+ranks[a]) hold adapter
+ * a's lora_A rows ([sum R, K] flat, or a padded [n, r_max, K] stack viewed as
+ * [n*r_max, K] with offsets[a] = a*r_max).  B element (adapter a, rank j,
+ * output n) is b[offsets[a]*N + j*b_sj + n*b_sn]: the flat rank-major table
+ * [sum R, N] has (b_sj, b_sn) = (N, 1); a padded PEFT stack [n, N, r_max] has
+ * (1, r_max).  offsets / ranks are int64 device arrays of n_adapters entries.
+ *
+ * lora_sgmv_schedule builds the tile list on the device: token blocks of 64
+ * split wherever the adapter changes, from either per-token ids (ids[T]) or
+ * segments (seg_start[S+1], seg_adapter[S]; pass ids = NULL).  The list lives
+ * in `tiles`, an int32 buffer of lora_sgmv_tiles_size(T, S) bytes.  Ids out of
+ * range become rank-0 tiles and set the device error word (LORA_ERR_INDEX).
+ * Replaces the per-token / per-request adapter lookup of _ragged_shrink_kernel
+ * (multilora.py:128-182), _bgmv_shrink_kernel (multilora.py:51-104),
+ * _shrink / _expand of segmented_branch.py:12-60 and ragged_branch.py:6-40.
+ * ------------------------------------------------------------------------- */
+LORA_API size_t lora_sgmv_tiles_size(int64_t T, int64_t S);
+LORA_API int lora_sgmv_schedule(const int64_t* ids, const int64_t* seg_start, const int64_t* seg_adapter,
+                       int64_t T, int64_t S, int64_t n_adapters, int32_t* tiles,
+                       size_t tiles_bytes, void* stream);
+
+/* z[t, :] = scale * x[t] . A_{a(t)}^T for every token, zero beyond the
+ * token's rank up to z_width.  Workspace: lora_sgmv_shrink_workspace_size()
+ * bytes, zero-filled before first use (self-resetting counters).
+ * rows (optional, int64 [T]): logical token t of the schedule reads x row
+ * rows[t] and writes z row rows[t] (a gather / scatter by index, e.g. the
+ * adapter-sorted order of lora_sgmv_sort or a rank bucket's positions);
+ * NULL = identity. */
+LORA_API size_t lora_sgmv_shrink_workspace_size(int64_t T, int64_t S, int64_t z_width, int split_k);
+LORA_API int lora_sgmv_shrink(const void* x, int64_t ldx, const void* a_flat, int64_t lda,
+                     const int64_t* offsets, const int64_t* ranks, int64_t n_adapters,
+                     const int32_t* tiles, const int64_t* rows, void* z, int64_t ldz, int z_dtype, int64_t z_width,
+                     int64_t T, int64_t S, int64_t K, int64_t r_max, float scale, int dtype,
+                     int split_k, void* workspace, size_t workspace_bytes, void* stream);
+
+/* out[t, :] = y[t, :] + scale * z[t, :r] . B_{a(t)}^T ; y may be NULL.
+ * rows (optional): logical token t uses row rows[t] of y, z and out. */
+LORA_API int lora_sgmv_expand(const void* y, int64_t ldy, const void* z, int64_t ldz, int z_dtype,
+                     const void* b, int64_t b_sj, int64_t b_sn, const int64_t* offsets,
+                     const int64_t* ranks, int64_t n_adapters, const int32_t* tiles,
+                     const int64_t* rows, void* out,
+                     int64_t ldo, int64_t T, int64_t S, int64_t N, int64_t r_max, float scale,
+                     int dtype, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* LORA_B200_H */

@@ -1,0 +1,250 @@
+// Shared device helpers for the LoRA-linear kernels (sm_100a only).
+//
+// Everything here is inline PTX for the Blackwell data path: mbarrier
+// pipelines, TMA tile loads, tcgen05 MMA / TMEM access, plus the bounded
+// waits every spin loop in this library goes through.  A wait that runs out
+// records an error code in a device word that the host can read back
+// (lora_b200_device_error) instead of trapping or hanging the GPU.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "lora_b200.h"
+
+#define LORA_DEVINL __device__ __forceinline__
+
+namespace lora {
+
+// Bounded waits give up after this many nanoseconds of %globaltimer.  No
+// legitimate wait in these kernels lasts longer than a few microseconds.
+constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s
+
+// Device-side error codes (written with atomicCAS so the first one sticks).
+constexpr int kDevErrTimeoutFull = 101;
+constexpr int kDevErrTimeoutEmpty = 102;
+constexpr int kDevErrTimeoutAccFull = 103;
+constexpr int kDevErrTimeoutAccEmpty = 104;
+constexpr int kDevErrTimeoutSplitK = 105;
+constexpr int kDevErrBadIndex = 110;
+
+LORA_DEVINL uint64_t globaltimer_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+LORA_DEVINL void record_error(int* err, int code) {
+  if (err != nullptr) atomicCAS(err, 0, code);
+}
+
+// ------------------------------------------------------------------ dtypes
+template <typename T> struct Vec8;  // 8 half-precision values in one uint4
+
+LORA_DEVINL float to_f32(__nv_bfloat16 v) { return __bfloat162float(v); }
+LORA_DEVINL float to_f32(__half v) { return __half2float(v); }
+LORA_DEVINL float to_f32(float v) { return v; }
+
+template <typename T> LORA_DEVINL T from_f32(float v);
+template <> LORA_DEVINL __nv_bfloat16 from_f32<__nv_bfloat16>(float v) { return __float2bfloat16_rn(v); }
+template <> LORA_DEVINL __half from_f32<__half>(float v) { return __float2half_rn(v); }
+template <> LORA_DEVINL float from_f32<float>(float v) { return v; }
+
+// Pack two floats into one 32-bit word of the 16-bit type T.
+template <typename T> LORA_DEVINL uint32_t pack2(float lo, float hi);
+template <> LORA_DEVINL uint32_t pack2<__nv_bfloat16>(float lo, float hi) {
+  __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+template <> LORA_DEVINL uint32_t pack2<__half>(float lo, float hi) {
+  __half2 v = __floats2half2_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+
+template <typename T> LORA_DEVINL float2 unpack2(uint32_t w);
+template <> LORA_DEVINL float2 unpack2<__nv_bfloat16>(uint32_t w) {
+  __nv_bfloat162 v = *reinterpret_cast<__nv_bfloat162*>(&w);
+  return __bfloat1622float2(v);
+}
+template <> LORA_DEVINL float2 unpack2<__half>(uint32_t w) {
+  __half2 v = *reinterpret_cast<__half2*>(&w);
+  return __half22float2(v);
+}
+
+// ------------------------------------------------------- legacy mma.sync
+// m16n8k16 with fp32 accumulation; used by the skinny memory-bound kernels
+// (shrink / expand / decode GEMV), where HBM, not the tensor pipe, is the
+// bound.  The dense GEMM uses tcgen05 below.
+template <typename T> LORA_DEVINL void mma16816(float* c, const uint32_t* a, const uint32_t* b);
+template <> LORA_DEVINL void mma16816<__nv_bfloat16>(float* c, const uint32_t* a, const uint32_t* b) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 "
+      "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};\n"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[0]), "r"(b[1]));
+}
+template <> LORA_DEVINL void mma16816<__half>(float* c, const uint32_t* a, const uint32_t* b) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 "
+      "{%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};\n"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[0]), "r"(b[1]));
+}
+
+// Streaming 16-byte global load that does not allocate in L1.
+LORA_DEVINL uint4 ldg_stream(const void* p) {
+  uint4 v;
+  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+               : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+               : "l"(p));
+  return v;
+}
+
+// Programmatic dependent launch: let the next kernel in the stream start its
+// prologue, and wait for the previous kernel's results.
+LORA_DEVINL void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+LORA_DEVINL void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+// ------------------------------------------------------------ mbarriers
+LORA_DEVINL uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+LORA_DEVINL void mbar_init(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count));
+}
+
+LORA_DEVINL void fence_mbar_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+LORA_DEVINL void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+               : "memory");
+}
+
+LORA_DEVINL void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+LORA_DEVINL bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Wait for the phase with the given parity to complete.  Gives up after
+// kWaitLimitNs or as soon as *abort becomes non-zero; returns false then.
+LORA_DEVINL bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, volatile int* abort, int* err,
+                                   int code) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  while (true) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if (*abort) return false;
+    if (globaltimer_ns() - t0 > kWaitLimitNs) {
+      *abort = 1;
+      record_error(err, code);
+      return false;
+    }
+  }
+}
+
+// -------------------------------------------------------------------- TMA
+LORA_DEVINL void tma_prefetch_desc(const CUtensorMap* map) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+
+// 2-D tiled load into this CTA's shared memory (no multicast).
+LORA_DEVINL void tma_load_2d(const CUtensorMap* map, void* smem_dst, uint64_t* bar, int32_t c0,
+                             int32_t c1) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes "
+      "[%0], [%1, {%3, %4}], [%2];" ::"r"(smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1)
+      : "memory");
+}
+
+// ---------------------------------------------------------------- tcgen05
+LORA_DEVINL void tmem_alloc(uint32_t* dst_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                   smem_u32(dst_smem)),
+               "r"(ncols)
+               : "memory");
+}
+LORA_DEVINL void tmem_relinquish() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+LORA_DEVINL void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols)
+               : "memory");
+}
+LORA_DEVINL void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+LORA_DEVINL void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// D[tmem] (+)= A[smem] * B[smem]^T, kind::f16 (bf16 or f16 inputs, fp32 accumulate).
+LORA_DEVINL void tc_mma_f16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                            uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Arrive once on the mbarrier when all previously issued tcgen05.mma of this
+// thread have completed.
+LORA_DEVINL void tc_commit(uint64_t* bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                   smem_u32(bar))
+               : "memory");
+}
+
+// 32 lanes x 32 bit, 16 consecutive columns per thread.
+LORA_DEVINL void tmem_ld_32x32b_x16(uint32_t taddr, uint32_t* r) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15])
+      : "r"(taddr));
+}
+LORA_DEVINL void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// Shared-memory matrix descriptor for a K-major tile written by TMA with
+// 128-byte swizzle: rows of 64 16-bit elements (128 B), 8-row groups 1024 B
+// apart.  Fields (sm_100 UMMA descriptor): start>>4 [0,14), LBO>>4 [16,30)
+// (unused for swizzled K-major, set to 1), SBO>>4 [32,46), version=1 [46,48),
+// base offset 0 [49,52), layout SWIZZLE_128B=2 [61,64).
+LORA_DEVINL uint64_t umma_desc_sw128(uint32_t smem_addr) {
+  uint64_t d = 0;
+  d |= (uint64_t)((smem_addr >> 4) & 0x3FFF);
+  d |= (uint64_t)1 << 16;
+  d |= (uint64_t)(1024 >> 4) << 32;
+  d |= (uint64_t)1 << 46;
+  d |= (uint64_t)2 << 61;
+  return d;
+}
+
+// Instruction descriptor for kind::f16, fp32 accumulator, both operands
+// K-major, dense.  a_fmt/b_fmt: 0 = f16, 1 = bf16.
+__host__ __device__ constexpr uint32_t umma_idesc_f16(int m, int n, int ab_fmt) {
+  return (1u << 4)                         // D format f32
+         | ((uint32_t)ab_fmt << 7)         // A format
+         | ((uint32_t)ab_fmt << 10)        // B format
+         | ((uint32_t)(n >> 3) << 17)      // N >> 3
+         | ((uint32_t)(m >> 4) << 24);     // M >> 4
+}
+
+}  // namespace lora

@@ -1,0 +1,387 @@
+// Dense fused LoRA GEMM on Blackwell tensor cores.
+//
+//   out[M,N] = alpha * ( x[M,K] . W[N,K]^T + z[M,R] . Bw[N,R]^T ) + bias[N]
+//
+// The LoRA expand rides along as an extra K-slice: after the K/64 blocks of
+// (x, W) the mainloop continues over ceil(R/64) blocks of (z, Bw) into the
+// same TMEM accumulator, so the base output is written exactly once.  This is
+// the B200 form of the reference's _kconcat ([x | s.z] @ [W | B]^T,
+// fused_linear.py:622-677) without materialising the concatenated operands:
+// two TMA descriptor pairs feed one accumulator.
+//
+// Structure (one persistent CTA per SM, 192 threads):
+//   warp 0      TMA producer: 128x64 x-tile + BNx64 W-tile per stage (128B swizzle)
+//   warp 1      MMA issuer: tcgen05.mma M=128 N=BN K=16, fp32 accumulator in TMEM
+//   warps 2..5  epilogue: tcgen05.ld -> alpha, bias, cast -> 32B stores
+// Two TMEM accumulators (2*BN columns) let the epilogue of tile i overlap the
+// mainloop of tile i+1.  Tiles are rasterised in GROUP_M bands so the W tiles
+// of a band stay L2-resident (the reference's GROUP_M swizzle,
+// fused_linear.py:245-254).  No cluster launch and no TMA multicast.
+#include <cudaTypedefs.h>
+
+#include <mutex>
+#include <type_traits>
+
+#include "common.cuh"
+#include "runtime.h"
+
+namespace lora {
+
+constexpr int kGemmBM = 128;
+constexpr int kGemmBK = 64;
+constexpr int kGemmThreads = 192;
+
+struct GemmArgs {
+  void* out;
+  const void* bias;
+  int* err;
+  int64_t ldo;
+  int M, N, K, R;
+  int num_kb_main, num_kb_tail, tail_last_k16;
+  int num_m_tiles, num_n_tiles, num_tiles, group_m;
+  float alpha;
+};
+
+LORA_DEVINL void gemm_tile_coords(int tile, const GemmArgs& a, int& mt, int& nt) {
+  const int group_size = a.group_m * a.num_n_tiles;
+  const int group = tile / group_size;
+  const int first_m = group * a.group_m;
+  const int gm = min(a.num_m_tiles - first_m, a.group_m);
+  const int in_group = tile - group * group_size;
+  mt = first_m + in_group % gm;
+  nt = in_group / gm;
+}
+
+template <int BN, int STAGES, typename T>
+struct GemmSmem {
+  static constexpr int kABytes = kGemmBM * kGemmBK * 2;
+  static constexpr int kBBytes = BN * kGemmBK * 2;
+  static constexpr int kStageBytes = kABytes + kBBytes;
+  static constexpr int kBarOffset = STAGES * kStageBytes;
+  static constexpr int kBytes = kBarOffset + 256 + 1024;  // barriers + alignment slack
+};
+
+template <int BN, int STAGES, typename T>
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_w,
+                   const __grid_constant__ CUtensorMap tm_z, const __grid_constant__ CUtensorMap tm_b,
+                   const GemmArgs args) {
+  using L = GemmSmem<BN, STAGES, T>;
+  constexpr uint32_t kTmemCols = 2 * BN;  // 128, 256 or 512: a power of two >= 32
+  constexpr uint32_t kIdesc = umma_idesc_f16(kGemmBM, BN, std::is_same<T, __nv_bfloat16>::value ? 1 : 0);
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  uint8_t* sm_a = smem;
+  uint8_t* sm_b = smem + STAGES * L::kABytes;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::kBarOffset);
+  uint64_t* empty = full + STAGES;
+  uint64_t* acc_full = empty + STAGES;
+  uint64_t* acc_empty = acc_full + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&acc_full[a], 1);
+      mbar_init(&acc_empty[a], 4);
+    }
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tm_x);
+    tma_prefetch_desc(&tm_w);
+    if (args.num_kb_tail > 0) {
+      tma_prefetch_desc(&tm_z);
+      tma_prefetch_desc(&tm_b);
+    }
+  }
+  if (warp == 2) {
+    tmem_alloc(tmem_slot, kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  const int num_kb = args.num_kb_main + args.num_kb_tail;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; ok && tile < args.num_tiles; tile += gridDim.x) {
+        int mt, nt;
+        gemm_tile_coords(tile, args, mt, nt);
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait_bounded(&empty[stage], phase ^ 1, abort_flag, args.err, kDevErrTimeoutEmpty)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&full[stage], L::kStageBytes);
+          if (kb < args.num_kb_main) {
+            tma_load_2d(&tm_x, sm_a + stage * L::kABytes, &full[stage], kb * kGemmBK, mt * kGemmBM);
+            tma_load_2d(&tm_w, sm_b + stage * L::kBBytes, &full[stage], kb * kGemmBK, nt * BN);
+          } else {
+            const int kt = kb - args.num_kb_main;
+            tma_load_2d(&tm_z, sm_a + stage * L::kABytes, &full[stage], kt * kGemmBK, mt * kGemmBM);
+            tma_load_2d(&tm_b, sm_b + stage * L::kBBytes, &full[stage], kt * kGemmBK, nt * BN);
+          }
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------------------------------------------------- MMA issuer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int local = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; ok && tile < args.num_tiles; tile += gridDim.x, ++local) {
+        const int acc = local & 1;
+        const uint32_t acc_phase = (local >> 1) & 1;
+        if (!mbar_wait_bounded(&acc_empty[acc], acc_phase ^ 1, abort_flag, args.err,
+                               kDevErrTimeoutAccEmpty)) {
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait_bounded(&full[stage], phase, abort_flag, args.err, kDevErrTimeoutFull)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint64_t adesc = umma_desc_sw128(smem_u32(sm_a + stage * L::kABytes));
+          const uint64_t bdesc = umma_desc_sw128(smem_u32(sm_b + stage * L::kBBytes));
+          // The last tail block only holds ceil(R%64 / 16) non-zero K16 steps.
+          const int nk = (kb == num_kb - 1 && args.num_kb_tail > 0) ? args.tail_last_k16 : 4;
+          for (int k = 0; k < nk; ++k) {
+            // +32 bytes per K16 step inside the 128B swizzle atom (>>4 => +2).
+            tc_mma_f16(d_tmem, adesc + static_cast<uint64_t>(2 * k), bdesc + static_cast<uint64_t>(2 * k),
+                       kIdesc, (kb > 0 || k > 0) ? 1u : 0u);
+          }
+          tc_commit(&empty[stage]);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (ok) tc_commit(&acc_full[acc]);
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int quad = warp & 3;  // TMEM lanes [32*quad, 32*quad+32) belong to this warp
+    const T* bias = static_cast<const T*>(args.bias);
+    const bool vec_ok = (args.ldo % 8) == 0 && (reinterpret_cast<uintptr_t>(args.out) % 16) == 0;
+    int local = 0;
+    for (int tile = blockIdx.x; tile < args.num_tiles; tile += gridDim.x, ++local) {
+      const int acc = local & 1;
+      const uint32_t acc_phase = (local >> 1) & 1;
+      int mt, nt;
+      gemm_tile_coords(tile, args, mt, nt);
+      if (!mbar_wait_bounded(&acc_full[acc], acc_phase, abort_flag, args.err, kDevErrTimeoutAccFull)) break;
+      tc_fence_after();
+      const int row = mt * kGemmBM + quad * 32 + lane;
+      T* out_row = static_cast<T*>(args.out) + static_cast<int64_t>(row) * args.ldo;
+      const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + static_cast<uint32_t>(acc * BN);
+#pragma unroll 1
+      for (int c = 0; c < BN; c += 16) {
+        uint32_t r[16];
+        tmem_ld_32x32b_x16(t_row + c, r);
+        tmem_wait_ld();
+        const int col0 = nt * BN + c;
+        if (row < args.M && col0 < args.N) {
+          float v[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]) * args.alpha;
+          if (bias != nullptr) {
+#pragma unroll
+            for (int i = 0; i < 16; ++i)
+              if (col0 + i < args.N) v[i] += to_f32(bias[col0 + i]);
+          }
+          if (vec_ok && col0 + 16 <= args.N) {
+            uint4 w0, w1;
+            w0.x = pack2<T>(v[0], v[1]);
+            w0.y = pack2<T>(v[2], v[3]);
+            w0.z = pack2<T>(v[4], v[5]);
+            w0.w = pack2<T>(v[6], v[7]);
+            w1.x = pack2<T>(v[8], v[9]);
+            w1.y = pack2<T>(v[10], v[11]);
+            w1.z = pack2<T>(v[12], v[13]);
+            w1.w = pack2<T>(v[14], v[15]);
+            uint4* dst = reinterpret_cast<uint4*>(out_row + col0);
+            dst[0] = w0;
+            dst[1] = w1;
+          } else {
+#pragma unroll
+            for (int i = 0; i < 16; ++i)
+              if (col0 + i < args.N) out_row[col0 + i] = from_f32<T>(v[i]);
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[acc]);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 2) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, kTmemCols);
+  }
+}
+
+// ------------------------------------------------------------------- host
+namespace {
+
+bool encode_tile_map(CUtensorMap* map, const void* ptr, int dtype, uint64_t inner, uint64_t outer,
+                     uint64_t ld_elems, uint32_t box_inner, uint32_t box_outer) {
+  auto encode = tensor_map_encoder();
+  if (encode == nullptr) return false;
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {ld_elems * 2};
+  cuuint32_t box[2] = {box_inner, box_outer};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = encode(map, dtype == LORA_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
+                      2, const_cast<void*>(ptr), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                      CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+template <int BN, int STAGES, typename T>
+int launch_gemm(const void* x, int64_t ldx, const void* w, int64_t ldw, const void* z, int64_t ldz,
+                const void* bw, int64_t ldbw, const void* bias, void* out, int64_t ldo, int64_t M,
+                int64_t N, int64_t K, int64_t R, float alpha, int dtype, cudaStream_t stream) {
+  using L = GemmSmem<BN, STAGES, T>;
+  const int dev = current_device();
+  if (dev < 0) return LORA_ERR_DEVICE;
+  const DeviceInfo& info = device_info(dev);
+
+  CUtensorMap tm_x, tm_w, tm_z, tm_b;
+  const uint64_t r64 = static_cast<uint64_t>((R + 63) / 64) * 64;
+  if (!encode_tile_map(&tm_x, x, dtype, K, M, ldx, kGemmBK, kGemmBM)) return LORA_ERR_CUDA;
+  if (!encode_tile_map(&tm_w, w, dtype, K, N, ldw, kGemmBK, BN)) return LORA_ERR_CUDA;
+  if (R > 0) {
+    if (!encode_tile_map(&tm_z, z, dtype, r64, M, ldz, kGemmBK, kGemmBM)) return LORA_ERR_CUDA;
+    if (!encode_tile_map(&tm_b, bw, dtype, r64, N, ldbw, kGemmBK, BN)) return LORA_ERR_CUDA;
+  } else {
+    tm_z = tm_x;
+    tm_b = tm_w;
+  }
+
+  GemmArgs a;
+  a.out = out;
+  a.bias = bias;
+  a.err = info.err_word;
+  a.ldo = ldo;
+  a.M = static_cast<int>(M);
+  a.N = static_cast<int>(N);
+  a.K = static_cast<int>(K);
+  a.R = static_cast<int>(R);
+  a.num_kb_main = static_cast<int>((K + kGemmBK - 1) / kGemmBK);
+  a.num_kb_tail = static_cast<int>((R + kGemmBK - 1) / kGemmBK);
+  const int tail_rem = static_cast<int>(R - static_cast<int64_t>(a.num_kb_tail - 1) * kGemmBK);
+  a.tail_last_k16 = a.num_kb_tail > 0 ? (tail_rem + 15) / 16 : 4;
+  a.num_m_tiles = static_cast<int>((M + kGemmBM - 1) / kGemmBM);
+  a.num_n_tiles = static_cast<int>((N + BN - 1) / BN);
+  a.num_tiles = a.num_m_tiles * a.num_n_tiles;
+  a.group_m = 8;
+  a.alpha = alpha;
+
+  auto kernel = gemm_tc_kernel<BN, STAGES, T>;
+  static std::once_flag once[64];
+  static cudaError_t attr_err[64];
+  std::call_once(once[dev & 63], [&] {
+    attr_err[dev & 63] = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kBytes);
+  });
+  if (attr_err[dev & 63] != cudaSuccess) return LORA_ERR_CUDA;
+  const int grid = static_cast<int>(std::min<int64_t>(a.num_tiles, info.num_sms));
+  kernel<<<grid, kGemmThreads, L::kBytes, stream>>>(tm_x, tm_w, tm_z, tm_b, a);
+  return cudaGetLastError() == cudaSuccess ? LORA_OK : LORA_ERR_CUDA;
+}
+
+template <typename T>
+int dispatch_gemm(int bn, const void* x, int64_t ldx, const void* w, int64_t ldw, const void* z, int64_t ldz,
+                  const void* bw, int64_t ldbw, const void* bias, void* out, int64_t ldo, int64_t M, int64_t N,
+                  int64_t K, int64_t R, float alpha, int dtype, cudaStream_t stream) {
+  switch (bn) {
+    case 64:
+      return launch_gemm<64, 8, T>(x, ldx, w, ldw, z, ldz, bw, ldbw, bias, out, ldo, M, N, K, R, alpha, dtype, stream);
+    case 128:
+      return launch_gemm<128, 6, T>(x, ldx, w, ldw, z, ldz, bw, ldbw, bias, out, ldo, M, N, K, R, alpha, dtype,
+                                    stream);
+    default:
+      return launch_gemm<256, 4, T>(x, ldx, w, ldw, z, ldz, bw, ldbw, bias, out, ldo, M, N, K, R, alpha, dtype,
+                                    stream);
+  }
+}
+
+inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+}  // namespace
+
+// Tile width: narrow outputs (a rank-r shrink, N <= 128) get the narrowest
+// tile that covers them; wide ones use 256 unless that leaves fewer than two
+// waves of tiles on the machine.
+int gemm_pick_bn(int64_t M, int64_t N, int num_sms) {
+  if (N <= 64) return 64;
+  if (N <= 128) return 128;
+  const int64_t mt = (M + kGemmBM - 1) / kGemmBM;
+  const int64_t tiles256 = mt * ((N + 255) / 256);
+  if (tiles256 >= 2 * num_sms || N % 256 == 0) return 256;
+  return 128;
+}
+
+}  // namespace lora
+
+extern "C" int lora_gemm(const void* x, int64_t ldx, const void* w, int64_t ldw, const void* z, int64_t ldz,
+                         const void* bw, int64_t ldbw, const void* bias, void* out, int64_t ldo, int64_t M,
+                         int64_t N, int64_t K, int64_t R, float alpha, int dtype, void* stream) {
+  using namespace lora;
+  if (x == nullptr || w == nullptr || out == nullptr) return LORA_ERR_ARG;
+  if (dtype != LORA_BF16 && dtype != LORA_F16) return LORA_ERR_DTYPE;
+  if (M < 0 || N < 0 || K < 0 || R < 0) return LORA_ERR_SHAPE;
+  if (M == 0 || N == 0) return LORA_OK;
+  if (K == 0 && R == 0) return LORA_ERR_UNSUPPORTED;
+  if (M > INT32_MAX || N > INT32_MAX || K > INT32_MAX || R > INT32_MAX) return LORA_ERR_SHAPE;
+  if (ldx < K || ldw < K || ldo < N) return LORA_ERR_SHAPE;
+  if (K % 8 != 0 || ldx % 8 != 0 || ldw % 8 != 0) return LORA_ERR_ALIGN;
+  if (!aligned16(x) || !aligned16(w)) return LORA_ERR_ALIGN;
+  if (K == 0) return LORA_ERR_UNSUPPORTED;
+  if (R > 0) {
+    if (z == nullptr || bw == nullptr) return LORA_ERR_ARG;
+    const int64_t r64 = (R + 63) / 64 * 64;
+    if (ldz < r64 || ldbw < r64) return LORA_ERR_SHAPE;
+    if (ldz % 8 != 0 || ldbw % 8 != 0 || !aligned16(z) || !aligned16(bw)) return LORA_ERR_ALIGN;
+  }
+  const int dev = current_device();
+  if (dev < 0) return LORA_ERR_DEVICE;
+  const DeviceInfo& info = device_info(dev);
+  if (!info.is_sm100) return LORA_ERR_DEVICE;
+  const int bn = gemm_pick_bn(M, N, info.num_sms);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (dtype == LORA_BF16)
+    return dispatch_gemm<__nv_bfloat16>(bn, x, ldx, w, ldw, z, ldz, bw, ldbw, bias, out, ldo, M, N, K, R, alpha,
+                                        dtype, s);
+  return dispatch_gemm<__half>(bn, x, ldx, w, ldw, z, ldz, bw, ldbw, bias, out, ldo, M, N, K, R, alpha, dtype, s);
+}

@@ -1,0 +1,149 @@
+// Device-side tile scheduling for segmented multi-adapter LoRA.
+//
+// The serving batch arrives either as per-token adapter ids (ragged_branch,
+// multilora BGMV) or as contiguous request segments (segmented_branch).  One
+// 1024-thread CTA turns either form into a list of tiles of <= 64 consecutive
+// tokens that share one adapter: a tile starts at every 64-token boundary and
+// wherever the adapter changes.  The shrink / expand kernels then walk that
+// list, so a segment's adapter rows are fetched once per 64 tokens instead of
+// once per token, and no host synchronisation is needed (the tile count stays
+// on the device).  Segments may have any length -- the Zipf-distributed
+// request lengths of a real batch -- unlike the reference's segmented_branch,
+// which requires equal-length requests (segmented_branch.py:50-53).
+#include <algorithm>
+
+#include "common.cuh"
+#include "runtime.h"
+#include "sgmv.h"
+
+namespace lora {
+
+namespace {
+
+// Adapter of token t, or -1 (out of range / not covered by any segment).
+struct AdapterLookup {
+  const int64_t* ids;
+  const int64_t* seg_start;
+  const int64_t* seg_adapter;
+  int T, S, n_adapters;
+  int* err;
+
+  __device__ int find_segment(int t) const {
+    // largest s with seg_start[s] <= t, s in [0, S)
+    int lo = 0, hi = S - 1, ans = -1;
+    while (lo <= hi) {
+      const int mid = (lo + hi) >> 1;
+      if (seg_start[mid] <= t) {
+        ans = mid;
+        lo = mid + 1;
+      } else {
+        hi = mid - 1;
+      }
+    }
+    return ans;
+  }
+
+  __device__ int validate(int64_t a) const {
+    if (a < 0 || a >= n_adapters) {
+      record_error(err, kDevErrBadIndex);
+      return -1;
+    }
+    return static_cast<int>(a);
+  }
+
+  // seg: running segment index for monotone walks (segment mode only)
+  __device__ int operator()(int t, int& seg) const {
+    if (ids != nullptr) return validate(ids[t]);
+    while (seg + 1 < S && seg_start[seg + 1] <= t) ++seg;
+    if (seg < 0 || t < seg_start[seg] || t >= seg_start[seg + 1]) {
+      record_error(err, kDevErrBadIndex);
+      return -1;
+    }
+    return validate(seg_adapter[seg]);
+  }
+};
+
+}  // namespace
+
+__global__ void __launch_bounds__(1024) sgmv_schedule_kernel(AdapterLookup look, int32_t* tiles, int max_tiles) {
+  __shared__ int scan[1024];
+  const int tid = threadIdx.x, nth = blockDim.x;
+  const int T = look.T;
+  const int chunk = (T + nth - 1) / nth;
+  const int c0 = min(T, tid * chunk), c1 = min(T, c0 + chunk);
+
+  int seg = -1;
+  if (look.ids == nullptr && c0 < c1) seg = look.find_segment(c0 > 0 ? c0 - 1 : 0);
+  int prev = -2;
+  if (c0 > 0 && c0 < c1) {
+    int s2 = seg;
+    prev = look(c0 - 1, s2);
+    seg = s2;
+  }
+  int count = 0;
+  {
+    int s = seg, pv = prev;
+    for (int t = c0; t < c1; ++t) {
+      const int a = look(t, s);
+      if ((t % kSgmvTileTokens) == 0 || a != pv) ++count;
+      pv = a;
+    }
+  }
+  scan[tid] = count;
+  __syncthreads();
+  for (int off = 1; off < nth; off <<= 1) {
+    const int v = tid >= off ? scan[tid - off] : 0;
+    __syncthreads();
+    scan[tid] += v;
+    __syncthreads();
+  }
+  const int total = scan[nth - 1];
+  int base = scan[tid] - count;
+  int32_t* starts = tiles + 2;
+  int32_t* adapters = tiles + 3 + max_tiles;
+  {
+    int s = seg, pv = prev;
+    for (int t = c0; t < c1; ++t) {
+      const int a = look(t, s);
+      if ((t % kSgmvTileTokens) == 0 || a != pv) {
+        if (base < max_tiles) {
+          starts[base] = t;
+          adapters[base] = a;
+        }
+        ++base;
+      }
+      pv = a;
+    }
+  }
+  if (tid == 0) {
+    const int n = min(total, max_tiles);
+    if (total > max_tiles) record_error(look.err, kDevErrBadIndex);
+    tiles[0] = n;
+    tiles[1] = max_tiles;
+    starts[n] = T;
+  }
+}
+
+}  // namespace lora
+
+using namespace lora;
+
+extern "C" size_t lora_sgmv_tiles_size(int64_t T, int64_t S) {
+  return static_cast<size_t>(sgmv_tiles_bytes(std::max<int64_t>(T, 0), std::max<int64_t>(S, 0)));
+}
+
+extern "C" int lora_sgmv_schedule(const int64_t* ids, const int64_t* seg_start, const int64_t* seg_adapter, int64_t T,
+                                  int64_t S, int64_t n_adapters, int32_t* tiles, size_t tiles_bytes, void* stream) {
+  if (tiles == nullptr) return LORA_ERR_ARG;
+  if (T < 0 || S < 0 || n_adapters < 0 || T > INT32_MAX / 2) return LORA_ERR_SHAPE;
+  if (ids == nullptr && (seg_start == nullptr || seg_adapter == nullptr || (S == 0 && T > 0))) return LORA_ERR_ARG;
+  if (ids != nullptr) S = 0;
+  if (tiles_bytes < lora_sgmv_tiles_size(T, S)) return LORA_ERR_WORKSPACE;
+  const int dev = current_device();
+  if (dev < 0 || !device_info(dev).is_sm100) return LORA_ERR_DEVICE;
+  AdapterLookup look{ids, seg_start, seg_adapter, static_cast<int>(T), static_cast<int>(S),
+                     static_cast<int>(std::min<int64_t>(n_adapters, INT32_MAX)), device_info(dev).err_word};
+  const int64_t mt = sgmv_max_tiles(T, S);
+  sgmv_schedule_kernel<<<1, 1024, 0, static_cast<cudaStream_t>(stream)>>>(look, tiles, static_cast<int>(mt));
+  return cudaGetLastError() == cudaSuccess ? LORA_OK : LORA_ERR_CUDA;
+}

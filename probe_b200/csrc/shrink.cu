@@ -1,0 +1,450 @@
+// Rank shrink  z = scale * x . A^T  (the skinny, memory-bound half of LoRA).
+//
+// One kernel serves the single-adapter shrink (lora_shrink) and the
+// segmented multi-adapter shrink (lora_sgmv_shrink):
+//   - a work tile is <= 64 consecutive tokens that share one adapter;
+//   - each warp multiplies 16 tokens against the adapter's R rows with
+//     mma.sync m16n8k16 (fp32 accumulate).  Both operands are read with
+//     16-byte loads, 32 contiguous bytes per thread: the K order inside a
+//     64-wide step is permuted identically for x and A, which leaves the dot
+//     product unchanged and keeps every access a full 32-byte sector;
+//   - K is split over CTAs (blockIdx.y).  Each split writes fp32 partials to
+//     the workspace; the last CTA to finish a tile (atomic ticket) sums them
+//     in split order, so results are deterministic and no float atomics or
+//     zero-fill launches are needed.  The ticket counters reset themselves.
+// With M <= 32 the four warps of a CTA also split their K slice and reduce
+// through shared memory, so decode-sized shrinks still fill the machine.
+//
+// Reference semantics: splitk_lora.py:22-63,104-126 (fp32 partials + sum),
+// splitk_shrink.py:34-141, multilora.py:128-182 (ragged table lookup),
+// segmented_branch.py:12-28 and ragged_branch.py:6-16 (per-segment / per-token
+// adapter, rank-0 skip).
+#include <algorithm>
+
+#include "common.cuh"
+#include "runtime.h"
+#include "sgmv.h"
+
+namespace lora {
+
+struct ShrinkArgs {
+  const void* x;
+  const void* a;
+  void* z;
+  float* partial;     // [split_k][M][pr] fp32, pr = partial row width
+  int* counters;      // one per tile
+  const int64_t* offsets;  // SGMV only
+  const int64_t* ranks;    // SGMV only
+  const int32_t* tiles;    // SGMV only: schedule (sgmv.h), NULL = plain shrink
+  const int64_t* rows;     // SGMV only: logical token -> physical row (NULL = identity)
+  int* err;
+  int64_t ldx, lda, ldz;
+  int M, K, R, z_width, pr;
+  int n_adapters;
+  int split_k, kslice;  // kslice: multiple of 64
+  int wt;               // token sub-tiles per CTA (1, 2, 4); 4 / wt warps split K
+  int num_tiles_plain;
+  float scale;
+};
+
+template <bool ALIGNED, typename T>
+LORA_DEVINL uint4 load8(const T* row, int k, int k_end, bool valid) {
+  if (!valid) return make_uint4(0, 0, 0, 0);
+  if (ALIGNED) {
+    if (k < k_end) return ldg_stream(row + k);
+    return make_uint4(0, 0, 0, 0);
+  }
+  union {
+    uint4 v;
+    T e[8];
+  } u;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) u.e[i] = (k + i < k_end) ? row[k + i] : from_f32<T>(0.f);
+  return u.v;
+}
+
+template <bool ALIGNED, typename T>
+LORA_DEVINL uint4 load8_cached(const T* row, int k, int k_end, bool valid) {
+  if (!valid) return make_uint4(0, 0, 0, 0);
+  if (ALIGNED) {
+    if (k < k_end) return __ldg(reinterpret_cast<const uint4*>(row + k));
+    return make_uint4(0, 0, 0, 0);
+  }
+  return load8<false, T>(row, k, k_end, true);
+}
+
+// acc[nt][*] += x[row0 .. row0+16) . A[nt*8 .. nt*8+8)^T over the 64-wide K
+// steps k_first, k_first + k_stride, ... < k_end.
+LORA_DEVINL int64_t phys_row(const int64_t* rows, int64_t t) { return rows ? rows[t] : t; }
+
+template <bool ALIGNED, typename T, int NT>
+LORA_DEVINL void shrink_warp(const T* x, int64_t ldx, const int64_t* rows, int row0, int nrows, const T* a,
+                             int64_t lda, int R, int k_first, int k_stride, int k_end, float (&acc)[NT][4]) {
+  const int lane = threadIdx.x & 31;
+  const int g = lane >> 2, q = lane & 3;
+  const bool v0 = g < nrows, v1 = g + 8 < nrows;
+  const T* xr0 = x + phys_row(rows, row0 + (v0 ? g : 0)) * ldx;
+  const T* xr1 = x + phys_row(rows, row0 + (v1 ? g + 8 : 0)) * ldx;
+#pragma unroll 1
+  for (int k = k_first; k < k_end; k += k_stride) {
+    const int kc = k + 16 * q;
+    const uint4 x00 = load8<ALIGNED>(xr0, kc, k_end, v0);
+    const uint4 x01 = load8<ALIGNED>(xr0, kc + 8, k_end, v0);
+    const uint4 x10 = load8<ALIGNED>(xr1, kc, k_end, v1);
+    const uint4 x11 = load8<ALIGNED>(xr1, kc + 8, k_end, v1);
+    const uint32_t wg[8] = {x00.x, x00.y, x00.z, x00.w, x01.x, x01.y, x01.z, x01.w};
+    const uint32_t wh[8] = {x10.x, x10.y, x10.z, x10.w, x11.x, x11.y, x11.z, x11.w};
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) {
+      if (nt * 8 >= R) break;
+      const int n = nt * 8 + g;
+      const bool vn = n < R;
+      const T* ar = a + static_cast<int64_t>(vn ? n : 0) * lda;
+      const uint4 a0 = load8_cached<ALIGNED>(ar, kc, k_end, vn);
+      const uint4 a1 = load8_cached<ALIGNED>(ar, kc + 8, k_end, vn);
+      const uint32_t wa[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const uint32_t af[4] = {wg[2 * j], wh[2 * j], wg[2 * j + 1], wh[2 * j + 1]};
+        const uint32_t bf[2] = {wa[2 * j], wa[2 * j + 1]};
+        mma16816<T>(acc[nt], af, bf);
+      }
+    }
+  }
+}
+
+template <typename TZ>
+LORA_DEVINL void store_z(TZ* z, float v) {
+  *z = from_f32<TZ>(v);
+}
+
+template <bool ALIGNED, typename T, typename TZ, int NT>
+__global__ void __launch_bounds__(128) shrink_kernel(const ShrinkArgs p) {
+  __shared__ float red[4][16][NT * 8 + 1];
+  __shared__ int s_last;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, q = lane & 3;
+  const int wt = p.wt, wk = 4 / p.wt;
+  const int t_sub = warp % wt, k_sub = warp / wt;
+  const int tile_tokens = 16 * wt;
+  const int ks = blockIdx.y;
+  const int k_begin = ks * p.kslice;
+  const int k_end = min(p.K, k_begin + p.kslice);
+  const T* x = static_cast<const T*>(p.x);
+  TZ* z = static_cast<TZ*>(p.z);
+
+  const int num_tiles = p.tiles ? sgmv_num_tiles(p.tiles) : p.num_tiles_plain;
+  for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x) {
+    // ---- resolve the tile: token range, adapter rows, rank
+    int t0, t1, R;
+    const T* a;
+    if (p.tiles) {
+      t0 = sgmv_tile_start(p.tiles, tile);
+      t1 = sgmv_tile_start(p.tiles, tile + 1);
+      const int ad = sgmv_tile_adapter(p.tiles, tile);
+      if (ad >= 0) {
+        R = static_cast<int>(p.ranks[ad] < p.R ? p.ranks[ad] : p.R);
+        a = static_cast<const T*>(p.a) + p.offsets[ad] * p.lda;
+      } else {
+        R = 0;
+        a = static_cast<const T*>(p.a);
+      }
+    } else {
+      t0 = tile * tile_tokens;
+      t1 = min(p.M, t0 + tile_tokens);
+      R = p.R;
+      a = static_cast<const T*>(p.a);
+    }
+    const int row0 = t0 + t_sub * 16;
+    const int nrows = min(16, t1 - row0);
+
+    float acc[NT][4];
+#pragma unroll
+    for (int nt = 0; nt < NT; ++nt) acc[nt][0] = acc[nt][1] = acc[nt][2] = acc[nt][3] = 0.f;
+    if (nrows > 0 && R > 0)
+      shrink_warp<ALIGNED, T, NT>(x, p.ldx, p.rows, row0, nrows, a, p.lda, R, k_begin + 64 * k_sub, 64 * wk, k_end,
+                                  acc);
+
+    // ---- reduce the K sub-slices of this CTA's warps through shared memory
+    if (wk > 1) {
+      if (k_sub > 0) {
+#pragma unroll
+        for (int nt = 0; nt < NT; ++nt) {
+          red[warp][g][nt * 8 + 2 * q] = acc[nt][0];
+          red[warp][g][nt * 8 + 2 * q + 1] = acc[nt][1];
+          red[warp][g + 8][nt * 8 + 2 * q] = acc[nt][2];
+          red[warp][g + 8][nt * 8 + 2 * q + 1] = acc[nt][3];
+        }
+      }
+      __syncthreads();
+      if (k_sub == 0) {
+        for (int s = 1; s < wk; ++s) {
+          const int w2 = t_sub + s * wt;
+#pragma unroll
+          for (int nt = 0; nt < NT; ++nt) {
+            acc[nt][0] += red[w2][g][nt * 8 + 2 * q];
+            acc[nt][1] += red[w2][g][nt * 8 + 2 * q + 1];
+            acc[nt][2] += red[w2][g + 8][nt * 8 + 2 * q];
+            acc[nt][3] += red[w2][g + 8][nt * 8 + 2 * q + 1];
+          }
+        }
+      }
+    }
+
+    // ---- write: final z (no split) or fp32 partials
+    if (k_sub == 0 && nrows > 0) {
+#pragma unroll
+      for (int nt = 0; nt < NT; ++nt) {
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const int row = g + 8 * h;
+          if (row >= nrows) continue;
+          const int64_t t = row0 + row;
+          const int64_t pt = phys_row(p.rows, t);
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            const int col = nt * 8 + 2 * q + e;
+            if (p.split_k == 1) {
+              if (col < p.z_width) store_z<TZ>(z + pt * p.ldz + col, col < R ? p.scale * acc[nt][2 * h + e] : 0.f);
+            } else if (col < p.pr) {
+              p.partial[(static_cast<int64_t>(ks) * p.M + t) * p.pr + col] = acc[nt][2 * h + e];
+            }
+          }
+        }
+      }
+      if (p.split_k == 1) {
+        // zero-fill columns beyond the mma tiles up to z_width
+        for (int row = 0; row < nrows; ++row)
+          for (int col = NT * 8 + lane; col < p.z_width; col += 32)
+            store_z<TZ>(z + phys_row(p.rows, row0 + row) * p.ldz + col, 0.f);
+      }
+    }
+
+    if (p.split_k > 1) {
+      __threadfence();
+      __syncthreads();
+      if (threadIdx.x == 0) {
+        const int prev = atomicAdd(&p.counters[tile], 1);
+        s_last = (prev == p.split_k - 1);
+      }
+      __syncthreads();
+      if (s_last) {
+        __threadfence();
+        const int ntok = t1 - t0;
+        const int width = p.z_width;
+        for (int idx = threadIdx.x; idx < ntok * width; idx += blockDim.x) {
+          const int row = idx / width, col = idx - row * width;
+          const int64_t t = t0 + row;
+          float v = 0.f;
+          if (col < R) {
+            for (int s = 0; s < p.split_k; ++s) v += __ldcg(&p.partial[(static_cast<int64_t>(s) * p.M + t) * p.pr + col]);
+            v *= p.scale;
+          }
+          store_z<TZ>(z + phys_row(p.rows, t) * p.ldz + col, v);
+        }
+        if (threadIdx.x == 0) p.counters[tile] = 0;
+      }
+    }
+    __syncthreads();
+  }
+}
+
+// ------------------------------------------------------------------- host
+namespace {
+
+inline bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+inline int shrink_wt(int64_t M) { return M <= 16 ? 1 : (M <= 32 ? 2 : 4); }
+
+template <bool AL, typename T, typename TZ>
+int launch_shrink_nt(int nt, const ShrinkArgs& p, dim3 grid, cudaStream_t s) {
+  switch (nt) {
+    case 1: shrink_kernel<AL, T, TZ, 1><<<grid, 128, 0, s>>>(p); break;
+    case 2: shrink_kernel<AL, T, TZ, 2><<<grid, 128, 0, s>>>(p); break;
+    case 4: shrink_kernel<AL, T, TZ, 4><<<grid, 128, 0, s>>>(p); break;
+    case 8: shrink_kernel<AL, T, TZ, 8><<<grid, 128, 0, s>>>(p); break;
+    case 16: shrink_kernel<AL, T, TZ, 16><<<grid, 128, 0, s>>>(p); break;
+    default: return LORA_ERR_UNSUPPORTED;
+  }
+  return cudaGetLastError() == cudaSuccess ? LORA_OK : LORA_ERR_CUDA;
+}
+
+template <typename T, typename TZ>
+int launch_shrink_t(bool aligned, int nt, const ShrinkArgs& p, dim3 grid, cudaStream_t s) {
+  return aligned ? launch_shrink_nt<true, T, TZ>(nt, p, grid, s) : launch_shrink_nt<false, T, TZ>(nt, p, grid, s);
+}
+
+inline int pick_nt(int64_t R) {
+  if (R <= 8) return 1;
+  if (R <= 16) return 2;
+  if (R <= 32) return 4;
+  if (R <= 64) return 8;
+  return 16;
+}
+
+}  // namespace
+
+int launch_shrink(const ShrinkArgs& p, int dtype, int z_dtype, bool aligned, dim3 grid, cudaStream_t s) {
+  const int nt = pick_nt(p.R);
+  if (dtype == LORA_BF16) {
+    if (z_dtype == LORA_F32) return launch_shrink_t<__nv_bfloat16, float>(aligned, nt, p, grid, s);
+    if (z_dtype == LORA_BF16) return launch_shrink_t<__nv_bfloat16, __nv_bfloat16>(aligned, nt, p, grid, s);
+  } else if (dtype == LORA_F16) {
+    if (z_dtype == LORA_F32) return launch_shrink_t<__half, float>(aligned, nt, p, grid, s);
+    if (z_dtype == LORA_F16) return launch_shrink_t<__half, __half>(aligned, nt, p, grid, s);
+  }
+  return LORA_ERR_DTYPE;
+}
+
+// K slice per split: a multiple of 64.
+int shrink_kslice(int64_t K, int split_k) {
+  const int64_t steps = (K + 63) / 64;
+  const int64_t per = (steps + split_k - 1) / split_k;
+  return static_cast<int>(std::max<int64_t>(per, 1) * 64);
+}
+
+int shrink_pick_split_k_impl(int64_t tiles, int64_t K, int num_sms) {
+  const int64_t steps = (K + 63) / 64;
+  int64_t sk = (2 * static_cast<int64_t>(num_sms) + tiles - 1) / std::max<int64_t>(tiles, 1);
+  sk = std::min<int64_t>(sk, std::max<int64_t>(steps / 4, 1));  // >= 256 of K per split
+  sk = std::max<int64_t>(std::min<int64_t>(sk, 64), 1);
+  // Fold the split so no slice is empty.
+  const int kslice = shrink_kslice(K, static_cast<int>(sk));
+  sk = (K + kslice - 1) / kslice;
+  return static_cast<int>(std::max<int64_t>(sk, 1));
+}
+
+}  // namespace lora
+
+using namespace lora;
+
+extern "C" size_t lora_shrink_workspace_size(int64_t M, int64_t R, int split_k) {
+  if (M <= 0 || R <= 0 || split_k <= 1) return 256;
+  const size_t partial = static_cast<size_t>(split_k) * M * R * sizeof(float);
+  const size_t counters = static_cast<size_t>((M + 15) / 16) * sizeof(int);
+  return ((partial + 255) / 256) * 256 + ((counters + 255) / 256) * 256;
+}
+
+extern "C" int lora_shrink_pick_split_k(int64_t M, int64_t K, int64_t R) {
+  (void)R;
+  const int dev = current_device();
+  const int sms = dev >= 0 ? device_info(dev).num_sms : 148;
+  const int64_t tt = 16 * shrink_wt(M);
+  return shrink_pick_split_k_impl((M + tt - 1) / tt, K, sms > 0 ? sms : 148);
+}
+
+extern "C" int lora_shrink(const void* x, int64_t ldx, const void* a, int64_t lda, void* z, int64_t ldz, int z_dtype,
+                           int64_t z_width, int64_t M, int64_t K, int64_t R, float scale, int dtype, int split_k,
+                           void* workspace, size_t workspace_bytes, void* stream) {
+  if (x == nullptr || a == nullptr || z == nullptr) return LORA_ERR_ARG;
+  if (dtype != LORA_BF16 && dtype != LORA_F16) return LORA_ERR_DTYPE;
+  if (z_dtype != LORA_F32 && z_dtype != dtype) return LORA_ERR_DTYPE;
+  if (M < 0 || K < 0 || R < 0 || R > 128 || z_width < R) return LORA_ERR_SHAPE;
+  if (M > INT32_MAX || K > INT32_MAX || ldz < z_width || ldx < K || lda < K) return LORA_ERR_SHAPE;
+  if (M == 0 || z_width == 0) return LORA_OK;
+  const int dev = current_device();
+  if (dev < 0 || !device_info(dev).is_sm100) return LORA_ERR_DEVICE;
+  const DeviceInfo& info = device_info(dev);
+  const int wt = shrink_wt(M);
+  const int64_t tiles = (M + 16 * wt - 1) / (16 * wt);
+  if (R == 0 || K == 0) split_k = 1;
+  if (split_k <= 0) split_k = shrink_pick_split_k_impl(tiles, K, info.num_sms);
+  const int kslice = shrink_kslice(K, split_k);
+  split_k = static_cast<int>(std::max<int64_t>((K + kslice - 1) / kslice, 1));
+
+  ShrinkArgs p{};
+  p.x = x;
+  p.a = a;
+  p.z = z;
+  p.err = info.err_word;
+  p.ldx = ldx;
+  p.lda = lda;
+  p.ldz = ldz;
+  p.M = static_cast<int>(M);
+  p.K = static_cast<int>(K);
+  p.R = static_cast<int>(R);
+  p.z_width = static_cast<int>(z_width);
+  p.pr = static_cast<int>(R);
+  p.split_k = split_k;
+  p.kslice = kslice;
+  p.wt = wt;
+  p.num_tiles_plain = static_cast<int>(tiles);
+  p.scale = scale;
+  if (split_k > 1) {
+    const size_t need = lora_shrink_workspace_size(M, R, split_k);
+    if (workspace == nullptr || workspace_bytes < need || !al16(workspace)) return LORA_ERR_WORKSPACE;
+    const size_t partial = static_cast<size_t>(split_k) * M * R * sizeof(float);
+    p.partial = static_cast<float*>(workspace);
+    p.counters = reinterpret_cast<int*>(static_cast<char*>(workspace) + ((partial + 255) / 256) * 256);
+  }
+  const bool aligned = (K % 8 == 0) && (ldx % 8 == 0) && (lda % 8 == 0) && al16(x) && al16(a);
+  const int64_t gx = std::min<int64_t>(tiles, std::max<int64_t>(1, (4 * static_cast<int64_t>(info.num_sms) + split_k - 1) / split_k));
+  dim3 grid(static_cast<unsigned>(gx), static_cast<unsigned>(split_k));
+  return launch_shrink(p, dtype, z_dtype, aligned, grid, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" size_t lora_sgmv_shrink_workspace_size(int64_t T, int64_t S, int64_t z_width, int split_k) {
+  if (T <= 0 || z_width <= 0 || split_k <= 1) return 256;
+  const size_t partial = static_cast<size_t>(split_k) * T * z_width * sizeof(float);
+  const size_t counters = static_cast<size_t>(sgmv_max_tiles(T, S)) * sizeof(int);
+  return ((partial + 255) / 256) * 256 + ((counters + 255) / 256) * 256;
+}
+
+extern "C" int lora_sgmv_shrink(const void* x, int64_t ldx, const void* a_flat, int64_t lda, const int64_t* offsets,
+                                const int64_t* ranks, int64_t n_adapters, const int32_t* tiles, const int64_t* rows,
+                                void* z, int64_t ldz,
+                                int z_dtype, int64_t z_width, int64_t T, int64_t S, int64_t K, int64_t r_max,
+                                float scale, int dtype, int split_k, void* workspace, size_t workspace_bytes,
+                                void* stream) {
+  if (x == nullptr || a_flat == nullptr || offsets == nullptr || ranks == nullptr || tiles == nullptr || z == nullptr)
+    return LORA_ERR_ARG;
+  if (dtype != LORA_BF16 && dtype != LORA_F16) return LORA_ERR_DTYPE;
+  if (z_dtype != LORA_F32 && z_dtype != dtype) return LORA_ERR_DTYPE;
+  if (T < 0 || K < 0 || r_max < 0 || r_max > 128 || z_width < r_max || n_adapters < 0) return LORA_ERR_SHAPE;
+  if (T > INT32_MAX / 2 || K > INT32_MAX || ldz < z_width || ldx < K || lda < K) return LORA_ERR_SHAPE;
+  if (T == 0 || z_width == 0) return LORA_OK;
+  const int dev = current_device();
+  if (dev < 0 || !device_info(dev).is_sm100) return LORA_ERR_DEVICE;
+  const DeviceInfo& info = device_info(dev);
+  const int64_t blocks = (T + kSgmvTileTokens - 1) / kSgmvTileTokens;
+  if (r_max == 0 || K == 0) split_k = 1;
+  if (split_k <= 0) split_k = shrink_pick_split_k_impl(blocks, K, info.num_sms);
+  const int kslice = shrink_kslice(K, split_k);
+  split_k = static_cast<int>(std::max<int64_t>((K + kslice - 1) / kslice, 1));
+
+  ShrinkArgs p{};
+  p.x = x;
+  p.a = a_flat;
+  p.z = z;
+  p.offsets = offsets;
+  p.ranks = ranks;
+  p.tiles = tiles;
+  p.rows = rows;
+  p.err = info.err_word;
+  p.ldx = ldx;
+  p.lda = lda;
+  p.ldz = ldz;
+  p.M = static_cast<int>(T);
+  p.K = static_cast<int>(K);
+  p.R = static_cast<int>(r_max);
+  p.z_width = static_cast<int>(z_width);
+  p.pr = static_cast<int>(z_width);
+  p.n_adapters = static_cast<int>(std::min<int64_t>(n_adapters, INT32_MAX));
+  p.split_k = split_k;
+  p.kslice = kslice;
+  p.wt = 4;
+  p.scale = scale;
+  if (split_k > 1) {
+    const size_t need = lora_sgmv_shrink_workspace_size(T, S, z_width, split_k);
+    if (workspace == nullptr || workspace_bytes < need || !al16(workspace)) return LORA_ERR_WORKSPACE;
+    const size_t partial = static_cast<size_t>(split_k) * T * z_width * sizeof(float);
+    p.partial = static_cast<float*>(workspace);
+    p.counters = reinterpret_cast<int*>(static_cast<char*>(workspace) + ((partial + 255) / 256) * 256);
+  }
+  const bool aligned = (K % 8 == 0) && (ldx % 8 == 0) && (lda % 8 == 0) && al16(x) && al16(a_flat);
+  const int64_t max_tiles = sgmv_max_tiles(T, S);
+  const int64_t gx = std::min<int64_t>(
+      max_tiles, std::max<int64_t>(1, (4 * static_cast<int64_t>(info.num_sms) + split_k - 1) / split_k));
+  dim3 grid(static_cast<unsigned>(gx), static_cast<unsigned>(split_k));
+  return launch_shrink(p, dtype, z_dtype, aligned, grid, static_cast<cudaStream_t>(stream));
+}

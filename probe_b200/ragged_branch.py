@@ -1,0 +1,27 @@
+"""Compact multi-LoRA branch with per-token adapter ids and rank-0 skip.
+
+Drop-in for ``loraforge_kernels.ragged_branch`` (ragged_branch.py:30-40):
+``A [sum ranks, K]``, ``B [sum ranks, N]`` with the adapter scale folded into B,
+int64 device ``offsets`` / ``ranks`` / ``indices``.  Consecutive tokens with the
+same id are grouped into tiles on the device, so a run of one request's tokens
+reads its adapter once per 64 tokens.
+"""
+
+from __future__ import annotations
+
+import torch
+
+from . import kernels
+
+
+def branch(x, y, a, b, offsets, ranks, indices, rmax, skip_zero=True, split_k=8):
+    """out = y + (x[t] @ A_{i(t)}.T) @ B_{i(t)} for every token t."""
+    if rmax == 0:
+        return y
+    x = x.contiguous()
+    y = y.contiguous()
+    t, k = x.shape
+    n = y.shape[1]
+    tiles, s = kernels.sgmv_schedule(t, offsets.numel(), ids=indices)
+    z = kernels.sgmv_shrink(x, a, offsets, ranks, tiles, s, rmax, z_dtype=torch.float32, split_k=split_k)
+    return kernels.sgmv_expand(y, z, b, n, 1, offsets, ranks, tiles, s, n, rmax)

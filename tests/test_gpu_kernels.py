@@ -1,0 +1,139 @@
+"""Parity of each CUDA entry point against the CPU oracle (GPU only).
+
+Every call goes through the C ABI (probe_b200.kernels -> liblora_b200.so).
+"""
+
+import math
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import lora_oracle as orc
+from probe_b200 import _lib, kernels
+from probe_b200.kernels import pad_cols, round_up
+from tests.helpers import assert_parity, np64, randn
+
+pytestmark = pytest.mark.gpu
+
+DTYPES = [torch.bfloat16, torch.float16]
+
+
+@pytest.mark.parametrize("dtype", DTYPES)
+@pytest.mark.parametrize("m,n,k", [(128, 256, 64), (256, 512, 1024), (300, 320, 320), (1000, 1536, 768),
+                                   (129, 200, 136), (64, 4096, 512)])
+@pytest.mark.parametrize("r", [0, 7, 16, 130])
+def test_gemm_kconcat(dtype, m, n, k, r):
+    x = randn((m, k), 1.0, dtype, seed=1)
+    w = randn((n, k), 1 / math.sqrt(k), dtype, seed=2)
+    bias = randn((n,), 1.0, dtype, seed=3)
+    if r:
+        a = randn((r, k), 1 / math.sqrt(k), dtype, seed=4)
+        b = randn((n, r), 1 / math.sqrt(r), dtype, seed=5)
+        width = round_up(r, 64)
+        # z = scale * x a^T rounded to dtype, zero tail (what the shrink produces)
+        z64 = orc.shrink(np64(x), np64(a), 0.75)
+        z = torch.zeros((m, width), dtype=dtype, device="cuda")
+        z[:, :r] = torch.from_numpy(z64).to(dtype).cuda()
+        out = kernels.gemm(x, w, z, pad_cols(b, width), rank=r, bias=bias)
+        want = np64(x) @ np64(w).T + np64(z)[:, :r] @ np64(b).T + np64(bias)
+    else:
+        out = kernels.gemm(x, w, bias=bias)
+        want = orc.naive_linear(np64(x), np64(w), np64(bias), None, None, 0.0)
+    torch.cuda.synchronize()
+    assert_parity(out, want, dtype)
+
+
+@pytest.mark.parametrize("m,n,k", [(256, 256, 256), (384, 640, 1280)])
+def test_gemm_alpha_no_bias(m, n, k):
+    x = randn((m, k), 1.0, seed=11)
+    w = randn((n, k), 1 / math.sqrt(k), seed=12)
+    out = kernels.gemm(x, w, alpha=0.5)
+    assert_parity(out, 0.5 * (np64(x) @ np64(w).T))
+
+
+def test_gemm_rejects_unaligned_k():
+    x = randn((128, 100), 1.0)
+    w = randn((64, 100), 0.1)
+    with pytest.raises(ValueError):
+        kernels.gemm(x, w)
+
+
+@pytest.mark.parametrize("dtype", DTYPES)
+@pytest.mark.parametrize("m", [1, 4, 16, 33, 64, 200, 1000])
+@pytest.mark.parametrize("k,r", [(4096, 16), (257, 7), (1536, 64), (640, 1), (768, 40), (512, 128)])
+@pytest.mark.parametrize("split_k", [0, 1, 3])
+def test_shrink(dtype, m, k, r, split_k):
+    x = randn((m, k), 1.0, dtype, seed=m + r)
+    a = randn((r, k), 1 / math.sqrt(k), dtype, seed=k)
+    width = round_up(r, 64)
+    z = kernels.shrink(x, a, 1.5, z_dtype=torch.float32, z_width=width, split_k=split_k)
+    want = np.zeros((m, width))
+    want[:, :r] = orc.shrink(np64(x), np64(a), 1.5)
+    g = np64(z)
+    assert np.array_equal(g[:, r:], np.zeros_like(g[:, r:]))
+    _, fro = orc.parity(g, want)
+    assert fro < 2e-6, fro
+    zq = kernels.shrink(x, a, 1.5, z_dtype=dtype, split_k=split_k)
+    assert_parity(zq, want[:, :r], dtype)
+
+
+def test_shrink_deterministic():
+    x = randn((64, 4096), 1.0, seed=5)
+    a = randn((16, 4096), 1 / 64, seed=6)
+    z1 = kernels.shrink(x, a, 1.0, split_k=16)
+    z2 = kernels.shrink(x, a, 1.0, split_k=16)
+    assert torch.equal(z1, z2)
+
+
+@pytest.mark.parametrize("dtype", DTYPES)
+@pytest.mark.parametrize("m,n,r", [(1, 11008, 16), (4, 512, 13), (64, 1280, 24), (200, 4096, 64),
+                                   (37, 259, 3), (128, 1000, 128), (16, 384, 224)])
+@pytest.mark.parametrize("layout", ["peft", "rank_major"])
+def test_expand_add(dtype, m, n, r, layout):
+    y = randn((m, n), 1.0, dtype, seed=7)
+    z = randn((m, r), 1.0, torch.float32, seed=8)
+    b = randn((n, r), 1 / math.sqrt(r), dtype, seed=9)
+    bias = randn((n,), 1.0, dtype, seed=10)
+    bb = b if layout == "peft" else b.t().contiguous()
+    y0 = y.clone()
+    out = kernels.expand_add(y, z, bb, 0.5, bias=bias, b_layout=layout)
+    assert torch.equal(y, y0)
+    zq = orc.round_dtype(np64(z).astype(np.float32), "bf16" if dtype == torch.bfloat16 else "f16")
+    want = orc.expand_add(np64(y), zq, np64(b), 0.5, np64(bias))
+    assert_parity(out, want, dtype)
+    out2 = kernels.expand_add(None, z, bb, 0.5, b_layout=layout, dtype=dtype)
+    assert_parity(out2, orc.expand_add(None, zq, np64(b), 0.5), dtype)
+
+
+@pytest.mark.parametrize("dtype", DTYPES)
+@pytest.mark.parametrize("m,k,n", [(1, 257, 131), (4, 1536, 512), (8, 769, 259), (16, 4096, 11008),
+                                   (64, 4096, 1024), (33, 512, 300)])
+@pytest.mark.parametrize("r", [0, 1, 13, 16, 64])
+def test_decode_linear(dtype, m, k, n, r):
+    x = randn((m, k), 1.0, dtype, seed=m)
+    w = randn((n, k), 1 / math.sqrt(k), dtype, seed=n)
+    bias = randn((n,), 1.0, dtype, seed=3)
+    a = randn((r, k), 1 / math.sqrt(k), dtype, seed=4) if r else None
+    b = randn((n, r), 1 / math.sqrt(max(r, 1)), dtype, seed=5) if r else None
+    z = kernels.shrink(x, a, 1.0, z_dtype=dtype) if r else None
+    out = kernels.decode_linear(x, w, z, b, bias, -0.7)
+    tag = "bf16" if dtype == torch.bfloat16 else "f16"
+    want = orc.decode_linear(np64(x), np64(w), np64(bias), np64(a) if r else None, np64(b) if r else None, -0.7,
+                             tag)
+    assert_parity(out, want, dtype)
+
+
+def test_decode_zero_rank_is_base():
+    x = randn((4, 1536), 1.0, seed=1)
+    w = randn((512, 1536), 1 / 40, seed=2)
+    base = kernels.decode_linear(x, w, None, None, None, 0.0)
+    a = randn((8, 1536), 1 / 40, seed=3)
+    b = torch.zeros((512, 8), dtype=torch.bfloat16, device="cuda")
+    z = kernels.shrink(x, a, 1.0, z_dtype=torch.bfloat16)
+    with_zero_b = kernels.decode_linear(x, w, z, b, None, 1.0)
+    assert torch.equal(base, with_zero_b)
+
+
+def test_device_error_word_clear():
+    assert _lib.device_error() == 0
