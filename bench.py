@@ -176,24 +176,19 @@ def run_gpu(args):
     runners = [_KConcat(p.w, p.bias, p.a, p.b, p.scale) for p in projs]
     outs = [torch.empty((p.m, p.n), device=dev, dtype=torch.bfloat16) for p in projs]
     flops = sum(p.flops() for p in projs)
-    gemm_flops = sum(2.0 * p.m * p.k * p.n + 2.0 * p.m * p.r * p.n for p in projs)
+    gemm_flops = sum(2.0 * p.m * p.k * p.n + 2.0 * p.m * p.r * p.n for p in projs)  # algorithmic (rank r, not 2 r16)
     launches_per_step = 2 * len(projs)  # shrink GEMM + fused GEMM per projection
 
     from probe_b200 import kernels
 
-    def shrink(run, x):
-        # r = 224 > 128: the shrink is itself a tcgen05 GEMM (N = 256, zero tail)
-        if run.a_pad is None:
-            return kernels.shrink(x, run.a, run.scale, z_dtype=x.dtype, z_width=run.width)
-        return kernels.gemm(x, run.a_pad, alpha=run.scale)
-
     def step(events=None):
         for i, (p, run) in enumerate(zip(projs, runners)):
-            z = shrink(run, p.x)
+            # r = 224 > 128: the shrink is itself a tcgen05 GEMM writing [hi | lo] of s.z
+            z = run.shrink(p.x)
             if events is not None:
                 events[i][0].record()
             # the fused GEMM: x.W^T with the LoRA expand as an extra K-slice
-            kernels.gemm(p.x, run.weight, z, run.b_pad, rank=run.r, bias=run.bias, out=outs[i])
+            kernels.gemm(p.x, run.weight, z, run.b_dup, rank=run.tail, bias=run.bias, out=outs[i])
             if events is not None:
                 events[i][1].record()
 

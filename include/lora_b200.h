@@ -77,29 +77,38 @@ LORA_API int lora_b200_device_error(int device, int* code);
  *   out[M,N] = alpha * ( x[M,K] . w[N,K]^T  +  z[M,R] . bw[N,R]^T ) + bias[N]
  *
  * The second product is the LoRA expand folded in as an extra K-slice
- * ("K-concat"): z = s * x . A^T comes from lora_shrink, bw is lora_B.weight
- * zero-padded to width ldbw.  R = 0 (z, bw NULL) gives a plain linear.
+ * ("K-concat"): z = s * x . A^T comes from lora_shrink, bw holds lora_B.weight
+ * columns.  For accuracy the caller usually passes z as a hi/lo pair
+ * [round(s.z) | s.z - round(s.z)] against bw = [B | B] (R = 2 * rank).
+ * R = 0 (z, bw NULL) gives a plain linear.
+ * lo_offset > 0 writes the result itself as a hi/lo pair: out[:, c] =
+ * round(v) and out[:, c + lo_offset] = round(v - round(v)) (lo_offset >= N,
+ * ldo >= N + lo_offset) -- the large-rank shrink producing such a z.
  * Requirements: 16-byte aligned pointers; ldx, ldw multiples of 8 and >= K;
- * K a multiple of 8; when R > 0, ldz and ldbw >= roundup(R, 64), multiples of
- * 8, and columns [R, roundup(R,64)) of z and bw are zero.  bias may be NULL.
+ * K a multiple of 8; when R > 0, ldz, ldbw >= R and multiples of 8 (columns
+ * beyond R are never read).  bias may be NULL.
  * Replaces: _fused_lora_gemm_kernel / fused_gemm (fused_linear.py:229-317),
  * _kconcat (fused_linear.py:676-677), the cuBLAS GEMM of _concat / _hybrid
  * (fused_linear.py:362-373) and cutlass_gemm (csrc/cutlass_gemm_gate.cu:91-106).
  * ------------------------------------------------------------------------- */
 LORA_API int lora_gemm(const void* x, int64_t ldx, const void* w, int64_t ldw, const void* z, int64_t ldz,
               const void* bw, int64_t ldbw, const void* bias, void* out, int64_t ldo, int64_t M,
-              int64_t N, int64_t K, int64_t R, float alpha, int dtype, void* stream);
+              int64_t N, int64_t K, int64_t R, float alpha, int64_t lo_offset, int dtype, void* stream);
 
 /* ---------------------------------------------------------------------------
  * Split-K rank shrink  z[M, z_width] = scale * x[M,K] . a[R,K]^T
  * Columns [R, z_width) of z are written with zeros.  z_dtype may be LORA_F32
- * or the input dtype.  split_k slices of K run in separate CTAs; their fp32
- * partials are summed in a fixed order by the last CTA to finish (no float
- * atomics: the result is deterministic).  split_k == 0 picks a value.
- * Workspace: lora_shrink_workspace_size() bytes, zero-filled before its first
- * use; the kernel leaves its counters at zero again on return, so the same
- * workspace can be reused (and captured in a CUDA graph) without re-zeroing.
- * Calls that share one workspace must not overlap on the GPU.
+ * or the input dtype.  z_split = 1 (input dtype only) also writes the
+ * rounding residual: z[:, z_width + j] = round(v - round(v)), so [hi | lo]
+ * carries ~16 mantissa bits into a K-concat expand (ldz >= 2 * z_width).
+ * split_k slices of K run in separate CTAs; their fp32 partials are summed in
+ * a fixed order by the last CTA to finish (no float atomics: the result is
+ * deterministic).  split_k == 0 picks a value.
+ * Workspace: lora_shrink_workspace_size() bytes.  It starts with a fixed
+ * 256 KiB region of ticket counters that must be zero before the first use;
+ * every call leaves them at zero again, so one workspace serves calls of any
+ * shape (and CUDA-graph replays) without re-zeroing.  Calls that share one
+ * workspace must not overlap on the GPU.
  * Replaces: _splitk_shrink_kernel + torch sum / splitk_lora_shrink
  * (splitk_lora.py:22-63,104-126), _splitk_shrink_partial / _splitk_shrink_atomic
  * (splitk_shrink.py:34-141), the x.A^T half of the fused_lora / tiled_lora /
@@ -109,13 +118,15 @@ LORA_API int lora_gemm(const void* x, int64_t ldx, const void* w, int64_t ldw, c
 LORA_API size_t lora_shrink_workspace_size(int64_t M, int64_t R, int split_k);
 LORA_API int lora_shrink_pick_split_k(int64_t M, int64_t K, int64_t R);
 LORA_API int lora_shrink(const void* x, int64_t ldx, const void* a, int64_t lda, void* z, int64_t ldz,
-                int z_dtype, int64_t z_width, int64_t M, int64_t K, int64_t R, float scale,
-                int dtype, int split_k, void* workspace, size_t workspace_bytes, void* stream);
+                int z_dtype, int64_t z_width, int z_split, int64_t M, int64_t K, int64_t R,
+                float scale, int dtype, int split_k, void* workspace, size_t workspace_bytes,
+                void* stream);
 
 /* ---------------------------------------------------------------------------
  * Expand + add   out[M,N] = y[M,N] + scale * z[M,R] . B^T + bias[N]
  * y may be NULL (treated as zero) and may not alias out.  z is f32 or the
- * input dtype (rounded to the input dtype before the tensor-core product).
+ * input dtype; an f32 z is carried into the tensor-core product as a
+ * hi/lo pair of the input dtype (R <= 128), keeping ~16 mantissa bits.
  * b_layout selects LORA_B_PEFT ([N,R]) or LORA_B_RANK_MAJOR ([R,N]).
  * Replaces: _expand_add_kernel / expand_add (fused_linear.py:112-200),
  * _persistent_expand_add_kernel (splitk_lora.py:66-153) and the expand half of
@@ -131,8 +142,9 @@ LORA_API int lora_expand_add(const void* y, int64_t ldy, const void* z, int64_t 
  * Decode linear (small M): out[M,N] = x . w^T + scale * z . b^T + bias
  * Streams w once with split-K over CTAs; z ([M,R], input dtype or f32) comes
  * from lora_shrink and may be NULL when R == 0.  b is lora_B.weight [N,R].
- * M <= 64.  Workspace: lora_decode_workspace_size() bytes, zero-filled before
- * first use (self-resetting counters, as for lora_shrink).
+ * scale * z is carried as a hi/lo pair of the input dtype.  M <= 64.
+ * Workspace: lora_decode_workspace_size() bytes, with the same zeroed
+ * counter region as lora_shrink's.
  * Replaces: _decode_linear_kernel / build_decode_linear / decode_lora_linear
  * (decode_linear.py:13-100).
  * ------------------------------------------------------------------------- */
@@ -170,7 +182,7 @@ LORA_API int lora_sgmv_schedule(const int64_t* ids, const int64_t* seg_start, co
 
 /* z[t, :] = scale * x[t] . A_{a(t)}^T for every token, zero beyond the
  * token's rank up to z_width.  Workspace: lora_sgmv_shrink_workspace_size()
- * bytes, zero-filled before first use (self-resetting counters).
+ * bytes, with the same zeroed counter region as lora_shrink's.
  * rows (optional, int64 [T]): logical token t of the schedule reads x row
  * rows[t] and writes z row rows[t] (a gather / scatter by index, e.g. the
  * adapter-sorted order of lora_sgmv_sort or a rank bucket's positions);

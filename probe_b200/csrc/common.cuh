@@ -23,6 +23,13 @@ namespace lora {
 // legitimate wait in these kernels lasts longer than a few microseconds.
 constexpr uint64_t kWaitLimitNs = 2000000000ull;  // 2 s
 
+// Split-K workspaces start with a fixed region of ticket counters (one int
+// per tile) that no call's partial sums ever overlap.  The region is zeroed
+// once when the workspace is created; every kernel returns the counters it
+// used to zero, so any later call -- of any shape -- finds them zero.
+constexpr size_t kCounterBytes = 256 * 1024;
+constexpr int64_t kMaxCounters = kCounterBytes / sizeof(int);
+
 // Device-side error codes (written with atomicCAS so the first one sticks).
 constexpr int kDevErrTimeoutFull = 101;
 constexpr int kDevErrTimeoutEmpty = 102;

@@ -10,15 +10,18 @@
 //     K-steps of 64 in flight, and multiplies them against the token slice
 //     staged in shared memory with mma.sync m16n8k16 in swap-AB form (W rows
 //     are the 16-row operand, tokens the 8-column operand);
-//   - the LoRA expand is one more K-slice on the last split: [x | z] against
+//   - the LoRA expand is one more K-slice on the last split: [x | s.z] against
 //     [W | B], so the output is written once (the decode analogue of the
-//     reference's K-concat, fused_linear.py:622-677);
+//     reference's K-concat, fused_linear.py:622-677).  s.z is staged as a
+//     bf16/f16 hi/lo pair against B twice, so the expand keeps ~16 mantissa
+//     bits of z (the reference rounds z to the input dtype first,
+//     decode_linear.py:42-44; pass z already rounded to reproduce that);
 //   - splits write fp32 partials; the last CTA of a row block (atomic
-//     ticket) sums them in split order and adds the bias.
-// z comes from lora_shrink (already rounded to the input dtype, as
-// decode_linear.py:42-44 rounds it).  When z is produced by the kernel right
-// before this one, programmatic dependent launch lets W streaming start
-// before z is ready: z is only read after griddepcontrol.wait.
+//     ticket) sums them in split order and adds the bias, then returns the
+//     ticket to zero (fixed counter region at the start of the workspace).
+// When z is produced by the kernel right before this one, programmatic
+// dependent launch lets W streaming start before z is ready: z is only read
+// after griddepcontrol.wait.
 // Reference: _decode_linear_kernel / decode_lora_linear (decode_linear.py:13-100).
 #include <algorithm>
 
@@ -56,7 +59,7 @@ __global__ void __launch_bounds__(128) decode_kernel(const DecodeArgs p) {
   const bool last_split = (ks == p.split_k - 1);
   const bool has_tail = last_split && p.R > 0;
   const int kmain = ((k1 - k0) + 63) & ~63;               // main columns in xs (64-padded)
-  const int kcols = kmain + (has_tail ? ((p.r16 + 63) & ~63) : 0);
+  const int kcols = kmain + (has_tail ? ((2 * p.r16 + 63) & ~63) : 0);
   const int xstride = kcols + 8;
   const int n_row0 = blockIdx.x * 64 + warp * 16;
   const T* x = static_cast<const T*>(p.x);
@@ -165,19 +168,27 @@ __global__ void __launch_bounds__(128) decode_kernel(const DecodeArgs p) {
     mma_step(wg, wh, kl);
   }
 
-  // ---- LoRA tail on the last split: [z] against [B] (B is [N, R], PEFT layout)
+  // ---- LoRA tail on the last split: [hi(s.z) | lo(s.z)] against [B | B]
   if (has_tail) {
     pdl_wait();  // z may come from the kernel launched just before this one
-    const int tcols = (p.r16 + 63) & ~63;
+    const int r16 = p.r16;
+    const int tcols = (2 * r16 + 63) & ~63;
     __syncthreads();
-    for (int idx = threadIdx.x; idx < TG * 8 * tcols; idx += blockDim.x) {
-      const int m = idx / tcols, j = idx - m * tcols;
+    for (int idx = threadIdx.x; idx < TG * 8 * r16; idx += blockDim.x) {
+      const int m = idx / r16, j = idx - m * r16;
       float v = 0.f;
       if (m < p.M && j < p.R) {
         if (p.ldz < 0) v = static_cast<const float*>(p.z)[static_cast<int64_t>(m) * (-p.ldz) + j];
         else v = to_f32(static_cast<const T*>(p.z)[static_cast<int64_t>(m) * p.ldz + j]);
       }
-      xs[m * xstride + kmain + j] = from_f32<T>(v * p.scale);
+      v *= p.scale;
+      const T hi = from_f32<T>(v);
+      xs[m * xstride + kmain + j] = hi;
+      xs[m * xstride + kmain + r16 + j] = from_f32<T>(v - to_f32(hi));
+    }
+    for (int idx = threadIdx.x; idx < TG * 8 * (tcols - 2 * r16); idx += blockDim.x) {
+      const int m = idx / (tcols - 2 * r16), j = idx - m * (tcols - 2 * r16);
+      xs[m * xstride + kmain + 2 * r16 + j] = from_f32<T>(0.f);
     }
     __syncthreads();
     const T* bsrc = static_cast<const T*>(p.b);
@@ -187,9 +198,11 @@ __global__ void __launch_bounds__(128) decode_kernel(const DecodeArgs p) {
       union { uint4 u4[2]; T e[16]; } ua, ub;
 #pragma unroll
       for (int i = 0; i < 16; ++i) {
-        const int j = kc + i;
-        ua.e[i] = (va && j < p.R) ? bsrc[static_cast<int64_t>(ra) * p.ldb + j] : from_f32<T>(0.f);
-        ub.e[i] = (vb && j < p.R) ? bsrc[static_cast<int64_t>(rb) * p.ldb + j] : from_f32<T>(0.f);
+        const int c = kc + i;
+        const int j = c < r16 ? c : c - r16;  // both halves multiply the same B columns
+        const bool vj = c < 2 * r16 && j < p.R;
+        ua.e[i] = (va && vj) ? bsrc[static_cast<int64_t>(ra) * p.ldb + j] : from_f32<T>(0.f);
+        ub.e[i] = (vb && vj) ? bsrc[static_cast<int64_t>(rb) * p.ldb + j] : from_f32<T>(0.f);
       }
       wg[0] = ua.u4[0].x; wg[1] = ua.u4[0].y; wg[2] = ua.u4[0].z; wg[3] = ua.u4[0].w;
       wg[4] = ua.u4[1].x; wg[5] = ua.u4[1].y; wg[6] = ua.u4[1].z; wg[7] = ua.u4[1].w;
@@ -302,11 +315,14 @@ int decode_pick_split_k_impl(int64_t M, int64_t N, int64_t K, int num_sms) {
 
 using namespace lora;
 
+namespace {
+inline size_t round256(size_t v) { return (v + 255) / 256 * 256; }
+}  // namespace
+
 extern "C" size_t lora_decode_workspace_size(int64_t M, int64_t N, int split_k) {
   if (M <= 0 || N <= 0 || split_k <= 1) return 256;
   const size_t partial = static_cast<size_t>(split_k) * M * N * sizeof(float);
-  const size_t counters = static_cast<size_t>((N + 63) / 64) * sizeof(int);
-  return ((partial + 255) / 256) * 256 + ((counters + 255) / 256) * 256;
+  return kCounterBytes + round256(partial);
 }
 
 extern "C" int lora_decode_pick_split_k(int64_t M, int64_t N, int64_t K) {
@@ -360,20 +376,20 @@ extern "C" int lora_decode_linear(const void* x, int64_t ldx, const void* w, int
   p.split_k = split_k;
   p.kslice = kslice;
   p.scale = scale;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (split_k > 1) {
     const size_t need = lora_decode_workspace_size(M, N, split_k);
     if (workspace == nullptr || workspace_bytes < need || !al16(workspace)) return LORA_ERR_WORKSPACE;
-    const size_t partial = static_cast<size_t>(split_k) * M * N * sizeof(float);
-    p.partial = static_cast<float*>(workspace);
-    p.counters = reinterpret_cast<int*>(static_cast<char*>(workspace) + ((partial + 255) / 256) * 256);
+    if ((N + 63) / 64 > kMaxCounters) return LORA_ERR_SHAPE;
+    p.counters = static_cast<int*>(workspace);
+    p.partial = reinterpret_cast<float*>(static_cast<char*>(workspace) + kCounterBytes);
   }
-  const int64_t tail_cols = R > 0 ? (p.r16 + 63) / 64 * 64 : 0;
+  const int64_t tail_cols = R > 0 ? (2 * p.r16 + 63) / 64 * 64 : 0;
   const size_t smem = static_cast<size_t>(tg * 8) * (kslice + tail_cols + 8) * 2;
   const bool aligned = (K % 8 == 0) && (ldx % 8 == 0) && (ldw % 8 == 0) && al16(x) && al16(w);
   const int64_t blocks = (N + 63) / 64;
   if (split_k > 65535) return LORA_ERR_SHAPE;
   dim3 grid(static_cast<unsigned>(blocks), static_cast<unsigned>(split_k));
-  cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (dtype == LORA_BF16)
     return aligned ? launch_decode_al<true, __nv_bfloat16>(tg, p, grid, smem, s)
                    : launch_decode_al<false, __nv_bfloat16>(tg, p, grid, smem, s);

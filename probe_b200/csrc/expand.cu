@@ -4,8 +4,10 @@
 // One kernel serves lora_expand_add (one adapter, every token) and
 // lora_sgmv_expand (per-tile adapter from the device schedule).  A CTA owns a
 // tile of <= 64 tokens x 128 output columns:
-//   1. z[tile, :R] is staged in shared memory (rounded to the input dtype,
-//      as the reference's tl.dot(z.to(b.dtype), b) does);
+//   1. z[tile, :R] is staged in shared memory in the input dtype.  An fp32 z
+//      (R <= 128) is staged as a hi/lo pair [round(z) | z - round(z)] and B
+//      twice, so the 16-bit tensor-core product keeps ~16 mantissa bits of z
+//      (the reference rounds z to the input dtype, tl.dot(z.to(b.dtype), b));
 //   2. B[:R, n-chunk] is staged as [n][j] rows (from the PEFT [N,R] layout or
 //      the rank-major flat table [sum R, N]) and re-staged only when the
 //      adapter changes;
@@ -44,10 +46,16 @@ struct ExpandArgs {
   float scale;
 };
 
+template <typename TZ>
+__host__ __device__ inline bool expand_splits(int rp) {
+  return sizeof(TZ) == 4 && rp <= 128;
+}
+
 template <typename T, typename TZ>
 __global__ void __launch_bounds__(128) expand_kernel(const ExpandArgs p) {
   extern __shared__ uint8_t smem_raw[];
-  const int rs = p.rp + 8;  // padded row stride (elements) -> conflict-free fragments
+  const bool split = expand_splits<TZ>(p.rp);
+  const int rs = (split ? 2 : 1) * p.rp + 8;  // padded row stride (elements) -> conflict-free fragments
   T* zs = reinterpret_cast<T*>(smem_raw);
   T* bs = zs + kExpTT * rs;
   float* cs = reinterpret_cast<float*>(bs + kExpBN * rs);
@@ -100,6 +108,7 @@ __global__ void __launch_bounds__(128) expand_kernel(const ExpandArgs p) {
           T v = from_f32<T>(0.f);
           if (j < R && n < p.N) v = b[bbase + static_cast<int64_t>(j) * p.b_sj + static_cast<int64_t>(n) * p.b_sn];
           bs[nn * rs + j] = v;
+          if (split) bs[nn * rs + r16 + j] = v;
         }
         staged_adapter = adapter;
       }
@@ -111,16 +120,19 @@ __global__ void __launch_bounds__(128) expand_kernel(const ExpandArgs p) {
           const int64_t zr = p.rows ? p.rows[t0 + t] : static_cast<int64_t>(t0 + t);
           v = to_f32(z[zr * p.ldz + j]);
         }
-        zs[t * rs + j] = from_f32<T>(v);
+        const T hi = from_f32<T>(v);
+        zs[t * rs + j] = hi;
+        if (split) zs[t * rs + r16 + j] = from_f32<T>(v - to_f32(hi));
       }
       __syncthreads();
+      const int kk = split ? 2 * r16 : r16;
 
       // ---- 16 tokens x 128 columns per warp
       float acc[16][4];
 #pragma unroll
       for (int i = 0; i < 16; ++i) acc[i][0] = acc[i][1] = acc[i][2] = acc[i][3] = 0.f;
       const T* za = zs + (warp * 16 + g) * rs + 2 * q;
-      for (int k = 0; k < r16; k += 16) {
+      for (int k = 0; k < kk; k += 16) {
         uint32_t af[4];
         af[0] = *reinterpret_cast<const uint32_t*>(za + k);
         af[1] = *reinterpret_cast<const uint32_t*>(za + 8 * rs + k);
@@ -196,13 +208,14 @@ __global__ void __launch_bounds__(128) expand_kernel(const ExpandArgs p) {
 }
 
 namespace {
-inline size_t expand_smem(int rp) {
-  return static_cast<size_t>(kExpTT + kExpBN) * (rp + 8) * 2 + static_cast<size_t>(kExpTT) * (kExpBN + 8) * 4;
+inline size_t expand_smem(int rp, bool split) {
+  return static_cast<size_t>(kExpTT + kExpBN) * ((split ? 2 : 1) * rp + 8) * 2 +
+         static_cast<size_t>(kExpTT) * (kExpBN + 8) * 4;
 }
 
 template <typename T, typename TZ>
 int launch_expand_t(const ExpandArgs& p, dim3 grid, cudaStream_t s) {
-  const size_t smem = expand_smem(p.rp);
+  const size_t smem = expand_smem(p.rp, expand_splits<TZ>(p.rp));
   auto kernel = expand_kernel<T, TZ>;
   if (smem > 48 * 1024) {
     if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)) !=

@@ -36,6 +36,7 @@ struct GemmArgs {
   const void* bias;
   int* err;
   int64_t ldo;
+  int64_t lo_offset;  // > 0: also write lo = v - round(v) at column + lo_offset
   int M, N, K, R;
   int num_kb_main, num_kb_tail, tail_last_k16;
   int num_m_tiles, num_n_tiles, num_tiles, group_m;
@@ -216,7 +217,17 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             for (int i = 0; i < 16; ++i)
               if (col0 + i < args.N) v[i] += to_f32(bias[col0 + i]);
           }
-          if (vec_ok && col0 + 16 <= args.N) {
+          if (args.lo_offset > 0) {
+            // hi/lo pair: out[c] = round(v), out[c + lo_offset] = round(v - round(v))
+#pragma unroll
+            for (int i = 0; i < 16; ++i) {
+              if (col0 + i < args.N) {
+                const T hi = from_f32<T>(v[i]);
+                out_row[col0 + i] = hi;
+                out_row[col0 + i + args.lo_offset] = from_f32<T>(v[i] - to_f32(hi));
+              }
+            }
+          } else if (vec_ok && col0 + 16 <= args.N) {
             uint4 w0, w1;
             w0.x = pack2<T>(v[0], v[1]);
             w0.y = pack2<T>(v[2], v[3]);
@@ -271,19 +282,20 @@ bool encode_tile_map(CUtensorMap* map, const void* ptr, int dtype, uint64_t inne
 template <int BN, int STAGES, typename T>
 int launch_gemm(const void* x, int64_t ldx, const void* w, int64_t ldw, const void* z, int64_t ldz,
                 const void* bw, int64_t ldbw, const void* bias, void* out, int64_t ldo, int64_t M,
-                int64_t N, int64_t K, int64_t R, float alpha, int dtype, cudaStream_t stream) {
+                int64_t N, int64_t K, int64_t R, float alpha, int64_t lo_offset, int dtype, cudaStream_t stream) {
   using L = GemmSmem<BN, STAGES, T>;
   const int dev = current_device();
   if (dev < 0) return LORA_ERR_DEVICE;
   const DeviceInfo& info = device_info(dev);
 
+  // The tail maps are exactly R wide: TMA fills the columns of the last
+  // 64-wide box beyond R with zeros, so z and bw need no padding.
   CUtensorMap tm_x, tm_w, tm_z, tm_b;
-  const uint64_t r64 = static_cast<uint64_t>((R + 63) / 64) * 64;
   if (!encode_tile_map(&tm_x, x, dtype, K, M, ldx, kGemmBK, kGemmBM)) return LORA_ERR_CUDA;
   if (!encode_tile_map(&tm_w, w, dtype, K, N, ldw, kGemmBK, BN)) return LORA_ERR_CUDA;
   if (R > 0) {
-    if (!encode_tile_map(&tm_z, z, dtype, r64, M, ldz, kGemmBK, kGemmBM)) return LORA_ERR_CUDA;
-    if (!encode_tile_map(&tm_b, bw, dtype, r64, N, ldbw, kGemmBK, BN)) return LORA_ERR_CUDA;
+    if (!encode_tile_map(&tm_z, z, dtype, R, M, ldz, kGemmBK, kGemmBM)) return LORA_ERR_CUDA;
+    if (!encode_tile_map(&tm_b, bw, dtype, R, N, ldbw, kGemmBK, BN)) return LORA_ERR_CUDA;
   } else {
     tm_z = tm_x;
     tm_b = tm_w;
@@ -294,6 +306,7 @@ int launch_gemm(const void* x, int64_t ldx, const void* w, int64_t ldw, const vo
   a.bias = bias;
   a.err = info.err_word;
   a.ldo = ldo;
+  a.lo_offset = lo_offset;
   a.M = static_cast<int>(M);
   a.N = static_cast<int>(N);
   a.K = static_cast<int>(K);
@@ -323,15 +336,16 @@ int launch_gemm(const void* x, int64_t ldx, const void* w, int64_t ldw, const vo
 template <typename T>
 int dispatch_gemm(int bn, const void* x, int64_t ldx, const void* w, int64_t ldw, const void* z, int64_t ldz,
                   const void* bw, int64_t ldbw, const void* bias, void* out, int64_t ldo, int64_t M, int64_t N,
-                  int64_t K, int64_t R, float alpha, int dtype, cudaStream_t stream) {
+                  int64_t K, int64_t R, float alpha, int64_t lo, int dtype, cudaStream_t stream) {
   switch (bn) {
     case 64:
-      return launch_gemm<64, 8, T>(x, ldx, w, ldw, z, ldz, bw, ldbw, bias, out, ldo, M, N, K, R, alpha, dtype, stream);
+      return launch_gemm<64, 8, T>(x, ldx, w, ldw, z, ldz, bw, ldbw, bias, out, ldo, M, N, K, R, alpha, lo, dtype,
+                                   stream);
     case 128:
-      return launch_gemm<128, 6, T>(x, ldx, w, ldw, z, ldz, bw, ldbw, bias, out, ldo, M, N, K, R, alpha, dtype,
+      return launch_gemm<128, 6, T>(x, ldx, w, ldw, z, ldz, bw, ldbw, bias, out, ldo, M, N, K, R, alpha, lo, dtype,
                                     stream);
     default:
-      return launch_gemm<256, 4, T>(x, ldx, w, ldw, z, ldz, bw, ldbw, bias, out, ldo, M, N, K, R, alpha, dtype,
+      return launch_gemm<256, 4, T>(x, ldx, w, ldw, z, ldz, bw, ldbw, bias, out, ldo, M, N, K, R, alpha, lo, dtype,
                                     stream);
   }
 }
@@ -356,7 +370,7 @@ int gemm_pick_bn(int64_t M, int64_t N, int num_sms) {
 
 extern "C" int lora_gemm(const void* x, int64_t ldx, const void* w, int64_t ldw, const void* z, int64_t ldz,
                          const void* bw, int64_t ldbw, const void* bias, void* out, int64_t ldo, int64_t M,
-                         int64_t N, int64_t K, int64_t R, float alpha, int dtype, void* stream) {
+                         int64_t N, int64_t K, int64_t R, float alpha, int64_t lo_offset, int dtype, void* stream) {
   using namespace lora;
   if (x == nullptr || w == nullptr || out == nullptr) return LORA_ERR_ARG;
   if (dtype != LORA_BF16 && dtype != LORA_F16) return LORA_ERR_DTYPE;
@@ -364,14 +378,14 @@ extern "C" int lora_gemm(const void* x, int64_t ldx, const void* w, int64_t ldw,
   if (M == 0 || N == 0) return LORA_OK;
   if (K == 0 && R == 0) return LORA_ERR_UNSUPPORTED;
   if (M > INT32_MAX || N > INT32_MAX || K > INT32_MAX || R > INT32_MAX) return LORA_ERR_SHAPE;
-  if (ldx < K || ldw < K || ldo < N) return LORA_ERR_SHAPE;
+  if (ldx < K || ldw < K || ldo < N || lo_offset < 0 || (lo_offset > 0 && (lo_offset < N || ldo < N + lo_offset)))
+    return LORA_ERR_SHAPE;
   if (K % 8 != 0 || ldx % 8 != 0 || ldw % 8 != 0) return LORA_ERR_ALIGN;
   if (!aligned16(x) || !aligned16(w)) return LORA_ERR_ALIGN;
   if (K == 0) return LORA_ERR_UNSUPPORTED;
   if (R > 0) {
     if (z == nullptr || bw == nullptr) return LORA_ERR_ARG;
-    const int64_t r64 = (R + 63) / 64 * 64;
-    if (ldz < r64 || ldbw < r64) return LORA_ERR_SHAPE;
+    if (ldz < R || ldbw < R) return LORA_ERR_SHAPE;
     if (ldz % 8 != 0 || ldbw % 8 != 0 || !aligned16(z) || !aligned16(bw)) return LORA_ERR_ALIGN;
   }
   const int dev = current_device();
@@ -382,6 +396,7 @@ extern "C" int lora_gemm(const void* x, int64_t ldx, const void* w, int64_t ldw,
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (dtype == LORA_BF16)
     return dispatch_gemm<__nv_bfloat16>(bn, x, ldx, w, ldw, z, ldz, bw, ldbw, bias, out, ldo, M, N, K, R, alpha,
-                                        dtype, s);
-  return dispatch_gemm<__half>(bn, x, ldx, w, ldw, z, ldz, bw, ldbw, bias, out, ldo, M, N, K, R, alpha, dtype, s);
+                                        lo_offset, dtype, s);
+  return dispatch_gemm<__half>(bn, x, ldx, w, ldw, z, ldz, bw, ldbw, bias, out, ldo, M, N, K, R, alpha, lo_offset,
+                               dtype, s);
 }

@@ -10,8 +10,13 @@
 //     product unchanged and keeps every access a full 32-byte sector;
 //   - K is split over CTAs (blockIdx.y).  Each split writes fp32 partials to
 //     the workspace; the last CTA to finish a tile (atomic ticket) sums them
-//     in split order, so results are deterministic and no float atomics or
-//     zero-fill launches are needed.  The ticket counters reset themselves.
+//     in split order, so results are deterministic and no float atomics are
+//     needed.  The ticket counters sit in a fixed region at the start of the
+//     workspace and the last CTA of each tile returns its counter to zero;
+//   - optionally z is written as a bf16/f16 hi/lo pair (hi = round(v),
+//     lo = round(v - hi), lo at column + z_width): fed to a tensor-core
+//     expand as two K-slices against a duplicated B, the pair carries ~16
+//     mantissa bits, so the expand is as accurate as an fp32 one.
 // With M <= 32 the four warps of a CTA also split their K slice and reduce
 // through shared memory, so decode-sized shrinks still fill the machine.
 //
@@ -41,6 +46,7 @@ struct ShrinkArgs {
   int64_t ldx, lda, ldz;
   int M, K, R, z_width, pr;
   int n_adapters;
+  int z_split;          // 1: also write lo = v - round(v) at column + z_width
   int split_k, kslice;  // kslice: multiple of 64
   int wt;               // token sub-tiles per CTA (1, 2, 4); 4 / wt warps split K
   int num_tiles_plain;
@@ -113,13 +119,20 @@ LORA_DEVINL void shrink_warp(const T* x, int64_t ldx, const int64_t* rows, int r
   }
 }
 
+// z_row[col] = v rounded to TZ; with split, z_row[col + width] = the residual.
 template <typename TZ>
-LORA_DEVINL void store_z(TZ* z, float v) {
-  *z = from_f32<TZ>(v);
+LORA_DEVINL void store_z(TZ* z_row, int col, int width, int split, float v) {
+  const TZ hi = from_f32<TZ>(v);
+  z_row[col] = hi;
+  if (split) z_row[col + width] = from_f32<TZ>(v - to_f32(hi));
 }
 
 template <bool ALIGNED, typename T, typename TZ, int NT>
 __global__ void __launch_bounds__(128) shrink_kernel(const ShrinkArgs p) {
+  // A kernel launched after this one with programmatic serialization (the
+  // decode GEMV) may start streaming W now; it reads z only after
+  // griddepcontrol.wait, i.e. after this grid has completed.
+  pdl_launch_dependents();
   __shared__ float red[4][16][NT * 8 + 1];
   __shared__ int s_last;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -205,7 +218,8 @@ __global__ void __launch_bounds__(128) shrink_kernel(const ShrinkArgs p) {
           for (int e = 0; e < 2; ++e) {
             const int col = nt * 8 + 2 * q + e;
             if (p.split_k == 1) {
-              if (col < p.z_width) store_z<TZ>(z + pt * p.ldz + col, col < R ? p.scale * acc[nt][2 * h + e] : 0.f);
+              if (col < p.z_width)
+                store_z<TZ>(z + pt * p.ldz, col, p.z_width, p.z_split, col < R ? p.scale * acc[nt][2 * h + e] : 0.f);
             } else if (col < p.pr) {
               p.partial[(static_cast<int64_t>(ks) * p.M + t) * p.pr + col] = acc[nt][2 * h + e];
             }
@@ -216,7 +230,7 @@ __global__ void __launch_bounds__(128) shrink_kernel(const ShrinkArgs p) {
         // zero-fill columns beyond the mma tiles up to z_width
         for (int row = 0; row < nrows; ++row)
           for (int col = NT * 8 + lane; col < p.z_width; col += 32)
-            store_z<TZ>(z + phys_row(p.rows, row0 + row) * p.ldz + col, 0.f);
+            store_z<TZ>(z + phys_row(p.rows, row0 + row) * p.ldz, col, p.z_width, p.z_split, 0.f);
       }
     }
 
@@ -240,7 +254,7 @@ __global__ void __launch_bounds__(128) shrink_kernel(const ShrinkArgs p) {
             for (int s = 0; s < p.split_k; ++s) v += __ldcg(&p.partial[(static_cast<int64_t>(s) * p.M + t) * p.pr + col]);
             v *= p.scale;
           }
-          store_z<TZ>(z + phys_row(p.rows, t) * p.ldz + col, v);
+          store_z<TZ>(z + phys_row(p.rows, t) * p.ldz, col, width, p.z_split, v);
         }
         if (threadIdx.x == 0) p.counters[tile] = 0;
       }
@@ -318,11 +332,14 @@ int shrink_pick_split_k_impl(int64_t tiles, int64_t K, int num_sms) {
 
 using namespace lora;
 
+namespace {
+inline size_t round256(size_t v) { return (v + 255) / 256 * 256; }
+}  // namespace
+
 extern "C" size_t lora_shrink_workspace_size(int64_t M, int64_t R, int split_k) {
   if (M <= 0 || R <= 0 || split_k <= 1) return 256;
   const size_t partial = static_cast<size_t>(split_k) * M * R * sizeof(float);
-  const size_t counters = static_cast<size_t>((M + 15) / 16) * sizeof(int);
-  return ((partial + 255) / 256) * 256 + ((counters + 255) / 256) * 256;
+  return kCounterBytes + round256(partial);
 }
 
 extern "C" int lora_shrink_pick_split_k(int64_t M, int64_t K, int64_t R) {
@@ -334,13 +351,14 @@ extern "C" int lora_shrink_pick_split_k(int64_t M, int64_t K, int64_t R) {
 }
 
 extern "C" int lora_shrink(const void* x, int64_t ldx, const void* a, int64_t lda, void* z, int64_t ldz, int z_dtype,
-                           int64_t z_width, int64_t M, int64_t K, int64_t R, float scale, int dtype, int split_k,
-                           void* workspace, size_t workspace_bytes, void* stream) {
+                           int64_t z_width, int z_split, int64_t M, int64_t K, int64_t R, float scale, int dtype,
+                           int split_k, void* workspace, size_t workspace_bytes, void* stream) {
   if (x == nullptr || a == nullptr || z == nullptr) return LORA_ERR_ARG;
   if (dtype != LORA_BF16 && dtype != LORA_F16) return LORA_ERR_DTYPE;
   if (z_dtype != LORA_F32 && z_dtype != dtype) return LORA_ERR_DTYPE;
+  if (z_split != 0 && (z_split != 1 || z_dtype == LORA_F32)) return LORA_ERR_ARG;
   if (M < 0 || K < 0 || R < 0 || R > 128 || z_width < R) return LORA_ERR_SHAPE;
-  if (M > INT32_MAX || K > INT32_MAX || ldz < z_width || ldx < K || lda < K) return LORA_ERR_SHAPE;
+  if (M > INT32_MAX || K > INT32_MAX || ldz < z_width * (1 + z_split) || ldx < K || lda < K) return LORA_ERR_SHAPE;
   if (M == 0 || z_width == 0) return LORA_OK;
   const int dev = current_device();
   if (dev < 0 || !device_info(dev).is_sm100) return LORA_ERR_DEVICE;
@@ -364,30 +382,31 @@ extern "C" int lora_shrink(const void* x, int64_t ldx, const void* a, int64_t ld
   p.K = static_cast<int>(K);
   p.R = static_cast<int>(R);
   p.z_width = static_cast<int>(z_width);
+  p.z_split = z_split;
   p.pr = static_cast<int>(R);
   p.split_k = split_k;
   p.kslice = kslice;
   p.wt = wt;
   p.num_tiles_plain = static_cast<int>(tiles);
   p.scale = scale;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (split_k > 1) {
     const size_t need = lora_shrink_workspace_size(M, R, split_k);
     if (workspace == nullptr || workspace_bytes < need || !al16(workspace)) return LORA_ERR_WORKSPACE;
-    const size_t partial = static_cast<size_t>(split_k) * M * R * sizeof(float);
-    p.partial = static_cast<float*>(workspace);
-    p.counters = reinterpret_cast<int*>(static_cast<char*>(workspace) + ((partial + 255) / 256) * 256);
+    if (tiles > kMaxCounters) return LORA_ERR_SHAPE;
+    p.counters = static_cast<int*>(workspace);
+    p.partial = reinterpret_cast<float*>(static_cast<char*>(workspace) + kCounterBytes);
   }
   const bool aligned = (K % 8 == 0) && (ldx % 8 == 0) && (lda % 8 == 0) && al16(x) && al16(a);
   const int64_t gx = std::min<int64_t>(tiles, std::max<int64_t>(1, (4 * static_cast<int64_t>(info.num_sms) + split_k - 1) / split_k));
   dim3 grid(static_cast<unsigned>(gx), static_cast<unsigned>(split_k));
-  return launch_shrink(p, dtype, z_dtype, aligned, grid, static_cast<cudaStream_t>(stream));
+  return launch_shrink(p, dtype, z_dtype, aligned, grid, s);
 }
 
 extern "C" size_t lora_sgmv_shrink_workspace_size(int64_t T, int64_t S, int64_t z_width, int split_k) {
   if (T <= 0 || z_width <= 0 || split_k <= 1) return 256;
   const size_t partial = static_cast<size_t>(split_k) * T * z_width * sizeof(float);
-  const size_t counters = static_cast<size_t>(sgmv_max_tiles(T, S)) * sizeof(int);
-  return ((partial + 255) / 256) * 256 + ((counters + 255) / 256) * 256;
+  return kCounterBytes + round256(partial);
 }
 
 extern "C" int lora_sgmv_shrink(const void* x, int64_t ldx, const void* a_flat, int64_t lda, const int64_t* offsets,
@@ -434,17 +453,18 @@ extern "C" int lora_sgmv_shrink(const void* x, int64_t ldx, const void* a_flat, 
   p.kslice = kslice;
   p.wt = 4;
   p.scale = scale;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (split_k > 1) {
     const size_t need = lora_sgmv_shrink_workspace_size(T, S, z_width, split_k);
     if (workspace == nullptr || workspace_bytes < need || !al16(workspace)) return LORA_ERR_WORKSPACE;
-    const size_t partial = static_cast<size_t>(split_k) * T * z_width * sizeof(float);
-    p.partial = static_cast<float*>(workspace);
-    p.counters = reinterpret_cast<int*>(static_cast<char*>(workspace) + ((partial + 255) / 256) * 256);
+    if (sgmv_max_tiles(T, S) > kMaxCounters) return LORA_ERR_SHAPE;
+    p.counters = static_cast<int*>(workspace);
+    p.partial = reinterpret_cast<float*>(static_cast<char*>(workspace) + kCounterBytes);
   }
   const bool aligned = (K % 8 == 0) && (ldx % 8 == 0) && (lda % 8 == 0) && al16(x) && al16(a_flat);
   const int64_t max_tiles = sgmv_max_tiles(T, S);
   const int64_t gx = std::min<int64_t>(
       max_tiles, std::max<int64_t>(1, (4 * static_cast<int64_t>(info.num_sms) + split_k - 1) / split_k));
   dim3 grid(static_cast<unsigned>(gx), static_cast<unsigned>(split_k));
-  return launch_shrink(p, dtype, z_dtype, aligned, grid, static_cast<cudaStream_t>(stream));
+  return launch_shrink(p, dtype, z_dtype, aligned, grid, s);
 }

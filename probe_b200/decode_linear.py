@@ -36,7 +36,7 @@ def build_decode_linear(weight, bias, a, b, scale=1.0, *, block_n=16, block_k=25
         outs = []
         for i in range(0, x.shape[0], 64):
             xs = x[i: i + 64]
-            z = kernels.shrink(xs, a, 1.0, z_dtype=xs.dtype)
+            z = kernels.shrink(xs, a, 1.0, z_dtype=torch.float32)
             outs.append(kernels.decode_linear(xs, weight, z, b, bias, scale))
         return outs[0] if len(outs) == 1 else torch.cat(outs)
 

@@ -29,7 +29,7 @@ import statistics
 import torch
 
 from . import kernels
-from .kernels import pad_cols, round_up
+from .kernels import round_up
 
 # Rank tile constants kept for API compatibility (fused_linear.py:61-72).
 MIN_RANK_TILE = 16
@@ -87,39 +87,43 @@ def expand_add(y, z, b, scale):
     return kernels.expand_add(y, z, b, scale)
 
 
-def _shrink_into(x, a, scale, width, z_dtype=None):
-    """``scale * x @ a.T`` as a ``[M, width]`` tensor zero beyond rank."""
-    r = a.shape[0]
-    z_dtype = x.dtype if z_dtype is None else z_dtype
-    if r <= SHRINK_MMA_MAX_RANK:
-        return kernels.shrink(x, a, scale, z_dtype=z_dtype, z_width=width)
-    a_pad = torch.zeros((width, a.shape[1]), device=a.device, dtype=a.dtype)
-    a_pad[:r] = a
-    return kernels.gemm(x, a_pad, alpha=scale)
-
-
 class _KConcat:
-    """Plan-time state of the kconcat variant: B zero-padded to a 64-wide tail."""
+    """Plan-time state of the kconcat variant.
+
+    The tail of the fused GEMM is ``[hi | lo]`` of ``s.z = scale * x @ A.T``
+    (each part r16 = roundup(r, 16) wide, zero beyond r) against
+    ``[B | B]``: hi = round(s.z) and lo = round(s.z - hi) in the input dtype, so
+    the expand keeps ~16 mantissa bits of z for twice the (small) tail width.
+    """
 
     def __init__(self, weight, bias, a, b, scale):
         self.weight = weight.contiguous()
         self.bias = None if bias is None else bias.contiguous()
         self.a = a.contiguous()
         self.r = a.shape[0]
-        self.width = round_up(self.r, kernels.GEMM_TAIL_ALIGN)
-        self.b_pad = pad_cols(b.to(weight.dtype), self.width)
+        self.r16 = round_up(self.r, 16)
+        self.tail = 2 * self.r16
+        b = b.to(weight.dtype)
+        self.b_dup = torch.zeros((weight.shape[0], self.tail), device=weight.device, dtype=weight.dtype)
+        self.b_dup[:, : self.r] = b
+        self.b_dup[:, self.r16: self.r16 + self.r] = b
         self.scale = float(scale)
         self.a_pad = None
         if self.r > SHRINK_MMA_MAX_RANK:
-            self.a_pad = torch.zeros((self.width, self.a.shape[1]), device=a.device, dtype=a.dtype)
+            self.a_pad = torch.zeros((self.r16, self.a.shape[1]), device=a.device, dtype=a.dtype)
             self.a_pad[: self.r] = self.a
 
-    def __call__(self, x, out=None):
+    def shrink(self, x):
+        """``[hi | lo]`` of ``scale * x @ A.T``, shape [M, 2 * r16]."""
         if self.a_pad is None:
-            z = kernels.shrink(x, self.a, self.scale, z_dtype=x.dtype, z_width=self.width)
-        else:
-            z = kernels.gemm(x, self.a_pad, alpha=self.scale)
-        return kernels.gemm(x, self.weight, z, self.b_pad, rank=self.r, bias=self.bias, out=out)
+            return kernels.shrink(x, self.a, self.scale, z_dtype=x.dtype, z_width=self.r16, z_split=True)
+        z = torch.empty((x.shape[0], self.tail), device=x.device, dtype=x.dtype)
+        kernels.gemm(x, self.a_pad, alpha=self.scale, out=z[:, : self.r16], lo_offset=self.r16)
+        return z
+
+    def __call__(self, x, out=None):
+        z = self.shrink(x)
+        return kernels.gemm(x, self.weight, z, self.b_dup, rank=self.tail, bias=self.bias, out=out)
 
 
 def fused_gemm(x, weight, bias, a, b, scale, out=None):
@@ -187,15 +191,15 @@ def _concat(x, weight_aug, bias_aug, b, scale, n):
 
 
 def _hybrid(x, weight, bias, a, b, scale):
-    """Base GEMM, shrink (rounded to the input dtype, as torch.mm does), expand-add."""
+    """Base GEMM, fp32 shrink, expand-add epilogue."""
     y = kernels.gemm(x, weight, bias=bias)
-    z = kernels.shrink(x, a, 1.0, z_dtype=x.dtype)
+    z = kernels.shrink(x, a, 1.0, z_dtype=torch.float32)
     return expand_add(y, z, b, scale)
 
 
 def _decode(x, weight, bias, a, b, scale):
-    """Small-M path: shrink then the W-streaming decode kernel with the expand as a K tail."""
-    z = kernels.shrink(x, a, 1.0, z_dtype=x.dtype)
+    """Small-M path: fp32 shrink then the W-streaming decode kernel with the expand as a K tail."""
+    z = kernels.shrink(x, a, 1.0, z_dtype=torch.float32)
     return kernels.decode_linear(x, weight, z, b, bias, scale)
 
 

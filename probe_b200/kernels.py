@@ -41,11 +41,12 @@ def pad_cols(t: torch.Tensor, width: int) -> torch.Tensor:
 # ----------------------------------------------------------------------- GEMM
 def gemm(x: torch.Tensor, w: torch.Tensor, z: torch.Tensor | None = None, bw: torch.Tensor | None = None,
          rank: int = 0, bias: torch.Tensor | None = None, alpha: float = 1.0,
-         out: torch.Tensor | None = None) -> torch.Tensor:
+         out: torch.Tensor | None = None, lo_offset: int = 0) -> torch.Tensor:
     """``out = alpha * (x @ w.T + z[:, :rank] @ bw[:, :rank].T) + bias`` on tcgen05.
 
-    ``z`` and ``bw`` must be zero-padded to a multiple of 64 columns (see
-    :func:`pad_cols`); ``rank`` is the true width.  rank == 0 is a plain linear.
+    ``rank`` is the width of the K-slice tail (columns of z / bw beyond it are
+    not read); rank == 0 is a plain linear.  ``lo_offset > 0`` writes the
+    result as a hi/lo pair, the residual at column + lo_offset of ``out``.
     """
     _lib.require_cuda(x, w, where="gemm")
     _check_half(x, "gemm")
@@ -65,25 +66,32 @@ def gemm(x: torch.Tensor, w: torch.Tensor, z: torch.Tensor | None = None, bw: to
         out = torch.empty((m, n), device=x.device, dtype=x.dtype)
     elif out.shape != (m, n) or out.stride(1) != 1 or out.dtype != x.dtype:
         raise ValueError("gemm: out must be a row-major [M, N] tensor of the input dtype")
+    if lo_offset and out.stride(0) < n + lo_offset:
+        raise ValueError("gemm: lo_offset needs out rows of at least N + lo_offset elements")
     if rank > 0:
         if z is None or bw is None or z.dtype != x.dtype or bw.dtype != x.dtype:
             raise ValueError("gemm: z and bw are required (input dtype) when rank > 0")
         z = _lib.row_major(z)
         bw = _lib.row_major(bw)
-        if z.shape[0] != m or bw.shape[0] != n or z.shape[1] < round_up(rank, 64) or bw.shape[1] < round_up(rank, 64):
-            raise ValueError("gemm: z / bw must be [M|N, >= roundup(rank, 64)] zero-padded tails")
+        if z.shape[0] != m or bw.shape[0] != n or z.shape[1] < rank or bw.shape[1] < rank:
+            raise ValueError("gemm: z / bw must be [M|N, >= rank]")
     _lib.call("lora_gemm", _lib.ptr(x), _lib.ld(x), _lib.ptr(w), _lib.ld(w),
               _lib.ptr(z) if rank > 0 else None, _lib.ld(z) if rank > 0 else 0,
               _lib.ptr(bw) if rank > 0 else None, _lib.ld(bw) if rank > 0 else 0,
-              _lib.ptr(bias), _lib.ptr(out), out.stride(0), m, n, k, int(rank), float(alpha), _dt(x),
+              _lib.ptr(bias), _lib.ptr(out), out.stride(0), m, n, k, int(rank), float(alpha), int(lo_offset), _dt(x),
               _lib.stream_handle(x.device))
     return out
 
 
 # --------------------------------------------------------------------- shrink
 def shrink(x: torch.Tensor, a: torch.Tensor, scale: float = 1.0, z_dtype: torch.dtype | None = torch.float32,
-           z_width: int | None = None, split_k: int = 0, out: torch.Tensor | None = None) -> torch.Tensor:
-    """Split-K ``z = scale * x @ a.T`` -> ``[M, z_width]`` (zeros beyond rank)."""
+           z_width: int | None = None, split_k: int = 0, out: torch.Tensor | None = None,
+           z_split: bool = False) -> torch.Tensor:
+    """Split-K ``z = scale * x @ a.T`` -> ``[M, z_width]`` (zeros beyond rank).
+
+    ``z_split`` (input dtype only) appends the rounding residual, giving
+    ``[round(z) | z - round(z)]`` of width ``2 * z_width``.
+    """
     _lib.require_cuda(x, a, where="shrink")
     _check_half(x, "shrink")
     if a.dtype != x.dtype:
@@ -98,15 +106,17 @@ def shrink(x: torch.Tensor, a: torch.Tensor, scale: float = 1.0, z_dtype: torch.
         raise ValueError("shrink: rank above 128 goes through the tensor-core GEMM (gemm)")
     z_dtype = x.dtype if z_dtype is None else z_dtype
     width = r if z_width is None else int(z_width)
+    if z_split and z_dtype == torch.float32:
+        raise ValueError("shrink: z_split needs a 16-bit z")
     if out is None:
-        out = torch.empty((m, width), device=x.device, dtype=z_dtype)
+        out = torch.empty((m, width * (2 if z_split else 1)), device=x.device, dtype=z_dtype)
     if split_k <= 0:
         split_k = _lib.load().lora_shrink_pick_split_k(m, k, r)
     ws_bytes = _lib.load().lora_shrink_workspace_size(m, r, split_k)
     ws = _lib.WORKSPACE.get(ws_bytes, x.device, "shrink")
     _lib.call("lora_shrink", _lib.ptr(x), _lib.ld(x), _lib.ptr(a), _lib.ld(a), _lib.ptr(out), out.stride(0),
-              _lib.dtype_code(out.dtype), width, m, k, r, float(scale), _dt(x), int(split_k), _lib.ptr(ws), ws.numel(),
-              _lib.stream_handle(x.device))
+              _lib.dtype_code(out.dtype), width, 1 if z_split else 0, m, k, r, float(scale), _dt(x), int(split_k),
+              _lib.ptr(ws), ws.numel(), _lib.stream_handle(x.device))
     return out
 
 

@@ -43,9 +43,13 @@ def test_workspace_sizes_are_host_only(lib):
 
 def test_argument_errors_without_gpu(lib):
     # NULL pointers and bad dtypes are rejected before any device work
-    assert lib.lora_gemm(None, 0, None, 0, None, 0, None, 0, None, None, 0, 1, 1, 8, 0, 1.0, 1, None) == _lib.LORA_ERR_ARG
+    assert lib.lora_gemm(None, 0, None, 0, None, 0, None, 0, None, None, 0, 1, 1, 8, 0, 1.0, 0, 1,
+                         None) == _lib.LORA_ERR_ARG
     p = ctypes.c_void_p(16)
-    assert lib.lora_shrink(p, 8, p, 8, p, 8, 7, 8, 1, 8, 4, 1.0, 1, 1, None, 0, None) == _lib.LORA_ERR_DTYPE
+    assert lib.lora_shrink(p, 8, p, 8, p, 8, 7, 8, 0, 1, 8, 4, 1.0, 1, 1, None, 0, None) == _lib.LORA_ERR_DTYPE
+    # a split (hi/lo) z must be 16-bit
+    assert lib.lora_shrink(p, 8, p, 8, p, 16, _lib.LORA_F32, 8, 1, 1, 8, 4, 1.0, 1, 1, None, 0,
+                           None) == _lib.LORA_ERR_ARG
     assert lib.lora_expand_add(p, 8, p, 8, 2, p, 8, 5, None, p, 8, 1, 8, 4, 1.0, 1, None) == _lib.LORA_ERR_ARG
     assert lib.lora_decode_linear(p, 8, p, 8, None, 0, 1, None, 0, None, p, 8, 65, 8, 8, 0, 1.0, 1, 0, None, 0,
                                   None) == _lib.LORA_ERR_SHAPE

@@ -76,6 +76,13 @@ def test_shrink(dtype, m, k, r, split_k):
     assert fro < 2e-6, fro
     zq = kernels.shrink(x, a, 1.5, z_dtype=dtype, split_k=split_k)
     assert_parity(zq, want[:, :r], dtype)
+    # hi/lo pair: hi is the rounded z, hi + lo carries ~16 mantissa bits
+    zs = kernels.shrink(x, a, 1.5, z_dtype=dtype, z_width=width, z_split=True, split_k=split_k)
+    assert zs.shape == (m, 2 * width)
+    assert torch.equal(zs[:, :r], zq)
+    pair = np64(zs[:, :width]) + np64(zs[:, width:])
+    _, fro = orc.parity(pair, want)
+    assert fro < 2e-5, fro
 
 
 def test_shrink_deterministic():
@@ -99,7 +106,9 @@ def test_expand_add(dtype, m, n, r, layout):
     y0 = y.clone()
     out = kernels.expand_add(y, z, bb, 0.5, bias=bias, b_layout=layout)
     assert torch.equal(y, y0)
-    zq = orc.round_dtype(np64(z).astype(np.float32), "bf16" if dtype == torch.bfloat16 else "f16")
+    # an fp32 z is carried as a hi/lo pair up to rank 128 (rounded above that)
+    zq = np64(z) if r <= 128 else orc.round_dtype(np64(z).astype(np.float32),
+                                                   "bf16" if dtype == torch.bfloat16 else "f16")
     want = orc.expand_add(np64(y), zq, np64(b), 0.5, np64(bias))
     assert_parity(out, want, dtype)
     out2 = kernels.expand_add(None, z, bb, 0.5, b_layout=layout, dtype=dtype)
@@ -116,12 +125,16 @@ def test_decode_linear(dtype, m, k, n, r):
     bias = randn((n,), 1.0, dtype, seed=3)
     a = randn((r, k), 1 / math.sqrt(k), dtype, seed=4) if r else None
     b = randn((n, r), 1 / math.sqrt(max(r, 1)), dtype, seed=5) if r else None
-    z = kernels.shrink(x, a, 1.0, z_dtype=dtype) if r else None
+    z = kernels.shrink(x, a, 1.0, z_dtype=torch.float32) if r else None
     out = kernels.decode_linear(x, w, z, b, bias, -0.7)
-    tag = "bf16" if dtype == torch.bfloat16 else "f16"
-    want = orc.decode_linear(np64(x), np64(w), np64(bias), np64(a) if r else None, np64(b) if r else None, -0.7,
-                             tag)
+    want = orc.naive_linear(np64(x), np64(w), np64(bias), np64(a) if r else None, np64(b) if r else None, -0.7)
     assert_parity(out, want, dtype)
+    # with z rounded to the input dtype first, the reference's decode semantics
+    if r:
+        zr = kernels.shrink(x, a, 1.0, z_dtype=dtype)
+        tag = "bf16" if dtype == torch.bfloat16 else "f16"
+        want_r = orc.decode_linear(np64(x), np64(w), np64(bias), np64(a), np64(b), -0.7, tag)
+        assert_parity(kernels.decode_linear(x, w, zr, b, bias, -0.7), want_r, dtype)
 
 
 def test_decode_zero_rank_is_base():
@@ -133,6 +146,34 @@ def test_decode_zero_rank_is_base():
     z = kernels.shrink(x, a, 1.0, z_dtype=torch.bfloat16)
     with_zero_b = kernels.decode_linear(x, w, z, b, None, 1.0)
     assert torch.equal(base, with_zero_b)
+
+
+def test_gemm_hi_lo_epilogue():
+    m, n, k = 300, 224, 512
+    x = randn((m, k), 1.0, seed=21)
+    w = randn((n, k), 1 / math.sqrt(k), seed=22)
+    z = torch.empty((m, 2 * n), dtype=torch.bfloat16, device="cuda")
+    kernels.gemm(x, w, alpha=0.7, out=z[:, :n], lo_offset=n)
+    want = 0.7 * (np64(x) @ np64(w).T)
+    assert_parity(z[:, :n], want)
+    _, fro = orc.parity(np64(z[:, :n]) + np64(z[:, n:]), want)
+    assert fro < 2e-5, fro
+
+
+def test_workspace_reuse_across_shapes():
+    """Split-K tickets stay valid when one workspace serves calls of different shapes."""
+    torch.manual_seed(3)
+    cases = [(64, 256, 192, 16), (33, 128, 96, 7), (8, 4096, 11008, 16), (1, 640, 64, 3), (64, 256, 192, 16)]
+    for rep in range(2):
+        for m, k, n, r in cases:
+            x = randn((m, k), 1.0, seed=m + rep)
+            w = randn((n, k), 1 / math.sqrt(k), seed=n)
+            a = randn((r, k), 1 / math.sqrt(k), seed=r)
+            b = randn((n, r), 1 / math.sqrt(r), seed=r + 1)
+            z = kernels.shrink(x, a, 1.0, z_dtype=torch.float32, split_k=4)
+            out = kernels.decode_linear(x, w, z, b, None, 0.5, split_k=3)
+            assert_parity(out, orc.naive_linear(np64(x), np64(w), None, np64(a), np64(b), 0.5))
+    assert _lib.device_error() == 0
 
 
 def test_device_error_word_clear():
