@@ -39,7 +39,7 @@ sys.path.insert(0, str(ROOT))
 METRIC = "fused LoRA-linear TFLOP/s & tokens/s per B200 (1/2/4/8 GPU), % of roofline"
 WORKLOAD = "C5 Wan DiT block projections (q,k,v,o 5120->5120; ffn 5120->13824->5120) with 3-LoRA stack r=32/64/128 (w 1.0/0.7/0.4) -> r224"
 M_TOKENS = 32760
-CPU_SAMPLE_TOKENS = 1024
+CPU_SAMPLE_TOKENS = 4096
 
 
 def parse():
@@ -118,7 +118,7 @@ class ClockSampler:
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
-                 "-lms", "200"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+                 "-lms", "100"], stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
         except (OSError, FileNotFoundError):
             self.proc = None
 
@@ -331,7 +331,7 @@ def run_gpu(args):
     if e2e is not None:
         line["e2e"] = e2e
     if world == 1 and not args.no_cpu:
-        line["cpu_baseline"] = cpu_baseline(steps=1)
+        line["cpu_baseline"] = cpu_baseline(steps=5)
     print(json.dumps(line), flush=True)
 
 

@@ -217,8 +217,22 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             for (int i = 0; i < 16; ++i)
               if (col0 + i < args.N) v[i] += to_f32(bias[col0 + i]);
           }
-          if (args.lo_offset > 0) {
+          if (args.lo_offset > 0 && vec_ok && (args.lo_offset % 8) == 0 && col0 + 16 <= args.N) {
             // hi/lo pair: out[c] = round(v), out[c + lo_offset] = round(v - round(v))
+            uint32_t hw[8], lw[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+              const T h0 = from_f32<T>(v[2 * i]), h1 = from_f32<T>(v[2 * i + 1]);
+              hw[i] = pack2<T>(to_f32(h0), to_f32(h1));
+              lw[i] = pack2<T>(v[2 * i] - to_f32(h0), v[2 * i + 1] - to_f32(h1));
+            }
+            uint4* dh = reinterpret_cast<uint4*>(out_row + col0);
+            uint4* dl = reinterpret_cast<uint4*>(out_row + col0 + args.lo_offset);
+            dh[0] = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+            dh[1] = make_uint4(hw[4], hw[5], hw[6], hw[7]);
+            dl[0] = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+            dl[1] = make_uint4(lw[4], lw[5], lw[6], lw[7]);
+          } else if (args.lo_offset > 0) {
 #pragma unroll
             for (int i = 0; i < 16; ++i) {
               if (col0 + i < args.N) {

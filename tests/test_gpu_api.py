@@ -69,8 +69,10 @@ def test_golden_c1_full_config():
                             p.a.to(DEV, torch.bfloat16), p.b.to(DEV, torch.bfloat16), p.scale)
     o = np64(out)
     assert_parity(out[torch.as_tensor(d["rows"], device=DEV)], d["bf16in_rows"])
-    # size-independent properties over the whole output
-    assert np.abs(o.sum(1) - d["bf16in_row_sums"]).max() < 0.5
+    # size-independent properties over the whole output.  Each bf16 output carries
+    # a rounding error of std ~ ulp/sqrt(12) (~0.0045 at |y| ~ 2); a row sum of
+    # 4096 of them random-walks to ~0.29, so 2.0 is a ~6 sigma bound.
+    assert np.abs(o.sum(1) - d["bf16in_row_sums"]).max() < 2.0
     assert abs(np.linalg.norm(o) - float(d["bf16in_fro"])) / float(d["bf16in_fro"]) < 2e-3
 
 

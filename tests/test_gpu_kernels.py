@@ -72,8 +72,9 @@ def test_shrink(dtype, m, k, r, split_k):
     want[:, :r] = orc.shrink(np64(x), np64(a), 1.5)
     g = np64(z)
     assert np.array_equal(g[:, r:], np.zeros_like(g[:, r:]))
+    # fp32 accumulation over K: relative error ~ sqrt(K) * 2^-24 (4e-6 at K = 4096)
     _, fro = orc.parity(g, want)
-    assert fro < 2e-6, fro
+    assert fro < 2e-5, fro
     zq = kernels.shrink(x, a, 1.5, z_dtype=dtype, split_k=split_k)
     assert_parity(zq, want[:, :r], dtype)
     # hi/lo pair: hi is the rounded z, hi + lo carries ~16 mantissa bits
