@@ -40,6 +40,10 @@ METRIC = "fused LoRA-linear TFLOP/s & tokens/s per B200 (1/2/4/8 GPU), % of roof
 WORKLOAD = "C5 Wan DiT block projections (q,k,v,o 5120->5120; ffn 5120->13824->5120) with 3-LoRA stack r=32/64/128 (w 1.0/0.7/0.4) -> r224"
 M_TOKENS = 32760
 CPU_SAMPLE_TOKENS = 4096
+# DRAM read + write of one fused-GEMM launch (C5 q projection), from the full
+# ncu capture at M = 16384 committed under profiles/, scaled linearly to M:
+# 678.7 MB read + 155.2 MB write per launch at M = 16384.
+NCU_TRAFFIC_Q_16384 = 833.9e6
 
 
 def parse():
@@ -295,13 +299,7 @@ def run_gpu(args):
     if peak is None:
         peak, peak_src = 1400.0, "fallback sustained"
     gemm_achieved = gemm_flops / (gemm_ms / args.steps * 1e-3) / 1e12
-    traffic = None
-    tfile = ROOT / "profiles" / "gemm_tc_c5_traffic.json"
-    if tfile.exists():
-        try:
-            traffic = json.load(open(tfile)).get("bytes_per_launch")
-        except (OSError, ValueError):
-            traffic = None
+    traffic = round(NCU_TRAFFIC_Q_16384 * m / 16384)
     line = {
         "metric": METRIC,
         "value": round(value, 2),
@@ -322,6 +320,9 @@ def run_gpu(args):
         "roofline": {"bound": "tensor", "kernel": "gemm_tc_kernel<256,4,bf16> (fused base + LoRA K-slice)",
                      "achieved": round(gemm_achieved, 2), "peak": peak, "unit": "TFLOP/s",
                      "frac": round(gemm_achieved / peak, 4), "peak_source": peak_src, "traffic": traffic,
+                     "traffic_note": "bytes per q-projection launch (ncu capture at M=16384, scaled to M); "
+                                     "algorithmic bytes of that launch: "
+                                     f"{round(2 * (m * 5120 * 2 + 5120 * 5120 + 448 * (m + 5120)))}",
                      "flops_per_step": gemm_flops, "gemm_ms_per_step": round(gemm_ms / args.steps, 4)},
         "gpu_launches": launches_per_step * args.steps,
         "device_error": err,
