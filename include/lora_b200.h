@@ -122,6 +122,28 @@ LORA_API int lora_shrink(const void* x, int64_t ldx, const void* a, int64_t lda,
                 float scale, int dtype, int split_k, void* workspace, size_t workspace_bytes,
                 void* stream);
 
+/* The same split-K shrink for callers that cannot allocate device memory:
+ * code running while a CUDA graph is being captured, serving loops that cannot
+ * afford cudaMalloc's implicit device synchronisation, or host frameworks that
+ * own all device memory and forbid plugins from allocating.  It takes no
+ * workspace: the ticket counters and partial sums live in an 8 MiB array of
+ * device memory that the library holds on every GPU that loads it, until the
+ * process exits.  The caller still passes x, a and z.  Limit: with split_k > 1
+ * the partials need split_k * M * R * 4 bytes <= 8 MiB - 16 KiB
+ * (lora_shrink_static_scratch_capacity()) and at most 4096 token tiles;
+ * split_k == 0 picks the widest split that fits (down to 1, which needs no
+ * scratch); an explicit split_k that does not fit returns LORA_ERR_WORKSPACE.
+ * The first call on a device looks up the array's device address
+ * (cudaGetSymbolAddress), so make that first call before any stream capture.
+ * All calls share the one array: calls that overlap on the GPU (several
+ * streams or threads) race and must be serialised on one stream.
+ * No counterpart in the reference (its wrappers allocate per call). */
+LORA_API size_t lora_shrink_static_scratch_capacity(void);
+LORA_API int lora_shrink_static_scratch(const void* x, int64_t ldx, const void* a, int64_t lda,
+                                        void* z, int64_t ldz, int z_dtype, int64_t z_width,
+                                        int z_split, int64_t M, int64_t K, int64_t R, float scale,
+                                        int dtype, int split_k, void* stream);
+
 /* ---------------------------------------------------------------------------
  * Expand + add   out[M,N] = y[M,N] + scale * z[M,R] . B^T + bias[N]
  * y may be NULL (treated as zero) and may not alias out.  z is f32 or the

@@ -53,6 +53,9 @@ SIGNATURES = {
     "lora_shrink_workspace_size": (_SZ, [_I64, _I64, _I]),
     "lora_shrink_pick_split_k": (_I, [_I64, _I64, _I64]),
     "lora_shrink": (_I, [_P, _I64, _P, _I64, _P, _I64, _I, _I64, _I, _I64, _I64, _I64, _F, _I, _I, _P, _SZ, _P]),
+    "lora_shrink_static_scratch_capacity": (_SZ, []),
+    "lora_shrink_static_scratch": (_I, [_P, _I64, _P, _I64, _P, _I64, _I, _I64, _I, _I64, _I64, _I64, _F, _I, _I,
+                                        _P]),
     "lora_expand_add": (_I, [_P, _I64, _P, _I64, _I, _P, _I64, _I, _P, _P, _I64, _I64, _I64, _I64, _F, _I, _P]),
     "lora_decode_workspace_size": (_SZ, [_I64, _I64, _I]),
     "lora_decode_pick_split_k": (_I, [_I64, _I64, _I64]),

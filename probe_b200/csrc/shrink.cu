@@ -25,6 +25,7 @@
 // segmented_branch.py:12-28 and ragged_branch.py:6-16 (per-segment / per-token
 // adapter, rank-0 skip).
 #include <algorithm>
+#include <mutex>
 
 #include "common.cuh"
 #include "runtime.h"
@@ -465,6 +466,118 @@ extern "C" int lora_sgmv_shrink(const void* x, int64_t ldx, const void* a_flat, 
   const int64_t max_tiles = sgmv_max_tiles(T, S);
   const int64_t gx = std::min<int64_t>(
       max_tiles, std::max<int64_t>(1, (4 * static_cast<int64_t>(info.num_sms) + split_k - 1) / split_k));
+  dim3 grid(static_cast<unsigned>(gx), static_cast<unsigned>(split_k));
+  return launch_shrink(p, dtype, z_dtype, aligned, grid, s);
+}
+
+// ---------------------------------------------------------------------------
+// Split-K shrink with library-held scratch.
+//
+// Some callers cannot call cudaMalloc: code that runs while a CUDA graph is
+// being captured, serving loops that cannot afford cudaMalloc's implicit
+// device synchronisation, and host frameworks that own all device memory and
+// forbid plugins from allocating.  lora_shrink_static_scratch takes no
+// workspace: its ticket counters and fp32 partials live in the file-scope
+// array below, which every GPU that loads this library holds until exit.
+// Every call shares that array, so calls that overlap on the GPU (concurrent
+// streams, several host threads) race; serialise them on one stream.
+namespace {
+
+constexpr size_t kStaticScratchBytes = size_t(8) << 20;   // 8 MiB in total
+constexpr size_t kStaticCounterBytes = size_t(16) << 10;  // 4096 ticket counters
+constexpr size_t kStaticPartialBytes = kStaticScratchBytes - kStaticCounterBytes;
+
+static __device__ __align__(256) unsigned char g_shrink_scratch[kStaticScratchBytes];
+
+// Device address of g_shrink_scratch, looked up once per device with that
+// device current (in host code the array's name is only a stand-in).
+std::once_flag g_scratch_once[64];
+void* g_scratch_addr[64];
+cudaError_t g_scratch_status[64];
+
+int static_scratch(int dev, void** addr) {
+  std::call_once(g_scratch_once[dev], [dev] {
+    void* p = nullptr;
+    g_scratch_status[dev] = cudaGetSymbolAddress(&p, g_shrink_scratch);
+    g_scratch_addr[dev] = (g_scratch_status[dev] == cudaSuccess) ? p : nullptr;
+  });
+  if (g_scratch_status[dev] != cudaSuccess || g_scratch_addr[dev] == nullptr) return LORA_ERR_CUDA;
+  *addr = g_scratch_addr[dev];
+  return LORA_OK;
+}
+
+}  // namespace
+
+extern "C" size_t lora_shrink_static_scratch_capacity(void) { return kStaticPartialBytes; }
+
+extern "C" int lora_shrink_static_scratch(const void* x, int64_t ldx, const void* a, int64_t lda, void* z,
+                                          int64_t ldz, int z_dtype, int64_t z_width, int z_split, int64_t M,
+                                          int64_t K, int64_t R, float scale, int dtype, int split_k,
+                                          void* stream) {
+  if (x == nullptr || a == nullptr || z == nullptr) return LORA_ERR_ARG;
+  if (dtype != LORA_BF16 && dtype != LORA_F16) return LORA_ERR_DTYPE;
+  if (z_dtype != LORA_F32 && z_dtype != dtype) return LORA_ERR_DTYPE;
+  if (z_split != 0 && (z_split != 1 || z_dtype == LORA_F32)) return LORA_ERR_ARG;
+  if (M < 0 || K < 0 || R < 0 || R > 128 || z_width < R || split_k < 0) return LORA_ERR_SHAPE;
+  if (M > INT32_MAX || K > INT32_MAX || ldz < z_width * (1 + z_split) || ldx < K || lda < K) return LORA_ERR_SHAPE;
+  if (M == 0 || z_width == 0) return LORA_OK;
+  // device_info() is not used here: it allocates the library's error word.
+  const int dev = current_device();
+  if (dev < 0) return LORA_ERR_DEVICE;
+  int major = 0, minor = 0, sms = 0;
+  if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess ||
+      cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev) != cudaSuccess ||
+      cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+    return LORA_ERR_DEVICE;
+  if (major != 10 || minor != 0) return LORA_ERR_DEVICE;
+  void* scratch = nullptr;
+  if (const int rc = static_scratch(dev, &scratch); rc != LORA_OK) return rc;
+
+  const int wt = shrink_wt(M);
+  const int64_t tiles = (M + 16 * wt - 1) / (16 * wt);
+  const bool explicit_split = split_k > 0;
+  if (R == 0 || K == 0) split_k = 1;
+  if (split_k <= 0) split_k = shrink_pick_split_k_impl(tiles, K, sms > 0 ? sms : 148);
+  auto fits = [&](int sk) {
+    return sk == 1 || (static_cast<size_t>(sk) * M * R * sizeof(float) <= kStaticPartialBytes &&
+                       tiles <= static_cast<int64_t>(kStaticCounterBytes / sizeof(int)));
+  };
+  if (!explicit_split)
+    while (split_k > 1 && !fits(split_k)) --split_k;
+  const int kslice = shrink_kslice(K, split_k);
+  split_k = static_cast<int>(std::max<int64_t>((K + kslice - 1) / kslice, 1));
+  if (!fits(split_k)) return LORA_ERR_WORKSPACE;  // would need more than the 8 MiB array holds
+
+  ShrinkArgs p{};
+  p.x = x;
+  p.a = a;
+  p.z = z;
+  p.err = nullptr;
+  p.ldx = ldx;
+  p.lda = lda;
+  p.ldz = ldz;
+  p.M = static_cast<int>(M);
+  p.K = static_cast<int>(K);
+  p.R = static_cast<int>(R);
+  p.z_width = static_cast<int>(z_width);
+  p.z_split = z_split;
+  p.pr = static_cast<int>(R);
+  p.split_k = split_k;
+  p.kslice = kslice;
+  p.wt = wt;
+  p.num_tiles_plain = static_cast<int>(tiles);
+  p.scale = scale;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (split_k > 1) {
+    p.counters = static_cast<int*>(scratch);
+    p.partial = reinterpret_cast<float*>(static_cast<char*>(scratch) + kStaticCounterBytes);
+    // The tickets must start at zero; the array keeps whatever the last call left.
+    if (cudaMemsetAsync(scratch, 0, static_cast<size_t>(tiles) * sizeof(int), s) != cudaSuccess)
+      return LORA_ERR_CUDA;
+  }
+  const bool aligned = (K % 8 == 0) && (ldx % 8 == 0) && (lda % 8 == 0) && al16(x) && al16(a);
+  const int64_t gx =
+      std::min<int64_t>(tiles, std::max<int64_t>(1, (4 * static_cast<int64_t>(sms) + split_k - 1) / split_k));
   dim3 grid(static_cast<unsigned>(gx), static_cast<unsigned>(split_k));
   return launch_shrink(p, dtype, z_dtype, aligned, grid, s);
 }
