@@ -317,7 +317,8 @@ def run_gpu(args):
         "config": {"workload": WORKLOAD, "tokens_per_gpu": m, "global_tokens": total_tokens, "lora_rank": 224,
                    "parallelism": f"token-sharded x{world}, weights+adapters replicated, no collective",
                    "l2": "every input > 126 MB L2 (x >= 335 MB per projection); no flush needed"},
-        "roofline": {"bound": "tensor", "kernel": "gemm_tc_kernel<256,4,bf16> (fused base + LoRA K-slice)",
+        "roofline": {"bound": "tensor", "kernel": ("gemm_tc_kernel<256,4,bf16>" if os.environ.get("LORA_B200_GEMM") == "1sm"
+                                else "gemm_tc2_kernel<6,bf16> (CTA pair)") + " fused base + LoRA K-slice",
                      "achieved": round(gemm_achieved, 2), "peak": peak, "unit": "TFLOP/s",
                      "frac": round(gemm_achieved / peak, 4), "peak_source": peak_src, "traffic": traffic,
                      "traffic_note": "bytes per q-projection launch (ncu capture at M=16384, scaled to M); "

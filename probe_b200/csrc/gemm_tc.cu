@@ -16,9 +16,13 @@
 // Two TMEM accumulators (2*BN columns) let the epilogue of tile i overlap the
 // mainloop of tile i+1.  Tiles are rasterised in GROUP_M bands so the W tiles
 // of a band stay L2-resident (the reference's GROUP_M swizzle,
-// fused_linear.py:245-254).  No cluster launch and no TMA multicast.
+// fused_linear.py:245-254).  No TMA multicast.  Wide outputs use the
+// CTA-pair form below (gemm_tc2_kernel); narrow ones (N < 256, e.g. a rank
+// shrink) and small problems use this single-CTA kernel.
 #include <cudaTypedefs.h>
 
+#include <cstdlib>
+#include <cstring>
 #include <mutex>
 #include <type_traits>
 
@@ -275,6 +279,240 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
   }
 }
 
+// ----------------------------------------------------------- CTA-pair GEMM
+//
+// The same fused GEMM on 256x256 tiles shared by a cluster of two CTAs
+// (tcgen05 cta_group::2).  Each CTA loads its own 128 rows of x (or z) and
+// its own 128 rows of W (or B_dup) per 64-wide K block -- 32 KB per SM per
+// block instead of 48 KB for a 128x256 single-CTA tile, with the same MMA work
+// per SM -- and the leader's single thread issues M=256 N=256 K=16 MMAs that
+// read both CTAs' shared memory and leave each CTA's 128 accumulator rows in
+// its own TMEM.  Both CTAs' TMA loads complete on the leader's "full"
+// barrier; the leader's commits arrive on the "empty" and "accumulator full"
+// barriers of both CTAs; both CTAs' epilogues arrive on the leader's
+// "accumulator empty" barrier.  No load uses cluster multicast.
+template <int STAGES>
+struct PairSmem {
+  static constexpr int kABytes = 128 * kGemmBK * 2;
+  static constexpr int kBBytes = 128 * kGemmBK * 2;
+  static constexpr int kStageBytes = kABytes + kBBytes;
+  static constexpr int kBarOffset = STAGES * kStageBytes;
+  static constexpr int kBytes = kBarOffset + 256 + 1024;
+};
+
+template <typename T>
+LORA_DEVINL void epilogue_store16(const GemmArgs& args, T* out_row, const T* bias, int row, int col0, bool vec_ok,
+                                  const uint32_t* r) {
+  if (row >= args.M || col0 >= args.N) return;
+  float v[16];
+#pragma unroll
+  for (int i = 0; i < 16; ++i) v[i] = __uint_as_float(r[i]) * args.alpha;
+  if (bias != nullptr) {
+#pragma unroll
+    for (int i = 0; i < 16; ++i)
+      if (col0 + i < args.N) v[i] += to_f32(bias[col0 + i]);
+  }
+  if (args.lo_offset > 0 && vec_ok && (args.lo_offset % 8) == 0 && col0 + 16 <= args.N) {
+    uint32_t hw[8], lw[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const T h0 = from_f32<T>(v[2 * i]), h1 = from_f32<T>(v[2 * i + 1]);
+      hw[i] = pack2<T>(to_f32(h0), to_f32(h1));
+      lw[i] = pack2<T>(v[2 * i] - to_f32(h0), v[2 * i + 1] - to_f32(h1));
+    }
+    uint4* dh = reinterpret_cast<uint4*>(out_row + col0);
+    uint4* dl = reinterpret_cast<uint4*>(out_row + col0 + args.lo_offset);
+    dh[0] = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+    dh[1] = make_uint4(hw[4], hw[5], hw[6], hw[7]);
+    dl[0] = make_uint4(lw[0], lw[1], lw[2], lw[3]);
+    dl[1] = make_uint4(lw[4], lw[5], lw[6], lw[7]);
+  } else if (args.lo_offset > 0) {
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      if (col0 + i < args.N) {
+        const T hi = from_f32<T>(v[i]);
+        out_row[col0 + i] = hi;
+        out_row[col0 + i + args.lo_offset] = from_f32<T>(v[i] - to_f32(hi));
+      }
+    }
+  } else if (vec_ok && col0 + 16 <= args.N) {
+    uint32_t w[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) w[i] = pack2<T>(v[2 * i], v[2 * i + 1]);
+    uint4* dst = reinterpret_cast<uint4*>(out_row + col0);
+    dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
+    dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
+  } else {
+#pragma unroll
+    for (int i = 0; i < 16; ++i)
+      if (col0 + i < args.N) out_row[col0 + i] = from_f32<T>(v[i]);
+  }
+}
+
+template <int STAGES, typename T>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
+    gemm_tc2_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_w,
+                    const __grid_constant__ CUtensorMap tm_z, const __grid_constant__ CUtensorMap tm_b,
+                    const GemmArgs args) {
+  using L = PairSmem<STAGES>;
+  constexpr uint32_t kTmemCols = 512;  // two 256-column fp32 accumulators
+  constexpr uint32_t kIdesc = umma_idesc_f16(256, 256, std::is_same<T, __nv_bfloat16>::value ? 1 : 0);
+  constexpr uint16_t kBoth = 0x3;
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  uint8_t* sm_a = smem;
+  uint8_t* sm_b = smem + STAGES * L::kABytes;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::kBarOffset);
+  uint64_t* empty = full + STAGES;
+  uint64_t* acc_full = empty + STAGES;
+  uint64_t* acc_empty = acc_full + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = (rank == 0);
+  const int pair = blockIdx.x >> 1;
+  const int npairs = gridDim.x >> 1;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&acc_full[a], 1);
+      mbar_init(&acc_empty[a], 8);  // 4 epilogue warps in each CTA of the pair
+    }
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tm_x);
+    tma_prefetch_desc(&tm_w);
+    if (args.num_kb_tail > 0) {
+      tma_prefetch_desc(&tm_z);
+      tma_prefetch_desc(&tm_b);
+    }
+  }
+  if (warp == 2) {
+    tmem_alloc_pair(tmem_slot, kTmemCols);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  cluster_sync_all();  // barriers of both CTAs initialised, TMEM allocated
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  const int num_kb = args.num_kb_main + args.num_kb_tail;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int tile = pair; ok && tile < args.num_tiles; tile += npairs) {
+        int mt, nt;
+        gemm_tile_coords(tile, args, mt, nt);
+        const int row_a = mt * 256 + static_cast<int>(rank) * 128;
+        const int row_b = nt * 256 + static_cast<int>(rank) * 128;
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait_bounded(&empty[stage], phase ^ 1, abort_flag, args.err, kDevErrTimeoutEmpty)) {
+            ok = false;
+            break;
+          }
+          if (leader) mbar_arrive_expect_tx(&full[stage], 2 * L::kStageBytes);
+          const uint32_t bar = mapa_shared(smem_u32(&full[stage]), 0);
+          if (kb < args.num_kb_main) {
+            tma_load_2d_pair(&tm_x, sm_a + stage * L::kABytes, bar, kb * kGemmBK, row_a);
+            tma_load_2d_pair(&tm_w, sm_b + stage * L::kBBytes, bar, kb * kGemmBK, row_b);
+          } else {
+            const int kt = kb - args.num_kb_main;
+            tma_load_2d_pair(&tm_z, sm_a + stage * L::kABytes, bar, kt * kGemmBK, row_a);
+            tma_load_2d_pair(&tm_b, sm_b + stage * L::kBBytes, bar, kt * kGemmBK, row_b);
+          }
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------- MMA issuer (leader CTA only)
+    if (leader && lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int local = 0;
+      bool ok = true;
+      for (int tile = pair; ok && tile < args.num_tiles; tile += npairs, ++local) {
+        const int acc = local & 1;
+        const uint32_t acc_phase = (local >> 1) & 1;
+        if (!mbar_wait_bounded(&acc_empty[acc], acc_phase ^ 1, abort_flag, args.err, kDevErrTimeoutAccEmpty))
+          break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * 256);
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait_bounded(&full[stage], phase, abort_flag, args.err, kDevErrTimeoutFull)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint64_t adesc = umma_desc_sw128(smem_u32(sm_a + stage * L::kABytes));
+          const uint64_t bdesc = umma_desc_sw128(smem_u32(sm_b + stage * L::kBBytes));
+          const int nk = (kb == num_kb - 1 && args.num_kb_tail > 0) ? args.tail_last_k16 : 4;
+          for (int k = 0; k < nk; ++k)
+            tc_mma_f16_pair(d_tmem, adesc + static_cast<uint64_t>(2 * k), bdesc + static_cast<uint64_t>(2 * k),
+                            kIdesc, (kb > 0 || k > 0) ? 1u : 0u);
+          tc_commit_pair(&empty[stage], kBoth);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (ok) tc_commit_pair(&acc_full[acc], kBoth);
+      }
+    }
+  } else {
+    // ------------------------------------------------ epilogue (both CTAs)
+    const int quad = warp & 3;
+    const T* bias = static_cast<const T*>(args.bias);
+    const bool vec_ok = (args.ldo % 8) == 0 && (reinterpret_cast<uintptr_t>(args.out) % 16) == 0;
+    int local = 0;
+    for (int tile = pair; tile < args.num_tiles; tile += npairs, ++local) {
+      const int acc = local & 1;
+      const uint32_t acc_phase = (local >> 1) & 1;
+      int mt, nt;
+      gemm_tile_coords(tile, args, mt, nt);
+      if (!mbar_wait_bounded(&acc_full[acc], acc_phase, abort_flag, args.err, kDevErrTimeoutAccFull)) break;
+      tc_fence_after();
+      const int row = mt * 256 + static_cast<int>(rank) * 128 + quad * 32 + lane;
+      T* out_row = static_cast<T*>(args.out) + static_cast<int64_t>(row) * args.ldo;
+      const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + static_cast<uint32_t>(acc * 256);
+#pragma unroll 1
+      for (int c = 0; c < 256; c += 16) {
+        uint32_t r[16];
+        tmem_ld_32x32b_x16(t_row + c, r);
+        tmem_wait_ld();
+        epilogue_store16<T>(args, out_row, bias, row, nt * 256 + c, vec_ok, r);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(&acc_empty[acc]), 0));
+    }
+  }
+
+  tc_fence_before();
+  cluster_sync_all();  // no CTA leaves while its partner may still touch its shared memory
+  if (warp == 2) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, kTmemCols);
+  }
+}
+
 // ------------------------------------------------------------------- host
 namespace {
 
@@ -371,6 +609,83 @@ inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 
 // Tile width: narrow outputs (a rank-r shrink, N <= 128) get the narrowest
 // tile that covers them; wide ones use 256 unless that leaves fewer than two
 // waves of tiles on the machine.
+namespace {
+
+template <int STAGES, typename T>
+int launch_gemm_pair(const void* x, int64_t ldx, const void* w, int64_t ldw, const void* z, int64_t ldz,
+                     const void* bw, int64_t ldbw, const void* bias, void* out, int64_t ldo, int64_t M, int64_t N,
+                     int64_t K, int64_t R, float alpha, int64_t lo_offset, int dtype, cudaStream_t stream) {
+  using L = PairSmem<STAGES>;
+  const int dev = current_device();
+  if (dev < 0) return LORA_ERR_DEVICE;
+  const DeviceInfo& info = device_info(dev);
+  CUtensorMap tm_x, tm_w, tm_z, tm_b;
+  if (!encode_tile_map(&tm_x, x, dtype, K, M, ldx, kGemmBK, 128)) return LORA_ERR_CUDA;
+  if (!encode_tile_map(&tm_w, w, dtype, K, N, ldw, kGemmBK, 128)) return LORA_ERR_CUDA;
+  if (R > 0) {
+    if (!encode_tile_map(&tm_z, z, dtype, R, M, ldz, kGemmBK, 128)) return LORA_ERR_CUDA;
+    if (!encode_tile_map(&tm_b, bw, dtype, R, N, ldbw, kGemmBK, 128)) return LORA_ERR_CUDA;
+  } else {
+    tm_z = tm_x;
+    tm_b = tm_w;
+  }
+  GemmArgs a;
+  a.out = out;
+  a.bias = bias;
+  a.err = info.err_word;
+  a.ldo = ldo;
+  a.lo_offset = lo_offset;
+  a.M = static_cast<int>(M);
+  a.N = static_cast<int>(N);
+  a.K = static_cast<int>(K);
+  a.R = static_cast<int>(R);
+  a.num_kb_main = static_cast<int>((K + kGemmBK - 1) / kGemmBK);
+  a.num_kb_tail = static_cast<int>((R + kGemmBK - 1) / kGemmBK);
+  const int tail_rem = static_cast<int>(R - static_cast<int64_t>(a.num_kb_tail - 1) * kGemmBK);
+  a.tail_last_k16 = a.num_kb_tail > 0 ? (tail_rem + 15) / 16 : 4;
+  a.num_m_tiles = static_cast<int>((M + 255) / 256);
+  a.num_n_tiles = static_cast<int>((N + 255) / 256);
+  a.num_tiles = a.num_m_tiles * a.num_n_tiles;
+  a.group_m = 8;
+  a.alpha = alpha;
+
+  auto kernel = gemm_tc2_kernel<STAGES, T>;
+  static std::once_flag once[64];
+  static cudaError_t attr_err[64];
+  static int max_clusters[64];
+  std::call_once(once[dev & 63], [&] {
+    attr_err[dev & 63] = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kBytes);
+    int clusters = 0;
+    if (attr_err[dev & 63] == cudaSuccess) {
+      cudaLaunchConfig_t cfg = {};
+      cfg.gridDim = dim3(2 * info.num_sms);
+      cfg.blockDim = dim3(kGemmThreads);
+      cfg.dynamicSmemBytes = L::kBytes;
+      if (cudaOccupancyMaxActiveClusters(&clusters, kernel, &cfg) != cudaSuccess) {
+        cudaGetLastError();
+        clusters = info.num_sms / 2;
+      }
+    }
+    max_clusters[dev & 63] = clusters > 0 ? clusters : info.num_sms / 2;
+  });
+  if (attr_err[dev & 63] != cudaSuccess) return LORA_ERR_CUDA;
+  const int pairs = static_cast<int>(std::min<int64_t>(a.num_tiles, max_clusters[dev & 63]));
+  kernel<<<2 * pairs, kGemmThreads, L::kBytes, stream>>>(tm_x, tm_w, tm_z, tm_b, a);
+  return cudaGetLastError() == cudaSuccess ? LORA_OK : LORA_ERR_CUDA;
+}
+
+// Pair tiles when the output is wide and there are enough 256x256 tiles to
+// keep every SM pair busy; LORA_B200_GEMM=1sm / 2sm forces one or the other.
+bool use_pair_tiles(int64_t M, int64_t N, int num_sms) {
+  const char* force = std::getenv("LORA_B200_GEMM");
+  if (force != nullptr && std::strcmp(force, "1sm") == 0) return false;
+  const int64_t tiles = ((M + 255) / 256) * ((N + 255) / 256);
+  if (force != nullptr && std::strcmp(force, "2sm") == 0) return N > 128;
+  return N >= 256 && tiles >= num_sms;
+}
+
+}  // namespace
+
 int gemm_pick_bn(int64_t M, int64_t N, int num_sms) {
   if (N <= 64) return 64;
   if (N <= 128) return 128;
@@ -408,6 +723,13 @@ extern "C" int lora_gemm(const void* x, int64_t ldx, const void* w, int64_t ldw,
   if (!info.is_sm100) return LORA_ERR_DEVICE;
   const int bn = gemm_pick_bn(M, N, info.num_sms);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (use_pair_tiles(M, N, info.num_sms)) {
+    if (dtype == LORA_BF16)
+      return launch_gemm_pair<6, __nv_bfloat16>(x, ldx, w, ldw, z, ldz, bw, ldbw, bias, out, ldo, M, N, K, R, alpha,
+                                                lo_offset, dtype, s);
+    return launch_gemm_pair<6, __half>(x, ldx, w, ldw, z, ldz, bw, ldbw, bias, out, ldo, M, N, K, R, alpha,
+                                       lo_offset, dtype, s);
+  }
   if (dtype == LORA_BF16)
     return dispatch_gemm<__nv_bfloat16>(bn, x, ldx, w, ldw, z, ldz, bw, ldbw, bias, out, ldo, M, N, K, R, alpha,
                                         lo_offset, dtype, s);
