@@ -56,6 +56,8 @@ def parse():
     p.add_argument("--tokens", type=int, default=M_TOKENS)
     p.add_argument("--no-e2e", action="store_true")
     p.add_argument("--no-cpu", action="store_true")
+    p.add_argument("--workload", default="c5", choices=["c1", "c2", "c3", "c4", "c5"],
+                   help="c5 is the headline; c1-c4 measure the other configs against their own rooflines")
     return p.parse_args()
 
 
@@ -364,10 +366,135 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
+# ------------------------------------------------------- other configs (C1-C4)
+def _peaks():
+    try:
+        return json.load(open(ROOT / "MEASURED_PEAKS.json"))
+    except (OSError, ValueError):
+        return {}
+
+
+def _time_flushed(fn, iters, dev):
+    """Median device time (ms) of fn, each run from a cold L2 (a 512 MB write in between).
+
+    fn is captured once in a CUDA graph, so the time is the kernels' own, not
+    the host's launch overhead."""
+    import torch
+
+    flush = torch.empty(512 << 20, dtype=torch.uint8, device=dev)
+    for _ in range(3):
+        fn()
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        fn()
+    times = []
+    for _ in range(iters):
+        flush.zero_()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        g.replay()
+        b.record()
+        b.synchronize()
+        times.append(a.elapsed_time(b))
+    del g
+    return statistics.median(times)
+
+
+def run_config(args):
+    """One JSON line for config c1-c4, each against the roofline that bounds it."""
+    import torch
+
+    from probe_b200 import _lib, kernels, segmented_branch, workloads
+    from probe_b200.fused_linear import _KConcat, build_plan
+
+    _lib.load()
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    peaks = _peaks()
+    hbm = peaks.get("hbm_gbs", 6650.0)
+    tc = peaks.get("bf16_tflops", 1590.0)
+    line = {"metric": METRIC, "n_gpus": 1, "steps": args.steps, "warmup": 3, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded Gaussian; no public dataset)"}
+    bf = torch.bfloat16
+    if args.workload in ("c1", "c2"):
+        cases = [workloads.c1(device="cpu")] if args.workload == "c1" else \
+            [workloads.c2(m, device="cpu") for m in (1, 4, 16, 64)]
+        rows = []
+        for p in cases:
+            x, w, a, b = (t.to(dev, bf) for t in (p.x, p.w, p.a, p.b))
+            plan = build_plan(x, w, None, a, b, p.scale)
+            ms = _time_flushed(lambda: plan(x), max(args.steps, 20), dev)
+            flops, nbytes = p.flops(), p.bytes()
+            rows.append({"m": p.m, "ms": round(ms, 5), "tflops": round(flops / ms / 1e9, 2),
+                         "gbs": round(nbytes / ms / 1e6, 1), "hbm_frac": round(nbytes / ms / 1e6 / hbm, 4),
+                         "t_star_us": round(max(flops / tc / 1e12, nbytes / hbm / 1e9) * 1e6, 2)})
+        main = rows[-1]
+        line.update({"value": main["gbs"], "unit": "GB/s", "ms_per_step": main["ms"],
+                     "tokens_per_s": round(main["m"] / main["ms"] * 1e3, 1),
+                     "config": {"workload": "C1 single fused LoRA linear 256x4096x4096 r16" if args.workload == "c1"
+                                else "C2 decode LoRA linear M in {1,4,16,64}, W 11008x4096, r16",
+                                "cases": rows, "l2": "512 MB flush before every timed run"},
+                     "roofline": {"bound": "hbm", "achieved": main["gbs"], "peak": hbm, "unit": "GB/s",
+                                  "frac": main["hbm_frac"], "peak_source": "measured (MEASURED_PEAKS.json)"}})
+    elif args.workload == "c3":
+        c = workloads.c3(device="cpu", dtype=bf)
+        x, w = c.x.to(dev), c.w.to(dev)
+        y = kernels.gemm(x, w)
+        tabs = [t.to(dev) for t in (c.a_flat, c.b_flat, c.offsets, c.ranks, c.seg_start, c.seg_adapter)]
+        fn = lambda: segmented_branch.segmented_branch_varlen(x, y, *tabs, c.r_max)
+        ms = _time_flushed(fn, max(args.steps, 20), dev)
+        flops, nbytes = c.branch_flops(), c.branch_bytes()
+        gbs = nbytes / ms / 1e6
+        line.update({"value": round(gbs, 1), "unit": "GB/s", "ms_per_step": round(ms, 5),
+                     "tokens_per_s": round(4096 / ms * 1e3, 1),
+                     "config": {"workload": "C3 segmented multi-LoRA branch: 4096 tokens, 128 Zipf(1.1) segments, "
+                                            "64 adapters r in {4..64}, K=N=4096",
+                                "tflops": round(flops / ms / 1e9, 3), "bytes": nbytes,
+                                "l2": "512 MB flush before every timed run"},
+                     "roofline": {"bound": "hbm", "achieved": round(gbs, 1), "peak": hbm, "unit": "GB/s",
+                                  "frac": round(gbs / hbm, 4), "peak_source": "measured (MEASURED_PEAKS.json)"}})
+    else:  # c4
+        projs = workloads.c4(device=dev, dtype=bf)
+        runners = [_KConcat(p.w, p.bias, p.a, p.b, p.scale) for p in projs]
+        outs = [torch.empty((p.m, p.n), device=dev, dtype=bf) for p in projs]
+
+        def step():
+            for p, run, o in zip(projs, runners, outs):
+                run(p.x, out=o)
+
+        for _ in range(3):
+            step()
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(args.steps):
+            step()
+        b.record()
+        b.synchronize()
+        ms = a.elapsed_time(b) / args.steps
+        flops = sum(p.flops() for p in projs)
+        tf = flops / ms / 1e9
+        sus = peaks.get("bf16_tflops_sustained", 1400.0)
+        line.update({"value": round(tf, 2), "unit": "TFLOP/s", "ms_per_step": round(ms, 4),
+                     "tokens_per_s": round(8192 / ms * 1e3, 1),
+                     "config": {"workload": "C4 Llama-7B layer prefill, M=8192, r16 on q,k,v,o,gate,up,down",
+                                "l2": "inputs >= 67 MB per projection, 7 projections per step"},
+                     "roofline": {"bound": "tensor", "achieved": round(tf, 2), "peak": sus, "unit": "TFLOP/s",
+                                  "frac": round(tf / sus, 4),
+                                  "peak_source": "measured sustained (MEASURED_PEAKS.json)"}})
+    line["workload_id"] = args.workload
+    line["device_error"] = _lib.device_error(0)
+    print(json.dumps(line), flush=True)
+
+
 def main():
     args = parse()
     if args.impl == "reference":
         run_reference(args)
+    elif args.workload != "c5":
+        run_config(args)
     else:
         run_gpu(args)
 

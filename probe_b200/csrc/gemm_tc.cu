@@ -44,6 +44,7 @@ struct GemmArgs {
   int M, N, K, R;
   int num_kb_main, num_kb_tail, tail_last_k16;
   int num_m_tiles, num_n_tiles, num_tiles, group_m;
+  int l2_hints;  // bit 0: W / B_dup evict_last; bit 1: x / z evict_first; bit 2: out evict_first
   float alpha;
 };
 
@@ -302,7 +303,7 @@ struct PairSmem {
 
 template <typename T>
 LORA_DEVINL void epilogue_store16(const GemmArgs& args, T* out_row, const T* bias, int row, int col0, bool vec_ok,
-                                  const uint32_t* r) {
+                                  const uint32_t* r, uint64_t st_policy) {
   if (row >= args.M || col0 >= args.N) return;
   float v[16];
 #pragma unroll
@@ -340,8 +341,13 @@ LORA_DEVINL void epilogue_store16(const GemmArgs& args, T* out_row, const T* bia
 #pragma unroll
     for (int i = 0; i < 8; ++i) w[i] = pack2<T>(v[2 * i], v[2 * i + 1]);
     uint4* dst = reinterpret_cast<uint4*>(out_row + col0);
-    dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
-    dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
+    if (args.l2_hints & 4) {
+      st_global_v4_hint(dst, make_uint4(w[0], w[1], w[2], w[3]), st_policy);
+      st_global_v4_hint(dst + 1, make_uint4(w[4], w[5], w[6], w[7]), st_policy);
+    } else {
+      dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
+      dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
+    }
   } else {
 #pragma unroll
     for (int i = 0; i < 16; ++i)
@@ -411,6 +417,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
   if (warp == 0) {
     // ------------------------------------------------------------ producer
     if (lane == 0) {
+      const uint64_t pol_keep = l2_policy_evict_last();     // W, B_dup: reused by every M band
+      const uint64_t pol_stream = l2_policy_evict_first();  // x, z
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
@@ -426,14 +434,18 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
           }
           if (leader) mbar_arrive_expect_tx(&full[stage], 2 * L::kStageBytes);
           const uint32_t bar = mapa_shared(smem_u32(&full[stage]), 0);
-          if (kb < args.num_kb_main) {
-            tma_load_2d_pair(&tm_x, sm_a + stage * L::kABytes, bar, kb * kGemmBK, row_a);
-            tma_load_2d_pair(&tm_w, sm_b + stage * L::kBBytes, bar, kb * kGemmBK, row_b);
-          } else {
-            const int kt = kb - args.num_kb_main;
-            tma_load_2d_pair(&tm_z, sm_a + stage * L::kABytes, bar, kt * kGemmBK, row_a);
-            tma_load_2d_pair(&tm_b, sm_b + stage * L::kBBytes, bar, kt * kGemmBK, row_b);
-          }
+          const bool tail = kb >= args.num_kb_main;
+          const CUtensorMap* ma = tail ? &tm_z : &tm_x;
+          const CUtensorMap* mb = tail ? &tm_b : &tm_w;
+          const int kc = (tail ? kb - args.num_kb_main : kb) * kGemmBK;
+          if (args.l2_hints & 2)
+            tma_load_2d_pair_hint(ma, sm_a + stage * L::kABytes, bar, kc, row_a, pol_stream);
+          else
+            tma_load_2d_pair(ma, sm_a + stage * L::kABytes, bar, kc, row_a);
+          if (args.l2_hints & 1)
+            tma_load_2d_pair_hint(mb, sm_b + stage * L::kBBytes, bar, kc, row_b, pol_keep);
+          else
+            tma_load_2d_pair(mb, sm_b + stage * L::kBBytes, bar, kc, row_b);
           if (++stage == STAGES) {
             stage = 0;
             phase ^= 1;
@@ -481,6 +493,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
     const int quad = warp & 3;
     const T* bias = static_cast<const T*>(args.bias);
     const bool vec_ok = (args.ldo % 8) == 0 && (reinterpret_cast<uintptr_t>(args.out) % 16) == 0;
+    const uint64_t st_policy = l2_policy_evict_first();
     int local = 0;
     for (int tile = pair; tile < args.num_tiles; tile += npairs, ++local) {
       const int acc = local & 1;
@@ -497,7 +510,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
         uint32_t r[16];
         tmem_ld_32x32b_x16(t_row + c, r);
         tmem_wait_ld();
-        epilogue_store16<T>(args, out_row, bias, row, nt * 256 + c, vec_ok, r);
+        epilogue_store16<T>(args, out_row, bias, row, nt * 256 + c, vec_ok, r, st_policy);
       }
       tc_fence_before();
       __syncwarp();
@@ -571,6 +584,7 @@ int launch_gemm(const void* x, int64_t ldx, const void* w, int64_t ldw, const vo
   a.num_n_tiles = static_cast<int>((N + BN - 1) / BN);
   a.num_tiles = a.num_m_tiles * a.num_n_tiles;
   a.group_m = 8;
+  a.l2_hints = 0;
   a.alpha = alpha;
 
   auto kernel = gemm_tc_kernel<BN, STAGES, T>;
@@ -611,6 +625,14 @@ inline bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 
 // waves of tiles on the machine.
 namespace {
 
+// Tuning knobs read from the environment (defaults are the tuned values).
+int env_int(const char* name, int fallback) {
+  const char* v = std::getenv(name);
+  if (v == nullptr || *v == '\0') return fallback;
+  const int parsed = std::atoi(v);
+  return parsed > 0 || std::strcmp(v, "0") == 0 ? parsed : fallback;
+}
+
 template <int STAGES, typename T>
 int launch_gemm_pair(const void* x, int64_t ldx, const void* w, int64_t ldw, const void* z, int64_t ldz,
                      const void* bw, int64_t ldbw, const void* bias, void* out, int64_t ldo, int64_t M, int64_t N,
@@ -646,7 +668,8 @@ int launch_gemm_pair(const void* x, int64_t ldx, const void* w, int64_t ldw, con
   a.num_m_tiles = static_cast<int>((M + 255) / 256);
   a.num_n_tiles = static_cast<int>((N + 255) / 256);
   a.num_tiles = a.num_m_tiles * a.num_n_tiles;
-  a.group_m = 8;
+  a.group_m = env_int("LORA_B200_GROUP_M", 8);
+  a.l2_hints = env_int("LORA_B200_L2_HINTS", 0);
   a.alpha = alpha;
 
   auto kernel = gemm_tc2_kernel<STAGES, T>;
