@@ -210,6 +210,10 @@ LORA_API int lora_sgmv_schedule(const int64_t* ids, const int64_t* seg_start, co
  * adapter-sorted order of lora_sgmv_sort or a rank bucket's positions);
  * NULL = identity. */
 LORA_API size_t lora_sgmv_shrink_workspace_size(int64_t T, int64_t S, int64_t z_width, int split_k);
+/* K split lora_sgmv_shrink uses when passed split_k <= 0 (size the workspace
+ * with it).  No counterpart in the reference, whose segmented shrink does not
+ * split K (segmented_branch.py:12-28). */
+LORA_API int lora_sgmv_pick_split_k(int64_t T, int64_t K, int64_t r_max);
 LORA_API int lora_sgmv_shrink(const void* x, int64_t ldx, const void* a_flat, int64_t lda,
                      const int64_t* offsets, const int64_t* ranks, int64_t n_adapters,
                      const int32_t* tiles, const int64_t* rows, void* z, int64_t ldz, int z_dtype, int64_t z_width,

@@ -37,6 +37,7 @@ constexpr int kDevErrTimeoutAccFull = 103;
 constexpr int kDevErrTimeoutAccEmpty = 104;
 constexpr int kDevErrTimeoutSplitK = 105;
 constexpr int kDevErrBadIndex = 110;
+constexpr int kDevErrSmemLayout = 120;  // a kernel's shared-memory layout exceeds its launch allocation
 
 LORA_DEVINL uint64_t globaltimer_ns() {
   uint64_t t;
@@ -110,12 +111,49 @@ LORA_DEVINL uint4 ldg_stream(const void* p) {
   return v;
 }
 
+// ------------------------------------------- cp.async + ldmatrix (register path)
+// 16-byte global -> shared copy that bypasses L1; src_bytes < 16 zero-fills
+// the rest of the destination (src_bytes = 0: a pure zero fill, src unread).
+LORA_DEVINL void cp_async16(void* smem_dst, const void* src, uint32_t src_bytes) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(
+                   static_cast<uint32_t>(__cvta_generic_to_shared(smem_dst))),
+               "l"(src), "r"(src_bytes)
+               : "memory");
+}
+LORA_DEVINL void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+LORA_DEVINL void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+// Four 8x8 16-bit matrices; lane i supplies the row address of row (i % 8)
+// of matrix (i / 8).
+LORA_DEVINL void ldmatrix_x4(uint32_t (&r)[4], uint32_t saddr) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(saddr));
+}
+LORA_DEVINL void ldmatrix_x4_trans(uint32_t (&r)[4], uint32_t saddr) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(saddr));
+}
+
+// Make this thread's generic-proxy shared-memory writes visible to the async
+// proxy (TMA, tcgen05.mma operand reads).
+LORA_DEVINL void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+
 // Programmatic dependent launch: let the next kernel in the stream start its
 // prologue, and wait for the previous kernel's results.
 LORA_DEVINL void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 LORA_DEVINL void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 
 // ------------------------------------------------------------ mbarriers
+LORA_DEVINL uint32_t dynamic_smem_bytes() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%dynamic_smem_size;" : "=r"(r));
+  return r;
+}
+
 LORA_DEVINL uint32_t smem_u32(const void* p) {
   return static_cast<uint32_t>(__cvta_generic_to_shared(p));
 }
@@ -272,6 +310,14 @@ LORA_DEVINL uint32_t mapa_shared(uint32_t smem_addr, uint32_t rank) {
   uint32_t r;
   asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_addr), "r"(rank));
   return r;
+}
+LORA_DEVINL float4 ld_dsmem_f4(uint32_t cluster_addr) {
+  float4 v;
+  asm volatile("ld.shared::cluster.v4.f32 {%0,%1,%2,%3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "r"(cluster_addr)
+               : "memory");
+  return v;
 }
 LORA_DEVINL void mbar_arrive_cluster(uint32_t cluster_addr) {
   asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");

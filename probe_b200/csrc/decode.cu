@@ -27,6 +27,7 @@
 
 #include "common.cuh"
 #include "runtime.h"
+#include "skinny.h"
 
 namespace lora {
 
@@ -328,6 +329,9 @@ extern "C" size_t lora_decode_workspace_size(int64_t M, int64_t N, int split_k) 
 extern "C" int lora_decode_pick_split_k(int64_t M, int64_t N, int64_t K) {
   const int dev = current_device();
   const int sms = dev >= 0 ? device_info(dev).num_sms : 148;
+  const int smem = dev >= 0 ? device_info(dev).smem_per_sm : 0;
+  if (M > 64 || K % 8 == 0)  // the tensor-core path (cluster split) takes aligned K and every M > 64
+    return skinny_pick_split(M, N, K, 128, sms > 0 ? sms : 148, smem > 0 ? smem : 232448);
   return decode_pick_split_k_impl(M, N, K, sms > 0 ? sms : 148);
 }
 
@@ -339,13 +343,21 @@ extern "C" int lora_decode_linear(const void* x, int64_t ldx, const void* w, int
   if (R > 0 && (z == nullptr || b == nullptr)) return LORA_ERR_ARG;
   if (dtype != LORA_BF16 && dtype != LORA_F16) return LORA_ERR_DTYPE;
   if (R > 0 && z_dtype != LORA_F32 && z_dtype != dtype) return LORA_ERR_DTYPE;
-  if (M < 0 || N < 0 || K < 0 || R < 0 || M > 64 || R > 128) return LORA_ERR_SHAPE;
+  if (M < 0 || N < 0 || K < 0 || R < 0 || M > kSkinnyMaxM || R > 128) return LORA_ERR_SHAPE;
   if (N > INT32_MAX || K > INT32_MAX || ldx < K || ldw < K || ldo < N) return LORA_ERR_SHAPE;
   if (R > 0 && (ldz < R || ldb < R)) return LORA_ERR_SHAPE;
   if (M == 0 || N == 0) return LORA_OK;
   const int dev = current_device();
   if (dev < 0 || !device_info(dev).is_sm100) return LORA_ERR_DEVICE;
   const DeviceInfo& info = device_info(dev);
+  {
+    // Tensor-core path: TMA-fed tcgen05 with the K split over a cluster (skinny_tc.cu).
+    const int rc = launch_skinny_linear(x, ldx, w, ldw, z, ldz, z_dtype == LORA_F32 ? 1 : 0, b, ldb, bias, out, ldo, M,
+                                        N, K, R, scale, dtype, split_k, info.num_sms, info.smem_per_sm,
+                                        info.err_word, stream);
+    if (rc != LORA_ERR_UNSUPPORTED) return rc;
+  }
+  if (M > 64) return LORA_ERR_SHAPE;  // the register-path kernel below covers M <= 64
   if (split_k <= 0) split_k = decode_pick_split_k_impl(M, N, K, info.num_sms);
   const int cap = decode_kslice_cap(M);
   const int64_t steps = std::max<int64_t>((K + 63) / 64, 1);

@@ -306,6 +306,29 @@ extern "C" int lora_sgmv_expand(const void* y, int64_t ldy, const void* z, int64
   const int dev = current_device();
   if (dev < 0 || !device_info(dev).is_sm100) return LORA_ERR_DEVICE;
   const DeviceInfo& info = device_info(dev);
+  if (b_sn == 1 && r_max > 0) {
+    // rank-major B: dense 64-token blocks (sgmv_block.cu)
+    SgmvExpandBlockArgs bp{};
+    bp.y = y;
+    bp.z = z;
+    bp.b = b;
+    bp.out = out;
+    bp.offsets = offsets;
+    bp.ranks = ranks;
+    bp.tiles = tiles;
+    bp.rows = rows;
+    bp.err = info.err_word;
+    bp.ldy = ldy;
+    bp.ldz = ldz;
+    bp.ldo = ldo;
+    bp.ldb = b_sj;
+    bp.T = static_cast<int>(T);
+    bp.N = static_cast<int>(N);
+    bp.R = static_cast<int>(r_max);
+    bp.scale = scale;
+    const int rc = launch_sgmv_expand_block(bp, dtype, z_dtype, stream);
+    if (rc != LORA_ERR_UNSUPPORTED) return rc;
+  }
   ExpandArgs p{};
   p.y = y;
   p.z = z;

@@ -24,14 +24,16 @@ int current_device() {
 const DeviceInfo& device_info(int dev) {
   std::call_once(g_dev_once[dev], [dev] {
     DeviceInfo& d = g_dev[dev];
-    int major = 0, minor = 0, sms = 0, optin = 0;
+    int major = 0, minor = 0, sms = 0, optin = 0, per_sm = 0;
     cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
     cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+    cudaDeviceGetAttribute(&per_sm, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev);
     d.num_sms = sms;
     d.is_sm100 = (major == 10 && minor == 0);
     d.max_smem_optin = static_cast<size_t>(optin);
+    d.smem_per_sm = per_sm;
     int* word = nullptr;
     if (cudaMalloc(&word, sizeof(int)) == cudaSuccess) {
       cudaMemset(word, 0, sizeof(int));

@@ -13,6 +13,7 @@ struct DeviceInfo {
   bool is_sm100 = false;
   int* err_word = nullptr;  // device int, first recorded error code (0 = none)
   size_t max_smem_optin = 0;
+  int smem_per_sm = 0;  // shared memory of one SM (all resident CTAs together)
 };
 
 // Current CUDA device, or -1 if none is usable.

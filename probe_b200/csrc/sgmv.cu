@@ -20,20 +20,36 @@ namespace lora {
 
 namespace {
 
+// Segment tables up to this many entries are staged in shared memory, so the
+// per-token lookups below cost no global round trips.
+constexpr int kSchedSmemSegs = 4096;
+
+// A segment boundary clamped to [-1, T+1]: comparisons against tokens in
+// [0, T) are unchanged and the value fits an int.
+__device__ __forceinline__ int clamp_start(int64_t v, int T) {
+  return v < -1 ? -1 : (v > T + 1 ? T + 1 : static_cast<int>(v));
+}
+
 // Adapter of token t, or -1 (out of range / not covered by any segment).
 struct AdapterLookup {
   const int64_t* ids;
   const int64_t* seg_start;
   const int64_t* seg_adapter;
+  const int* s_start;    // shared-memory copy of seg_start (clamped to [-1, T+1]) or NULL
+  const int* s_adapter;  // shared-memory copy of seg_adapter (-1 where out of range) or NULL
   int T, S, n_adapters;
   int* err;
+
+  __device__ int start(int s) const {
+    return s_start ? s_start[s] : clamp_start(seg_start[s], T);
+  }
 
   __device__ int find_segment(int t) const {
     // largest s with seg_start[s] <= t, s in [0, S)
     int lo = 0, hi = S - 1, ans = -1;
     while (lo <= hi) {
       const int mid = (lo + hi) >> 1;
-      if (seg_start[mid] <= t) {
+      if (start(mid) <= t) {
         ans = mid;
         lo = mid + 1;
       } else {
@@ -54,12 +70,12 @@ struct AdapterLookup {
   // seg: running segment index for monotone walks (segment mode only)
   __device__ int operator()(int t, int& seg) const {
     if (ids != nullptr) return validate(ids[t]);
-    while (seg + 1 < S && seg_start[seg + 1] <= t) ++seg;
-    if (seg < 0 || t < seg_start[seg] || t >= seg_start[seg + 1]) {
+    while (seg + 1 < S && start(seg + 1) <= t) ++seg;
+    if (seg < 0 || t < start(seg) || t >= start(seg + 1)) {
       record_error(err, kDevErrBadIndex);
       return -1;
     }
-    return validate(seg_adapter[seg]);
+    return validate(s_adapter ? s_adapter[seg] : seg_adapter[seg]);
   }
 };
 
@@ -67,8 +83,22 @@ struct AdapterLookup {
 
 __global__ void __launch_bounds__(1024) sgmv_schedule_kernel(AdapterLookup look, int32_t* tiles, int max_tiles) {
   __shared__ int scan[1024];
+  __shared__ int s_start[kSchedSmemSegs + 1];
+  __shared__ int s_adapter[kSchedSmemSegs];
   const int tid = threadIdx.x, nth = blockDim.x;
   const int T = look.T;
+  if (look.ids == nullptr && look.S <= kSchedSmemSegs) {
+    for (int i = tid; i <= look.S; i += nth) {
+      s_start[i] = clamp_start(look.seg_start[i], T);
+      if (i < look.S) {
+        const int64_t a = look.seg_adapter[i];
+        s_adapter[i] = (a < 0 || a >= look.n_adapters) ? -1 : static_cast<int>(a);
+      }
+    }
+    look.s_start = s_start;
+    look.s_adapter = s_adapter;
+  }
+  __syncthreads();
   const int chunk = (T + nth - 1) / nth;
   const int c0 = min(T, tid * chunk), c1 = min(T, c0 + chunk);
 
@@ -101,11 +131,13 @@ __global__ void __launch_bounds__(1024) sgmv_schedule_kernel(AdapterLookup look,
   int base = scan[tid] - count;
   int32_t* starts = tiles + 2;
   int32_t* adapters = tiles + 3 + max_tiles;
+  int32_t* block_first = tiles + 3 + 2 * max_tiles;
   {
     int s = seg, pv = prev;
     for (int t = c0; t < c1; ++t) {
       const int a = look(t, s);
       if ((t % kSgmvTileTokens) == 0 || a != pv) {
+        if ((t % kSgmvTileTokens) == 0) block_first[t / kSgmvTileTokens] = min(base, max_tiles);
         if (base < max_tiles) {
           starts[base] = t;
           adapters[base] = a;
@@ -121,6 +153,7 @@ __global__ void __launch_bounds__(1024) sgmv_schedule_kernel(AdapterLookup look,
     tiles[0] = n;
     tiles[1] = max_tiles;
     starts[n] = T;
+    block_first[(T + kSgmvTileTokens - 1) / kSgmvTileTokens] = n;
   }
 }
 
@@ -141,7 +174,7 @@ extern "C" int lora_sgmv_schedule(const int64_t* ids, const int64_t* seg_start, 
   if (tiles_bytes < lora_sgmv_tiles_size(T, S)) return LORA_ERR_WORKSPACE;
   const int dev = current_device();
   if (dev < 0 || !device_info(dev).is_sm100) return LORA_ERR_DEVICE;
-  AdapterLookup look{ids, seg_start, seg_adapter, static_cast<int>(T), static_cast<int>(S),
+  AdapterLookup look{ids, seg_start, seg_adapter, nullptr, nullptr, static_cast<int>(T), static_cast<int>(S),
                      static_cast<int>(std::min<int64_t>(n_adapters, INT32_MAX)), device_info(dev).err_word};
   const int64_t mt = sgmv_max_tiles(T, S);
   sgmv_schedule_kernel<<<1, 1024, 0, static_cast<cudaStream_t>(stream)>>>(look, tiles, static_cast<int>(mt));

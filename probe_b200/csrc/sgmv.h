@@ -1,11 +1,15 @@
 // Device-side tile schedule for the segmented multi-adapter kernels.
 //
 // A schedule is an int32 buffer built on the GPU by lora_sgmv_schedule:
-//   [0]                       number of tiles (set by the schedule kernel)
-//   [1]                       capacity (max_tiles, set by the host)
-//   [2 .. 3 + max_tiles)      tile start token; entry [num_tiles] == T
-//   [3 + max_tiles .. )       adapter id of each tile (-1 = skip / invalid)
-// Every tile covers <= 64 consecutive tokens that use the same adapter.
+//   [0]                              number of tiles (set by the schedule kernel)
+//   [1]                              capacity (max_tiles, set by the host)
+//   [2 .. 3 + max_tiles)             tile start token; entry [num_tiles] == T
+//   [3 + max_tiles .. 3 + 2 max_tiles)  adapter id of each tile (-1 = skip / invalid)
+//   [3 + 2 max_tiles .. + blocks + 1)   first tile of each 64-token block;
+//                                       entry [blocks] == num_tiles
+// Every tile covers <= 64 consecutive tokens that use the same adapter, and a
+// tile starts at every multiple of 64, so the tiles of block b are exactly
+// first[b] .. first[b+1].
 #pragma once
 
 #include <stdint.h>
@@ -20,13 +24,54 @@ __host__ __device__ inline int64_t sgmv_max_tiles(int64_t T, int64_t S) {
   return blocks + boundaries + 1;
 }
 
+__host__ __device__ inline int64_t sgmv_blocks(int64_t T) { return (T + kSgmvTileTokens - 1) / kSgmvTileTokens; }
+
 __host__ __device__ inline int64_t sgmv_tiles_bytes(int64_t T, int64_t S) {
   const int64_t mt = sgmv_max_tiles(T, S);
-  return (2 + (mt + 1) + mt) * static_cast<int64_t>(sizeof(int32_t));
+  return (2 + (mt + 1) + mt + (sgmv_blocks(T) + 1)) * static_cast<int64_t>(sizeof(int32_t));
 }
 
 __device__ __forceinline__ int sgmv_num_tiles(const int32_t* tiles) { return tiles[0]; }
 __device__ __forceinline__ int sgmv_tile_start(const int32_t* tiles, int i) { return tiles[2 + i]; }
 __device__ __forceinline__ int sgmv_tile_adapter(const int32_t* tiles, int i) { return tiles[3 + tiles[1] + i]; }
+__device__ __forceinline__ const int32_t* sgmv_block_first(const int32_t* tiles) { return tiles + 3 + 2 * tiles[1]; }
+
+// Block-structured kernels of sgmv_block.cu (dense 64-token blocks, cp.async
+// pipelines; the shrink's K splits are the CTAs of one thread-block cluster,
+// reduced through distributed shared memory, so it needs no workspace).  They return LORA_ERR_UNSUPPORTED when a layout or alignment
+// condition of their fast path does not hold; the caller then uses the
+// per-tile kernels.
+struct SgmvShrinkBlockArgs {
+  const void* x;
+  const void* a;
+  void* z;
+  const int64_t* offsets;
+  const int64_t* ranks;
+  const int32_t* tiles;
+  const int64_t* rows;
+  int* err;
+  int64_t ldx, lda, ldz;
+  int T, K, R, z_width, z_split, split_k, kslice;  // split_k CTAs of one cluster share a block
+  float scale;
+};
+int launch_sgmv_shrink_block(const SgmvShrinkBlockArgs& p, int dtype, int z_dtype, int num_sms, void* stream);
+int sgmv_shrink_block_split(int64_t T, int64_t K, int num_sms);
+constexpr int kSgmvMaxClusterSplit = 8;  // portable cluster size
+
+struct SgmvExpandBlockArgs {
+  const void* y;
+  const void* z;
+  const void* b;
+  void* out;
+  const int64_t* offsets;
+  const int64_t* ranks;
+  const int32_t* tiles;
+  const int64_t* rows;
+  int* err;
+  int64_t ldy, ldz, ldo, ldb;  // B element (adapter a, rank j, column n) at b[(offsets[a] + j) * ldb + n]
+  int T, N, R;
+  float scale;
+};
+int launch_sgmv_expand_block(const SgmvExpandBlockArgs& p, int dtype, int z_dtype, void* stream);
 
 }  // namespace lora

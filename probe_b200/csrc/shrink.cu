@@ -404,6 +404,13 @@ extern "C" int lora_shrink(const void* x, int64_t ldx, const void* a, int64_t ld
   return launch_shrink(p, dtype, z_dtype, aligned, grid, s);
 }
 
+extern "C" int lora_sgmv_pick_split_k(int64_t T, int64_t K, int64_t r_max) {
+  if (T <= 0 || K <= 0 || r_max <= 0) return 1;
+  const int dev = current_device();
+  const int sms = dev >= 0 ? device_info(dev).num_sms : 148;
+  return sgmv_shrink_block_split(T, K, sms > 0 ? sms : 148);
+}
+
 extern "C" size_t lora_sgmv_shrink_workspace_size(int64_t T, int64_t S, int64_t z_width, int split_k) {
   if (T <= 0 || z_width <= 0 || split_k <= 1) return 256;
   const size_t partial = static_cast<size_t>(split_k) * T * z_width * sizeof(float);
@@ -426,11 +433,44 @@ extern "C" int lora_sgmv_shrink(const void* x, int64_t ldx, const void* a_flat, 
   const int dev = current_device();
   if (dev < 0 || !device_info(dev).is_sm100) return LORA_ERR_DEVICE;
   const DeviceInfo& info = device_info(dev);
-  const int64_t blocks = (T + kSgmvTileTokens - 1) / kSgmvTileTokens;
   if (r_max == 0 || K == 0) split_k = 1;
-  if (split_k <= 0) split_k = shrink_pick_split_k_impl(blocks, K, info.num_sms);
+  if (split_k <= 0) split_k = sgmv_shrink_block_split(T, K, info.num_sms);
   const int kslice = shrink_kslice(K, split_k);
   split_k = static_cast<int>(std::max<int64_t>((K + kslice - 1) / kslice, 1));
+  if (split_k > 1) {
+    const size_t need = lora_sgmv_shrink_workspace_size(T, S, z_width, split_k);
+    if (workspace == nullptr || workspace_bytes < need || !al16(workspace)) return LORA_ERR_WORKSPACE;
+    if (sgmv_max_tiles(T, S) > kMaxCounters) return LORA_ERR_SHAPE;
+  }
+
+  // Dense 64-token blocks first (sgmv_block.cu); the per-tile kernel below
+  // covers the layouts that path does not take (unaligned rows, r_max > 128).
+  if (r_max > 0 && K > 0) {
+    SgmvShrinkBlockArgs bp{};
+    bp.x = x;
+    bp.a = a_flat;
+    bp.z = z;
+    bp.offsets = offsets;
+    bp.ranks = ranks;
+    bp.tiles = tiles;
+    bp.rows = rows;
+    bp.err = info.err_word;
+    bp.ldx = ldx;
+    bp.lda = lda;
+    bp.ldz = ldz;
+    bp.T = static_cast<int>(T);
+    bp.K = static_cast<int>(K);
+    bp.R = static_cast<int>(r_max);
+    bp.z_width = static_cast<int>(z_width);
+    bp.z_split = 0;
+    // the block path splits K over the CTAs of a cluster (at most 8)
+    bp.split_k = std::min(split_k, kSgmvMaxClusterSplit);
+    bp.kslice = shrink_kslice(K, bp.split_k);
+    bp.split_k = static_cast<int>(std::max<int64_t>((K + bp.kslice - 1) / bp.kslice, 1));
+    bp.scale = scale;
+    const int rc = launch_sgmv_shrink_block(bp, dtype, z_dtype, info.num_sms, stream);
+    if (rc != LORA_ERR_UNSUPPORTED) return rc;
+  }
 
   ShrinkArgs p{};
   p.x = x;
@@ -456,9 +496,6 @@ extern "C" int lora_sgmv_shrink(const void* x, int64_t ldx, const void* a_flat, 
   p.scale = scale;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (split_k > 1) {
-    const size_t need = lora_sgmv_shrink_workspace_size(T, S, z_width, split_k);
-    if (workspace == nullptr || workspace_bytes < need || !al16(workspace)) return LORA_ERR_WORKSPACE;
-    if (sgmv_max_tiles(T, S) > kMaxCounters) return LORA_ERR_SHAPE;
     p.counters = static_cast<int*>(workspace);
     p.partial = reinterpret_cast<float*>(static_cast<char*>(workspace) + kCounterBytes);
   }

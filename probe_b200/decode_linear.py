@@ -34,8 +34,9 @@ def build_decode_linear(weight, bias, a, b, scale=1.0, *, block_n=16, block_k=25
         if x.shape[0] == 0:
             return torch.empty((0, weight.shape[0]), device=x.device, dtype=x.dtype)
         outs = []
-        for i in range(0, x.shape[0], 64):
-            xs = x[i: i + 64]
+        step = 256 if x.shape[1] % 8 == 0 else 64
+        for i in range(0, x.shape[0], step):
+            xs = x[i: i + step]
             z = kernels.shrink(xs, a, 1.0, z_dtype=torch.float32)
             outs.append(kernels.decode_linear(xs, weight, z, b, bias, scale))
         return outs[0] if len(outs) == 1 else torch.cat(outs)

@@ -3,15 +3,16 @@
 Drop-in for ``loraforge_kernels.fused_linear`` (same names, signatures and
 error behaviour).  The implementations are this package's sm_100a kernels:
 
-``kconcat``  (default for M > 64)
+``kconcat``  (default for M > 256)
     rank shrink ``z = scale * x @ A.T`` (split-K kernel, or the tcgen05 GEMM
     for ranks above 128), then ONE tcgen05 GEMM whose mainloop runs over
     ``[x | z]`` against ``[W | B]`` -- the LoRA expand is an extra K-slice, so
     the output is written once and no concatenated copy of x or W is built.
     The reference reached the same algebra by materialising ``[x | s.z]`` and
     ``[W | B]`` for cuBLAS (fused_linear.py:622-677).
-``decode``   (default for M <= 64)
-    shrink + a W-streaming split-K GEMV with the expand as a K tail
+``decode``   (default for M <= 256; M <= 64 when K is not a multiple of 8)
+    shrink, then W streamed once through TMA into tcgen05 MMAs with the tokens
+    as the narrow operand, K split over a cluster and the expand as a K tail
     (decode_linear.py:13-100).
 ``hybrid``   tcgen05 base GEMM, shrink, expand-add epilogue (fused_linear.py:370-373).
 ``concat``   tcgen05 GEMM on ``[W; A; 0]`` then expand-add (fused_linear.py:336-367).
@@ -35,8 +36,10 @@ from .kernels import round_up
 MIN_RANK_TILE = 16
 FUSED_MAX_RANK = 64
 MIN_GEMM_ROWS = 128
-# Rows at or below which the W-streaming decode kernel is the default.
+# Rows at or below which the W-streaming decode kernel is the default: up to
+# 256 on the tensor-core path (K a multiple of 8), 64 on the register path.
 DECODE_MAX_ROWS = 64
+SKINNY_MAX_ROWS = 256
 # Ranks above this use the tensor-core GEMM for the shrink.
 SHRINK_MMA_MAX_RANK = 128
 
@@ -203,18 +206,24 @@ def _decode(x, weight, bias, a, b, scale):
     return kernels.decode_linear(x, weight, z, b, bias, scale)
 
 
+def _decode_rows(k: int) -> int:
+    """Largest token count of one decode-kernel call for inner dimension k."""
+    return SKINNY_MAX_ROWS if _gemm_aligned(k) else DECODE_MAX_ROWS
+
+
 def _base_linear(x, weight, bias):
     """``x @ W.T + bias`` with this package's kernels (the r == 0 / scale == 0 path)."""
-    if x.shape[0] <= DECODE_MAX_ROWS or not _gemm_aligned(x.shape[1]):
+    if x.shape[0] <= _decode_rows(x.shape[1]) or not _gemm_aligned(x.shape[1]):
         return _rowwise(lambda xs: kernels.decode_linear(xs, weight, None, None, bias, 0.0), x)
     return kernels.gemm(x, weight, bias=bias)
 
 
 def _rowwise(fn, x):
-    """Apply a <= 64-row kernel to any number of rows (odd-K fallback)."""
-    if x.shape[0] <= DECODE_MAX_ROWS:
+    """Apply a decode-sized kernel to any number of rows (odd-K fallback)."""
+    step = _decode_rows(x.shape[1])
+    if x.shape[0] <= step:
         return fn(x)
-    return torch.cat([fn(x[i: i + DECODE_MAX_ROWS]) for i in range(0, x.shape[0], DECODE_MAX_ROWS)])
+    return torch.cat([fn(x[i: i + step]) for i in range(0, x.shape[0], step)])
 
 
 def _gemm_aligned(k: int) -> bool:
@@ -226,7 +235,7 @@ def eligible(variant, m, k, n, r, dtype, has_augmented):
     if not _half(dtype):
         return False
     if variant == "decode":
-        return m <= DECODE_MAX_ROWS and r <= SHRINK_MMA_MAX_RANK
+        return m <= _decode_rows(k) and r <= SHRINK_MMA_MAX_RANK
     if not _gemm_aligned(k):
         return False
     if variant in ("kconcat", "fused"):
@@ -311,7 +320,7 @@ def selection_report() -> dict:
 
 
 def _default_variant(rows, k, r):
-    if rows <= DECODE_MAX_ROWS and r <= SHRINK_MMA_MAX_RANK:
+    if rows <= _decode_rows(k) and r <= SHRINK_MMA_MAX_RANK:
         return "decode"
     return "kconcat"
 
@@ -321,7 +330,8 @@ def build_plan(probe, weight, bias, a, b, scale, base_layer=None):
 
     Reference: fused_linear.py:476-524.  With ``LORAFORGE_TUNE=1`` every
     eligible variant is timed on ``probe`` (the reference's behaviour);
-    otherwise the shape rule picks decode for M <= 64 and kconcat above.
+    otherwise the shape rule picks decode for M <= 256 (64 with K not a multiple of
+    8) and kconcat above.
     ``base_layer`` is accepted for signature compatibility; no packed weight
     aliases it here because kconcat needs no packed copy of W.
     """

@@ -173,8 +173,8 @@ def decode_linear(x: torch.Tensor, w: torch.Tensor, z: torch.Tensor | None, b: t
     m, k = x.shape
     n = w.shape[0]
     r = 0 if z is None else b.shape[1]
-    if m > 64:
-        raise ValueError("decode_linear: at most 64 rows")
+    if m > 256:
+        raise ValueError("decode_linear: at most 256 rows")
     if out is None:
         out = torch.empty((m, n), device=x.device, dtype=x.dtype)
     if r > 0:
@@ -240,7 +240,7 @@ def sgmv_shrink(x: torch.Tensor, a_flat: torch.Tensor, offsets: torch.Tensor, ra
             torch.empty((x.shape[0], width), device=x.device, dtype=z_dtype)
     lib = _lib.load()
     if split_k <= 0:
-        split_k = lib.lora_shrink_pick_split_k(t, k, r_max)
+        split_k = lib.lora_sgmv_pick_split_k(t, k, r_max)
     ws = _lib.WORKSPACE.get(lib.lora_sgmv_shrink_workspace_size(t, s, width, split_k), x.device, "sgmv")
     offsets = _i64(offsets, x.device)
     ranks = _i64(ranks, x.device)

@@ -138,6 +138,30 @@ def test_decode_linear(dtype, m, k, n, r):
         assert_parity(kernels.decode_linear(x, w, zr, b, bias, -0.7), want_r, dtype)
 
 
+@pytest.mark.parametrize("m,k,n,r,split", [(65, 512, 384, 16, 0), (128, 4096, 4096, 16, 0), (200, 1024, 1000, 40, 3),
+                                           (256, 4096, 4096, 16, 2), (17, 2048, 11008, 128, 8),
+                                           (3, 320, 200, 72, 1), (256, 128, 130, 8, 0), (256, 256, 512, 0, 0),
+                                           (4, 256, 512, 0, 0), (100, 512, 640, 0, 5), (256, 256, 512, 3, 0)])
+def test_decode_linear_tensor_core_path(m, k, n, r, split):
+    """Token counts up to 256, ranks 0 and across one and two 64-wide tail chunks,
+    and clusters of 1..8 K slices (the tensor-core path of lora_decode_linear).
+    Rank 0 with 128-token tiles and a 2-deep pipeline is the layout where the
+    fp32 partial tile is larger than the operand buffers it reuses."""
+    dtype = torch.bfloat16
+    x = randn((m, k), 1.0, dtype, seed=m + 1)
+    w = randn((n, k), 1 / math.sqrt(k), dtype, seed=n + 1)
+    bias = randn((n,), 1.0, dtype, seed=7)
+    a = randn((r, k), 1 / math.sqrt(k), dtype, seed=8) if r else None
+    b = randn((n, r), 1 / math.sqrt(max(r, 1)), dtype, seed=9) if r else None
+    z = kernels.shrink(x, a, 1.0, z_dtype=torch.float32) if r else None
+    out = kernels.decode_linear(x, w, z, b, bias, 1.3, split_k=split)
+    want = orc.naive_linear(np64(x), np64(w), np64(bias), np64(a) if r else None, np64(b) if r else None, 1.3)
+    assert_parity(out, want, dtype)
+    again = kernels.decode_linear(x, w, z, b, bias, 1.3, split_k=split)
+    assert torch.equal(out, again)  # cluster reduction in rank order: deterministic
+    assert _lib.device_error() == 0
+
+
 def test_decode_zero_rank_is_base():
     x = randn((4, 1536), 1.0, seed=1)
     w = randn((512, 1536), 1 / 40, seed=2)
