@@ -164,9 +164,12 @@ LORA_API int lora_expand_add(const void* y, int64_t ldy, const void* z, int64_t 
  * Decode linear (small M): out[M,N] = x . w^T + scale * z . b^T + bias
  * Streams w once with split-K over CTAs; z ([M,R], input dtype or f32) comes
  * from lora_shrink and may be NULL when R == 0.  b is lora_B.weight [N,R].
- * scale * z is carried as a hi/lo pair of the input dtype.  M <= 64.
- * Workspace: lora_decode_workspace_size() bytes, with the same zeroed
- * counter region as lora_shrink's.
+ * scale * z is carried as a hi/lo pair of the input dtype.
+ * M <= 256 when K, ldx and ldw are multiples of 8 and x, w are 16-byte
+ * aligned (tcgen05 path: TMA-fed, K split over a thread-block cluster, no
+ * workspace used); M <= 64 otherwise (register path, split-K through the
+ * workspace).  Workspace: lora_decode_workspace_size() bytes, with the same
+ * zeroed counter region as lora_shrink's.
  * Replaces: _decode_linear_kernel / build_decode_linear / decode_lora_linear
  * (decode_linear.py:13-100).
  * ------------------------------------------------------------------------- */

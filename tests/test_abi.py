@@ -51,7 +51,7 @@ def test_argument_errors_without_gpu(lib):
     assert lib.lora_shrink(p, 8, p, 8, p, 16, _lib.LORA_F32, 8, 1, 1, 8, 4, 1.0, 1, 1, None, 0,
                            None) == _lib.LORA_ERR_ARG
     assert lib.lora_expand_add(p, 8, p, 8, 2, p, 8, 5, None, p, 8, 1, 8, 4, 1.0, 1, None) == _lib.LORA_ERR_ARG
-    assert lib.lora_decode_linear(p, 8, p, 8, None, 0, 1, None, 0, None, p, 8, 65, 8, 8, 0, 1.0, 1, 0, None, 0,
+    assert lib.lora_decode_linear(p, 8, p, 8, None, 0, 1, None, 0, None, p, 8, 257, 8, 8, 0, 1.0, 1, 0, None, 0,
                                   None) == _lib.LORA_ERR_SHAPE
 
 
