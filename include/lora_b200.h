@@ -182,6 +182,22 @@ LORA_API int lora_decode_linear(const void* x, int64_t ldx, const void* w, int64
                        size_t workspace_bytes, void* stream);
 
 /* ---------------------------------------------------------------------------
+ * Small-M LoRA linear in one kernel: out[M,N] = x . w^T + scale * (x . a^T) . b^T + bias
+ * a is lora_A.weight [R,K], b is lora_B.weight [N,R]; R == 0 (a, b NULL) gives
+ * the base linear.  The shrink is computed inside the W-streaming kernel (z
+ * never written to memory) and scale * z enters the expand as a hi/lo pair of
+ * the input dtype.  M <= 256, R <= 128; K, ldx, ldw, lda multiples of 8 and
+ * x, w, a 16-byte aligned, else LORA_ERR_UNSUPPORTED (use lora_shrink +
+ * lora_decode_linear).  No workspace.
+ * Replaces: decode_lora_linear (decode_linear.py:81-100) and the small-M
+ * fused_lora_linear (fused_linear.py:527-551) -- shrink, expand and base in
+ * one launch, where the reference re-derives x . A^T in every output tile.
+ * ------------------------------------------------------------------------- */
+LORA_API int lora_linear_small(const void* x, int64_t ldx, const void* w, int64_t ldw, const void* a, int64_t lda,
+                               const void* b, int64_t ldb, const void* bias, void* out, int64_t ldo, int64_t M,
+                               int64_t N, int64_t K, int64_t R, float scale, int dtype, void* stream);
+
+/* ---------------------------------------------------------------------------
  * Segmented multi-adapter LoRA (SGMV / BGMV).
  *
  * Adapter tables: a_flat rows (offsets[a] .. offsets[a]+ranks[a]) hold adapter

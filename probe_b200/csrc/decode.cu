@@ -329,9 +329,7 @@ extern "C" size_t lora_decode_workspace_size(int64_t M, int64_t N, int split_k) 
 extern "C" int lora_decode_pick_split_k(int64_t M, int64_t N, int64_t K) {
   const int dev = current_device();
   const int sms = dev >= 0 ? device_info(dev).num_sms : 148;
-  const int smem = dev >= 0 ? device_info(dev).smem_per_sm : 0;
-  if (M > 64 || K % 8 == 0)  // the tensor-core path (cluster split) takes aligned K and every M > 64
-    return skinny_pick_split(M, N, K, 128, sms > 0 ? sms : 148, smem > 0 ? smem : 232448);
+  if (M > 64) return 1;  // only the tensor-core path, which needs no workspace, takes M > 64
   return decode_pick_split_k_impl(M, N, K, sms > 0 ? sms : 148);
 }
 
@@ -352,8 +350,8 @@ extern "C" int lora_decode_linear(const void* x, int64_t ldx, const void* w, int
   const DeviceInfo& info = device_info(dev);
   {
     // Tensor-core path: TMA-fed tcgen05 with the K split over a cluster (skinny_tc.cu).
-    const int rc = launch_skinny_linear(x, ldx, w, ldw, z, ldz, z_dtype == LORA_F32 ? 1 : 0, b, ldb, bias, out, ldo, M,
-                                        N, K, R, scale, dtype, split_k, info.num_sms, info.smem_per_sm,
+    const int rc = launch_skinny_linear(x, ldx, w, ldw, z, ldz, z_dtype == LORA_F32 ? 1 : 0, nullptr, 0, b, ldb, bias,
+                                        out, ldo, M, N, K, R, scale, dtype, split_k, info.num_sms, info.smem_per_sm,
                                         info.err_word, stream);
     if (rc != LORA_ERR_UNSUPPORTED) return rc;
   }

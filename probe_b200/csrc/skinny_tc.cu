@@ -1,6 +1,8 @@
 // Skinny fused LoRA linear on Blackwell tensor cores (small token counts).
 //
 //   out[M,N] = x[M,K] . W[N,K]^T + scale * z[M,R] . B[N,R]^T + bias[N],  M <= 256
+//   with z = x . A^T given (lora_decode_linear) or computed in the same kernel
+//   (lora_linear_small: the fused shrink below)
 //
 // With few tokens the cost is streaming W once, so the roles of the GEMM are
 // swapped: 128 rows of W are the M=128 operand of tcgen05.mma and the tokens
@@ -14,6 +16,13 @@
 // z is ready (griddepcontrol.wait: z may come from the shrink launched just
 // before this kernel), so W streaming overlaps the shrink.
 //
+// Fused shrink: every stage also brings the k-block of lora_A (r16 rows), and
+// a second set of MMAs (A rows as the 128-row operand, the same x tile as the
+// N operand) accumulates z^T over the CTA's K slice in a second TMEM region.
+// The cluster then sums those partial z tiles through distributed shared
+// memory, and the last CTA turns z into the [hi | lo] operand of its tail --
+// one kernel for base GEMV, shrink and expand; z never leaves the chip.
+//
 // Roles (192 threads): warp 0 TMA producer, warp 1 TMEM owner and MMA issuer,
 // warps 2..5 z staging and epilogue (tcgen05.ld of their 32 TMEM lanes).
 // Every wait is bounded; a CTA whose wait runs out still reaches both cluster
@@ -21,6 +30,8 @@
 // Reference: _decode_linear_kernel / decode_lora_linear (decode_linear.py:13-100),
 // fused_lora_linear for small M (fused_linear.py:527-551).
 #include <algorithm>
+#include <cstdio>
+#include <cstdlib>
 #include <type_traits>
 
 #include "common.cuh"
@@ -37,19 +48,32 @@ constexpr int kSkThreads = 192;
 constexpr int kSkABytes = kSkBM * kSkBK * 2;  // 16 KB
 
 struct SkinnyLayout {
-  int nb, stages, rch;
-  int b_bytes, a_off, b_off, bl_off, z_off, bar_off, bytes;
-  __host__ __device__ SkinnyLayout(int nb_, int stages_, int rch_) : nb(nb_), stages(stages_), rch(rch_) {
+  int nb, stages, rch, r16, fz;
+  int b_bytes, at_bytes;                            // x tile, A tile (fused shrink) per stage
+  int at_off, a_off, b_off, bl_off, z_off, zr_off, bar_off, bytes;
+  __host__ __device__ SkinnyLayout(int nb_, int stages_, int rch_, int r16_ = 0, int fz_ = 0)
+      : nb(nb_), stages(stages_), rch(rch_), r16(r16_), fz(fz_) {
     b_bytes = nb * kSkBK * 2;
-    a_off = 0;
-    b_off = stages * kSkABytes;
-    bl_off = b_off + stages * b_bytes;             // [rch][128 x 64]: lora_B rows of the band
-    z_off = bl_off + rch * kSkABytes;              // [rch][hi, lo][nb x 64]
-    // After the mainloop the fp32 partial tile [128][nb + 4] reuses the space
-    // from offset 0; the barriers sit above whichever region is larger.
+    at_bytes = fz ? r16 * kSkBK * 2 : 0;
+    at_off = 0;                                     // [stages][r16 x 64]: lora_A rows (fused shrink)
+    a_off = at_off + stages * at_bytes;             // [stages][128 x 64]: W rows of the band
+    b_off = a_off + stages * kSkABytes;             // [stages][nb x 64]: x tokens
+    bl_off = b_off + stages * b_bytes;              // [rch][128 x 64]: lora_B rows of the band
+    // [rch][hi, lo][nb x 64]: z as the tail's operand.  Staged from global z
+    // during the mainloop, it needs its own space; built from the fused shrink
+    // after the mainloop, it reuses the (then idle) stage buffers at offset 0.
+    const int z_bytes = rch * 2 * b_bytes;
+    const bool z_alias = fz && z_bytes <= bl_off;
+    z_off = z_alias ? 0 : bl_off + rch * kSkABytes;
+    // After the mainloop (and the tail) the fp32 partial tile [128][nb + 4]
+    // reuses the space from offset 0; the z partials [r16][nb + 4] of the
+    // fused shrink, which cluster peers read while other CTAs already write
+    // their partial tiles, and the barriers sit above it.
     const int red_bytes = kSkBM * (nb + 4) * 4;
-    const int end = z_off + rch * 2 * b_bytes;
-    bar_off = ((end > red_bytes ? end : red_bytes) + 1023) & ~1023;
+    const int end = z_alias ? bl_off + rch * kSkABytes : z_off + z_bytes;
+    zr_off = ((end > red_bytes ? end : red_bytes) + 1023) & ~1023;
+    const int zr_bytes = fz ? ((r16 * (nb + 4) * 4 + 1023) & ~1023) : 0;
+    bar_off = zr_off + zr_bytes;
     bytes = bar_off + 256 + 1024;                   // barriers, tmem slot, flags + alignment slack
   }
 };
@@ -59,28 +83,32 @@ struct SkinnyLayout {
 template <int NB, typename T>
 __global__ void __launch_bounds__(kSkThreads) skinny_linear_kernel(const __grid_constant__ CUtensorMap tm_w,
                                                                    const __grid_constant__ CUtensorMap tm_x,
+                                                                   const __grid_constant__ CUtensorMap tm_a,
                                                                    const SkinnyArgs p) {
-  constexpr uint32_t kTmemCols = NB < 32 ? 32 : NB;
+  constexpr int kNbc = NB < 16 ? 16 : NB;
   constexpr uint32_t kIdesc = umma_idesc_f16(kSkBM, NB, std::is_same<T, __nv_bfloat16>::value ? 1 : 0);
   constexpr int kRS = NB + 4;  // partial-tile row stride (floats)
-  const SkinnyLayout L(NB, p.stages, p.rch);
+  const SkinnyLayout L(NB, p.stages, p.rch, p.r16, p.fuse);
+  const uint32_t tmem_cols = p.fuse ? (2 * kNbc <= 32 ? 32u : static_cast<uint32_t>(2 * kNbc))
+                                    : (kNbc <= 32 ? 32u : static_cast<uint32_t>(kNbc));
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + L.bar_off);
-  uint64_t* empty = full + 8;
-  uint64_t* acc_full = empty + 8;
-  uint64_t* z_ready = acc_full + 1;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(z_ready + 1);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
-
   // Layout check (uniform over the grid, so a failing launch returns from every
   // CTA before any cluster barrier): the aligned layout must fit the allocation.
   if (static_cast<uint32_t>(smem - smem_raw) + static_cast<uint32_t>(L.bar_off) + 160u > dynamic_smem_bytes()) {
     if (threadIdx.x == 0) record_error(p.err, kDevErrSmemLayout);
     return;
   }
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + L.bar_off);
+  uint64_t* empty = full + 8;
+  uint64_t* acc_full = empty + 8;
+  uint64_t* z_ready = acc_full + 1;
+  uint64_t* tail_full = z_ready + 1;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tail_full + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n0 = blockIdx.x * kSkBM;      // first W row (output feature)
   const int ks = blockIdx.y;              // K slice == rank in the cluster
@@ -90,6 +118,10 @@ __global__ void __launch_bounds__(kSkThreads) skinny_linear_kernel(const __grid_
   const int kb1 = min(p.num_kb, kb0 + p.kb_per);
   const bool tail = (ks == cs - 1) && p.R > 0;
   const int n_main = max(kb1 - kb0, 0);
+  // Bands start their K slice at different k-blocks, so the W requests in flight
+  // across the grid spread over many column offsets.
+  const int rot = (n_main > 0 && p.rotate) ? static_cast<int>((blockIdx.x * 5u + blockIdx.z * 3u) % n_main) : 0;
+  const int stage_tx = kSkABytes + L.b_bytes + L.at_bytes;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < L.stages; ++s) {
@@ -98,37 +130,65 @@ __global__ void __launch_bounds__(kSkThreads) skinny_linear_kernel(const __grid_
     }
     mbar_init(acc_full, 1);
     mbar_init(z_ready, 128);
+    mbar_init(tail_full, 1);
     *abort_flag = 0;
     fence_mbar_init();
   }
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&tm_w);
     tma_prefetch_desc(&tm_x);
+    if (p.fuse) tma_prefetch_desc(&tm_a);
   }
   if (warp == 1) {
-    tmem_alloc(tmem_slot, kTmemCols);
+    tmem_alloc(tmem_slot, tmem_cols);
     tmem_relinquish();
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  const uint32_t tmem_z = tmem_base + static_cast<uint32_t>(kNbc);  // fused shrink accumulator
   bool acc_ok = false;  // epilogue: the accumulator is complete
 
+  // ================================================================ phase A
   if (warp == 0) {
     // ------------------------------------------------------------ producer
     if (lane == 0) {
       int stage = 0;
       uint32_t phase = 0;
-      for (int i = 0; i < n_main; ++i) {
-        if (!mbar_wait_bounded(&empty[stage], phase ^ 1, abort_flag, p.err, kDevErrTimeoutEmpty)) break;
-        const int kb = kb0 + i;
-        mbar_arrive_expect_tx(&full[stage], kSkABytes + L.b_bytes);
-        tma_load_2d(&tm_w, smem + L.a_off + stage * kSkABytes, &full[stage], kb * kSkBK, n0);
-        tma_load_2d(&tm_x, smem + L.b_off + stage * L.b_bytes, &full[stage], kb * kSkBK, tok0);
-        if (++stage == L.stages) {
-          stage = 0;
-          phase ^= 1;
+      // Stages are filled kgroup at a time and W is fetched as br-row boxes
+      // interleaved across the group's k-blocks (defaults: one stage, one
+      // 128-row box; the interleaved forms are tuning knobs that measured
+      // slower on B200).
+      const int kg = p.kgroup, br = p.box_rows;
+      bool ok = true;
+      for (int i = 0; ok && i < n_main; i += kg) {
+        const int cnt = min(kg, n_main - i);
+        int st[8];
+        for (int j = 0; j < cnt; ++j) {
+          if (!mbar_wait_bounded(&empty[stage], phase ^ 1, abort_flag, p.err, kDevErrTimeoutEmpty)) {
+            ok = false;
+            break;
+          }
+          st[j] = stage;
+          mbar_arrive_expect_tx(&full[stage], stage_tx);
+          if (++stage == L.stages) {
+            stage = 0;
+            phase ^= 1;
+          }
+        }
+        if (!ok) break;
+        for (int r0 = 0; r0 < kSkBM; r0 += br)
+          for (int j = 0; j < cnt; ++j) {
+            const int ii = i + j;
+            const int kb = kb0 + (ii + rot < n_main ? ii + rot : ii + rot - n_main);
+            tma_load_2d(&tm_w, smem + L.a_off + st[j] * kSkABytes + r0 * 128, &full[st[j]], kb * kSkBK, n0 + r0);
+          }
+        for (int j = 0; j < cnt; ++j) {
+          const int ii = i + j;
+          const int kb = kb0 + (ii + rot < n_main ? ii + rot : ii + rot - n_main);
+          tma_load_2d(&tm_x, smem + L.b_off + st[j] * L.b_bytes, &full[st[j]], kb * kSkBK, tok0);
+          if (p.fuse) tma_load_2d(&tm_a, smem + L.at_off + st[j] * L.at_bytes, &full[st[j]], kb * kSkBK, 0);
         }
       }
     }
@@ -148,39 +208,28 @@ __global__ void __launch_bounds__(kSkThreads) skinny_linear_kernel(const __grid_
         const uint64_t adesc = umma_desc_sw128(smem_u32(smem + L.a_off + stage * kSkABytes));
         const uint64_t bdesc = umma_desc_sw128(smem_u32(smem + L.b_off + stage * L.b_bytes));
 #pragma unroll
-        for (int k = 0; k < 4; ++k) {
+        for (int k = 0; k < 4; ++k)
           tc_mma_f16(tmem_base, adesc + static_cast<uint64_t>(2 * k), bdesc + static_cast<uint64_t>(2 * k), kIdesc,
-                     accumulate);
-          accumulate = 1;
+                     (accumulate | static_cast<uint32_t>(k)) ? 1u : 0u);
+        if (p.fuse) {
+          // z^T[A rows, tokens] += A[r16 (of 128) x 64] . x[NB x 64]^T; rows >= r16 are never read back
+          const uint64_t zdesc = umma_desc_sw128(smem_u32(smem + L.at_off + stage * L.at_bytes));
+#pragma unroll
+          for (int k = 0; k < 4; ++k)
+            tc_mma_f16(tmem_z, zdesc + static_cast<uint64_t>(2 * k), bdesc + static_cast<uint64_t>(2 * k), kIdesc,
+                       (accumulate | static_cast<uint32_t>(k)) ? 1u : 0u);
         }
+        accumulate = 1;
         tc_commit(&empty[stage]);
         if (++stage == L.stages) {
           stage = 0;
           phase ^= 1;
         }
       }
-      // LoRA tail: lora_B rows of the band against [hi | lo] of scale * z
-      if (ok && tail) {
-        if (!mbar_wait_bounded(z_ready, 0, abort_flag, p.err, kDevErrTimeoutFull)) ok = false;
-        tc_fence_after();
-        for (int c = 0; ok && c < p.rch; ++c) {
-          const int nk = min(4, (p.R - c * kSkBK + 15) / 16);
-          const uint64_t adesc = umma_desc_sw128(smem_u32(smem + L.bl_off + c * kSkABytes));
-          const uint64_t hdesc = umma_desc_sw128(smem_u32(smem + L.z_off + (2 * c) * L.b_bytes));
-          const uint64_t ldesc = umma_desc_sw128(smem_u32(smem + L.z_off + (2 * c + 1) * L.b_bytes));
-          for (int k = 0; k < nk; ++k) {
-            tc_mma_f16(tmem_base, adesc + static_cast<uint64_t>(2 * k), hdesc + static_cast<uint64_t>(2 * k), kIdesc,
-                       accumulate);
-            accumulate = 1;
-            tc_mma_f16(tmem_base, adesc + static_cast<uint64_t>(2 * k), ldesc + static_cast<uint64_t>(2 * k), kIdesc,
-                       1u);
-          }
-        }
-      }
       if (ok) tc_commit(acc_full);
     }
   } else {
-    // ------------------------------------------ z staging, then the epilogue
+    // ------------------------------------------------ epilogue warps, phase A
     const int et = threadIdx.x - 64;  // 0..127
     if (tail) {
       // lora_B rows n0 .. n0+128, ranks c*64 .. c*64+64 (zero beyond N and R), SW128 K-major
@@ -208,45 +257,135 @@ __global__ void __launch_bounds__(kSkThreads) skinny_linear_kernel(const __grid_
         }
         *reinterpret_cast<uint4*>(smem + L.bl_off + c * kSkABytes + row * 128 + ((ch ^ (row & 7)) << 4)) = v.u;
       }
-      pdl_wait();  // z may be written by the kernel launched just before this one
-      // [hi | lo] of scale * z for tokens tok0 .. tok0+NB, ranks c*64 .. c*64+64, SW128 K-major
-      for (int idx = et; idx < p.rch * NB * 8; idx += 128) {
-        const int c = idx / (NB * 8);
-        const int rem = idx - c * NB * 8;
-        const int row = rem >> 3, ch = rem & 7;
-        const int t = tok0 + row;
-        float v[8];
+      if (!p.fuse) {
+        pdl_wait();  // z may be written by the kernel launched just before this one
+        // [hi | lo] of scale * z for tokens tok0 .. tok0+NB, ranks c*64 .. c*64+64, SW128 K-major
+        for (int idx = et; idx < p.rch * NB * 8; idx += 128) {
+          const int c = idx / (NB * 8);
+          const int rem = idx - c * NB * 8;
+          const int row = rem >> 3, ch = rem & 7;
+          const int t = tok0 + row;
+          float v[8];
 #pragma unroll
-        for (int e = 0; e < 8; ++e) {
-          const int j = c * kSkBK + ch * 8 + e;
-          float zv = 0.f;
-          if (t < p.M && j < p.R)
-            zv = p.z_f32 ? static_cast<const float*>(p.z)[static_cast<int64_t>(t) * p.ldz + j]
-                         : to_f32(static_cast<const T*>(p.z)[static_cast<int64_t>(t) * p.ldz + j]);
-          v[e] = p.scale * zv;
-        }
-        uint32_t hw[4], lw[4];
+          for (int e = 0; e < 8; ++e) {
+            const int j = c * kSkBK + ch * 8 + e;
+            float zv = 0.f;
+            if (t < p.M && j < p.R)
+              zv = p.z_f32 ? static_cast<const float*>(p.z)[static_cast<int64_t>(t) * p.ldz + j]
+                           : to_f32(static_cast<const T*>(p.z)[static_cast<int64_t>(t) * p.ldz + j]);
+            v[e] = p.scale * zv;
+          }
+          uint32_t hw[4], lw[4];
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const T h0 = from_f32<T>(v[2 * e]), h1 = from_f32<T>(v[2 * e + 1]);
-          hw[e] = pack2<T>(to_f32(h0), to_f32(h1));
-          lw[e] = pack2<T>(v[2 * e] - to_f32(h0), v[2 * e + 1] - to_f32(h1));
+          for (int e = 0; e < 4; ++e) {
+            const T h0 = from_f32<T>(v[2 * e]), h1 = from_f32<T>(v[2 * e + 1]);
+            hw[e] = pack2<T>(to_f32(h0), to_f32(h1));
+            lw[e] = pack2<T>(v[2 * e] - to_f32(h0), v[2 * e + 1] - to_f32(h1));
+          }
+          const uint32_t off = static_cast<uint32_t>(row * 128 + ((ch ^ (row & 7)) << 4));
+          *reinterpret_cast<uint4*>(smem + L.z_off + (2 * c) * L.b_bytes + off) =
+              make_uint4(hw[0], hw[1], hw[2], hw[3]);
+          *reinterpret_cast<uint4*>(smem + L.z_off + (2 * c + 1) * L.b_bytes + off) =
+              make_uint4(lw[0], lw[1], lw[2], lw[3]);
         }
-        const uint32_t off = static_cast<uint32_t>(row * 128 + ((ch ^ (row & 7)) << 4));
-        *reinterpret_cast<uint4*>(smem + L.z_off + (2 * c) * L.b_bytes + off) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
-        *reinterpret_cast<uint4*>(smem + L.z_off + (2 * c + 1) * L.b_bytes + off) =
-            make_uint4(lw[0], lw[1], lw[2], lw[3]);
+        fence_proxy_async_smem();  // generic-proxy writes -> visible to the tensor core
+        mbar_arrive(z_ready);
       }
-      fence_proxy_async_smem();  // generic-proxy writes -> visible to the tensor core
-      mbar_arrive(z_ready);
     }
     acc_ok = mbar_wait_bounded(acc_full, 0, abort_flag, p.err, kDevErrTimeoutAccFull);
     tc_fence_after();
+    if (p.fuse) {
+      // this CTA's partial z^T (TMEM lanes = lora_A rows) -> zred[row][token]
+      const int quad = warp & 3;
+      if (quad * 32 < p.r16) {
+        __syncwarp();
+        const int row = quad * 32 + lane;
+        float* zred = reinterpret_cast<float*>(smem + L.zr_off);
+#pragma unroll
+        for (int c = 0; c < NB; c += 16) {
+          uint32_t r[16];
+          tmem_ld_32x32b_x16(tmem_z + (static_cast<uint32_t>(quad * 32) << 16) + static_cast<uint32_t>(c), r);
+          tmem_wait_ld();
+          if (row < p.r16) {
+#pragma unroll
+            for (int i = 0; i < 16; i += 4)
+              *reinterpret_cast<float4*>(zred + row * kRS + c + i) =
+                  make_float4(__uint_as_float(r[i]), __uint_as_float(r[i + 1]), __uint_as_float(r[i + 2]),
+                              __uint_as_float(r[i + 3]));
+          }
+        }
+      }
+    }
   }
 
-  // ---- partial tile: TMEM -> registers -> shared memory at offset 0, below bar_off
-  //      (the operand buffers there are free: every TMA load was consumed by an
-  //      MMA before acc_full fired)
+  // ================================================================ phase B
+  if (p.fuse) {
+    __syncwarp();
+    cluster_sync_all();  // every CTA's partial z is in its shared memory
+  }
+  if (tail) {
+    if (p.fuse && warp >= 2) {
+      // z[t, j] = scale * sum over the cluster (rank order) -> [hi | lo] operand tiles
+      const int et = threadIdx.x - 64;
+      const uint32_t zr_addr = smem_u32(smem + L.zr_off);
+      for (int idx = et; idx < p.rch * kSkBK * (NB / 4); idx += 128) {
+        const int j = idx / (NB / 4);          // rank (0 .. rch*64)
+        const int t4 = (idx % (NB / 4)) * 4;   // first of 4 tokens
+        float4 sum = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (j < p.R) {
+          const uint32_t off = zr_addr + static_cast<uint32_t>((j * kRS + t4) * 4);
+          for (int s = 0; s < cs; ++s) {
+            const float4 v = ld_dsmem_f4(mapa_shared(off, static_cast<uint32_t>(s)));
+            sum.x += v.x;
+            sum.y += v.y;
+            sum.z += v.z;
+            sum.w += v.w;
+          }
+        }
+        const float vals[4] = {sum.x, sum.y, sum.z, sum.w};
+        const int c = j / kSkBK, jj = j % kSkBK, ch = jj >> 3, e = jj & 7;
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const int row = t4 + q;  // token row of the operand tile
+          const float v = (tok0 + row < p.M) ? p.scale * vals[q] : 0.f;
+          const T hi = from_f32<T>(v);
+          const T lo = from_f32<T>(v - to_f32(hi));
+          const uint32_t off = static_cast<uint32_t>(row * 128 + ((ch ^ (row & 7)) << 4) + e * 2);
+          *reinterpret_cast<T*>(smem + L.z_off + (2 * c) * L.b_bytes + off) = hi;
+          *reinterpret_cast<T*>(smem + L.z_off + (2 * c + 1) * L.b_bytes + off) = lo;
+        }
+      }
+      fence_proxy_async_smem();
+      mbar_arrive(z_ready);
+    }
+    if (warp == 1 && lane == 0) {
+      // LoRA tail: lora_B rows of the band against [hi | lo] of scale * z
+      bool ok = mbar_wait_bounded(z_ready, 0, abort_flag, p.err, kDevErrTimeoutFull);
+      tc_fence_after();
+      for (int c = 0; ok && c < p.rch; ++c) {
+        const int nk = min(4, (p.R - c * kSkBK + 15) / 16);
+        const uint64_t adesc = umma_desc_sw128(smem_u32(smem + L.bl_off + c * kSkABytes));
+        const uint64_t hdesc = umma_desc_sw128(smem_u32(smem + L.z_off + (2 * c) * L.b_bytes));
+        const uint64_t ldesc = umma_desc_sw128(smem_u32(smem + L.z_off + (2 * c + 1) * L.b_bytes));
+        for (int k = 0; k < nk; ++k) {
+          tc_mma_f16(tmem_base, adesc + static_cast<uint64_t>(2 * k), hdesc + static_cast<uint64_t>(2 * k), kIdesc,
+                     1u);
+          tc_mma_f16(tmem_base, adesc + static_cast<uint64_t>(2 * k), ldesc + static_cast<uint64_t>(2 * k), kIdesc,
+                     1u);
+        }
+      }
+      if (ok) tc_commit(tail_full);
+    }
+    if (warp >= 2) {
+      acc_ok = acc_ok && mbar_wait_bounded(tail_full, 0, abort_flag, p.err, kDevErrTimeoutAccFull);
+      tc_fence_after();
+    }
+  }
+
+  // ================================================================ phase C
+  // partial tile: TMEM -> registers -> shared memory at offset 0, below zr_off
+  // (the operand buffers there are free: every TMA load was consumed by an MMA
+  // before acc_full fired, and the tail's operands before tail_full)
   float* red = reinterpret_cast<float*>(smem);
   const T* bias = static_cast<const T*>(p.bias);
   T* out = static_cast<T*>(p.out);
@@ -316,7 +455,7 @@ __global__ void __launch_bounds__(kSkThreads) skinny_linear_kernel(const __grid_
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem_base, kTmemCols);
+    tmem_dealloc(tmem_base, tmem_cols);
   }
 }
 
@@ -341,27 +480,79 @@ inline bool al16(const void* ptr) { return (reinterpret_cast<uintptr_t>(ptr) & 1
 int pick_nb(int64_t M) { return M <= 16 ? 16 : (M <= 32 ? 32 : (M <= 64 ? 64 : 128)); }
 
 // CTAs of this kernel that fit one SM (shared memory bound; TMEM and threads allow more).
-int ctas_per_sm(int nb, int stages, int rch, int smem_per_sm) {
-  const SkinnyLayout L(nb, stages, rch);
-  return std::max(1, smem_per_sm / (L.bytes + 1024));
+int ctas_per_sm(const SkinnyLayout& L, int smem_per_sm) { return std::max(1, smem_per_sm / (L.bytes + 1024)); }
+
+struct SkinnyPlan {
+  int stages, split;
+};
+
+// Pipeline depth and K split chosen together.  Measured on B200 (M = 1..256,
+// W 11008 x 4096): a grid that needs a second wave costs a whole extra pass,
+// two-stage pipelines stream ~20% slower than deeper ones, and beyond three
+// stages depth no longer matters.  A plan's cost is therefore
+//   waves x ((CTAs per SM in a wave) x (K blocks per CTA + fill) / efficiency + F)
+// with F ~ 16 K-block times of prologue, reduction and epilogue per wave.
+
+// LORA_B200_SKINNY="stages,split" pins the plan (read once; for tuning sweeps).
+SkinnyPlan forced_plan() {
+  static const SkinnyPlan forced = [] {
+    SkinnyPlan f{0, 0};
+    const char* v = std::getenv("LORA_B200_SKINNY");
+    if (v != nullptr && std::sscanf(v, "%d,%d", &f.stages, &f.split) != 2) f = SkinnyPlan{0, 0};
+    return f;
+  }();
+  return forced;
 }
 
-// Deepest pipeline (2..4 stages) that still lets the most CTAs share an SM.
-int pick_stages(int nb, int rch, int smem_per_sm) {
-  int best = 2, best_ctas = ctas_per_sm(nb, 2, rch, smem_per_sm);
-  for (int st = 3; st <= 4; ++st) {
-    const int c = ctas_per_sm(nb, st, rch, smem_per_sm);
-    if (c >= std::min(best_ctas, 3)) {
-      best = st;
-      best_ctas = c;
+int tune_env(const char* name, int fallback) {
+  const char* v = std::getenv(name);
+  return (v != nullptr && v[0] >= '0' && v[0] <= '9') ? std::atoi(v) : fallback;
+}
+
+int rotate_env() {
+  static const int r = [] {
+    const char* v = std::getenv("LORA_B200_SKINNY_ROTATE");
+    return (v != nullptr && v[0] == '0') ? 0 : 1;
+  }();
+  return r;
+}
+
+SkinnyPlan plan_skinny(int nb, int rch, int r16, int fz, int64_t tiles, int64_t steps, int num_sms, int smem_per_sm,
+                       int split_req) {
+  const SkinnyPlan f = forced_plan();
+  if (f.stages >= 2 && f.split >= 1 && SkinnyLayout(nb, f.stages, rch, r16, fz).bytes <= 227 * 1024) {
+    const int s = static_cast<int>(std::min<int64_t>(std::min(f.split, kSkinnyMaxSplit), steps));
+    return SkinnyPlan{std::min(f.stages, 8), s};
+  }
+  SkinnyPlan best{2, 1};
+  double best_cost = 1e300;
+  for (int st = 2; st <= 6; ++st) {
+    const SkinnyLayout L(nb, st, rch, r16, fz);
+    if (L.bytes > 227 * 1024) break;
+    const int c = ctas_per_sm(L, smem_per_sm);
+    const int64_t slots = static_cast<int64_t>(num_sms) * c;
+    for (int s = 1; s <= kSkinnyMaxSplit && s <= steps; ++s) {
+      if (split_req > 0 && s != std::min<int64_t>(split_req, std::min<int64_t>(kSkinnyMaxSplit, steps))) continue;
+      const int64_t per = (steps + s - 1) / s;
+      if ((steps + per - 1) / per != s) continue;  // no empty slice
+      const int64_t ctas = tiles * s;
+      const int64_t waves = (ctas + slots - 1) / slots;
+      const int64_t per_sm = (std::min(ctas, slots) + num_sms - 1) / num_sms;
+      const double eff = st >= 3 ? 1.0 : 0.8;
+      const double cost = static_cast<double>(waves) * (static_cast<double>(per_sm * (per + 2)) / eff + 16.0) +
+                          0.01 * s - 0.001 * st;
+      if (cost < best_cost) {
+        best_cost = cost;
+        best = SkinnyPlan{st, s};
+      }
     }
   }
   return best;
 }
 
 template <int NB, typename T>
-int launch_nb(const CUtensorMap& tw, const CUtensorMap& tx, const SkinnyArgs& p, dim3 grid, size_t smem,
-              cudaStream_t s) {
+int launch_nb(const CUtensorMap& tw, const CUtensorMap& tx, const CUtensorMap& ta, const SkinnyArgs& p, dim3 grid,
+              size_t smem, bool pdl, cudaStream_t s) {
   auto kernel = skinny_linear_kernel<NB, T>;
   if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)) !=
       cudaSuccess)
@@ -379,18 +570,18 @@ int launch_nb(const CUtensorMap& tw, const CUtensorMap& tx, const SkinnyArgs& p,
   attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 2;
-  return cudaLaunchKernelEx(&cfg, kernel, tw, tx, p) == cudaSuccess ? LORA_OK : LORA_ERR_CUDA;
+  cfg.numAttrs = pdl ? 2 : 1;  // only the z-consuming form overlaps the kernel before it
+  return cudaLaunchKernelEx(&cfg, kernel, tw, tx, ta, p) == cudaSuccess ? LORA_OK : LORA_ERR_CUDA;
 }
 
 template <typename T>
-int launch_t(int nb, const CUtensorMap& tw, const CUtensorMap& tx, const SkinnyArgs& p, dim3 grid, size_t smem,
-             cudaStream_t s) {
+int launch_t(int nb, const CUtensorMap& tw, const CUtensorMap& tx, const CUtensorMap& ta, const SkinnyArgs& p,
+             dim3 grid, size_t smem, bool pdl, cudaStream_t s) {
   switch (nb) {
-    case 16: return launch_nb<16, T>(tw, tx, p, grid, smem, s);
-    case 32: return launch_nb<32, T>(tw, tx, p, grid, smem, s);
-    case 64: return launch_nb<64, T>(tw, tx, p, grid, smem, s);
-    case 128: return launch_nb<128, T>(tw, tx, p, grid, smem, s);
+    case 16: return launch_nb<16, T>(tw, tx, ta, p, grid, smem, pdl, s);
+    case 32: return launch_nb<32, T>(tw, tx, ta, p, grid, smem, pdl, s);
+    case 64: return launch_nb<64, T>(tw, tx, ta, p, grid, smem, pdl, s);
+    case 128: return launch_nb<128, T>(tw, tx, ta, p, grid, smem, pdl, s);
     default: return LORA_ERR_UNSUPPORTED;
   }
 }
@@ -402,46 +593,49 @@ int skinny_pick_split(int64_t M, int64_t N, int64_t K, int64_t R, int num_sms, i
   const int rch = R > 0 ? static_cast<int>((R + 63) / 64) : 0;
   const int64_t tiles = ((N + kSkBM - 1) / kSkBM) * ((M + nb - 1) / nb);
   const int64_t steps = std::max<int64_t>((K + kSkBK - 1) / kSkBK, 1);
-  const int64_t slots = static_cast<int64_t>(num_sms) * ctas_per_sm(nb, pick_stages(nb, rch, smem_per_sm), rch, smem_per_sm);
-  int best = 1;
-  double best_cost = 1e300;
-  for (int s = 1; s <= kSkinnyMaxSplit && s <= steps; ++s) {
-    const int64_t per = (steps + s - 1) / s;
-    if ((steps + per - 1) / per != s) continue;  // no empty slice
-    const int64_t waves = (tiles * s + slots - 1) / slots;
-    const double cost = static_cast<double>(waves * (per + 3)) + 0.1 * s;  // +3: pipeline fill and reduction
-    if (cost < best_cost) {
-      best_cost = cost;
-      best = s;
-    }
-  }
-  return best;
+  return plan_skinny(nb, rch, 0, 0, tiles, steps, num_sms, smem_per_sm, 0).split;
 }
 
 int launch_skinny_linear(const void* x, int64_t ldx, const void* w, int64_t ldw, const void* z, int64_t ldz,
-                         int z_f32, const void* b, int64_t ldb, const void* bias, void* out, int64_t ldo, int64_t M,
-                         int64_t N, int64_t K, int64_t R, float scale, int dtype, int split, int num_sms,
-                         int smem_per_sm, int* err, void* stream) {
+                         int z_f32, const void* a, int64_t lda, const void* b, int64_t ldb, const void* bias,
+                         void* out, int64_t ldo, int64_t M, int64_t N, int64_t K, int64_t R, float scale, int dtype,
+                         int split, int num_sms, int smem_per_sm, int* err, void* stream) {
+  const int fuse = (R > 0 && a != nullptr) ? 1 : 0;
   if (M <= 0 || M > kSkinnyMaxM || R > 128 || K <= 0) return LORA_ERR_UNSUPPORTED;
   if (K % 8 != 0 || ldx % 8 != 0 || ldw % 8 != 0 || !al16(x) || !al16(w)) return LORA_ERR_UNSUPPORTED;
+  if (fuse && (lda % 8 != 0 || !al16(a))) return LORA_ERR_UNSUPPORTED;
   const int nb = pick_nb(M);
   const int rch = R > 0 ? static_cast<int>((R + 63) / 64) : 0;
-  const int stages = pick_stages(nb, rch, smem_per_sm);
-  const SkinnyLayout L(nb, stages, rch);
-  if (L.bytes > 227 * 1024) return LORA_ERR_UNSUPPORTED;
+  const int r16 = fuse ? static_cast<int>((R + 15) / 16 * 16) : 0;
   const int num_kb = static_cast<int>((K + kSkBK - 1) / kSkBK);
-  if (split <= 0) split = skinny_pick_split(M, N, K, R, num_sms, smem_per_sm);
-  split = std::max(1, std::min(split, std::min(kSkinnyMaxSplit, num_kb)));
+  const int64_t tiles = ((N + kSkBM - 1) / kSkBM) * ((M + nb - 1) / nb);
+  const SkinnyPlan plan = plan_skinny(nb, rch, r16, fuse, tiles, num_kb, num_sms, smem_per_sm, split);
+  const int stages = plan.stages;
+  const SkinnyLayout L(nb, stages, rch, r16, fuse);
+  if (L.bytes > 227 * 1024) return LORA_ERR_UNSUPPORTED;
+  split = plan.split;
   const int kb_per = (num_kb + split - 1) / split;
   split = (num_kb + kb_per - 1) / kb_per;
 
-  CUtensorMap tw, tx;
+  // W box rows (128: one box per k-block; smaller boxes measured slower on B200)
+  const int box_rows_pre = tune_env("LORA_B200_SKINNY_BR", 128);
+  const uint32_t wbox = (box_rows_pre == 8 || box_rows_pre == 16 || box_rows_pre == 32 || box_rows_pre == 64 ||
+                         box_rows_pre == 128) ? static_cast<uint32_t>(box_rows_pre) : 128u;
+  CUtensorMap tw, tx, ta;
   if (!encode_map(&tw, w, dtype, static_cast<uint64_t>(K), static_cast<uint64_t>(N), static_cast<uint64_t>(ldw),
-                  kSkBK, kSkBM))
+                  kSkBK, wbox))
     return LORA_ERR_CUDA;
   if (!encode_map(&tx, x, dtype, static_cast<uint64_t>(K), static_cast<uint64_t>(M), static_cast<uint64_t>(ldx),
                   kSkBK, static_cast<uint32_t>(nb)))
     return LORA_ERR_CUDA;
+  if (fuse) {
+    // lora_A [R, K]: boxes of r16 rows, rows R .. r16 filled with zeros
+    if (!encode_map(&ta, a, dtype, static_cast<uint64_t>(K), static_cast<uint64_t>(R), static_cast<uint64_t>(lda),
+                    kSkBK, static_cast<uint32_t>(r16)))
+      return LORA_ERR_CUDA;
+  } else {
+    ta = tw;
+  }
   SkinnyArgs p{};
   p.out = out;
   p.bias = bias;
@@ -461,14 +655,39 @@ int launch_skinny_linear(const void* x, int64_t ldx, const void* w, int64_t ldw,
   p.split = split;
   p.stages = stages;
   p.rch = rch;
+  p.r16 = r16;
+  p.fuse = fuse;
   p.scale = scale;
+  p.rotate = rotate_env();
+  p.kgroup = std::max(1, std::min(tune_env("LORA_B200_SKINNY_KG", 1), std::min(stages, 8)));
+  p.box_rows = static_cast<int>(wbox);
   const int64_t bands = (N + kSkBM - 1) / kSkBM;
   const int64_t ttiles = (M + nb - 1) / nb;
   if (bands > INT32_MAX || ttiles > 65535) return LORA_ERR_SHAPE;
   dim3 grid(static_cast<unsigned>(bands), static_cast<unsigned>(split), static_cast<unsigned>(ttiles));
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  if (dtype == LORA_BF16) return launch_t<__nv_bfloat16>(nb, tw, tx, p, grid, L.bytes, s);
-  return launch_t<__half>(nb, tw, tx, p, grid, L.bytes, s);
+  const bool pdl = !fuse && R > 0;
+  if (dtype == LORA_BF16) return launch_t<__nv_bfloat16>(nb, tw, tx, ta, p, grid, L.bytes, pdl, s);
+  return launch_t<__half>(nb, tw, tx, ta, p, grid, L.bytes, pdl, s);
 }
 
 }  // namespace lora
+
+using namespace lora;
+
+extern "C" int lora_linear_small(const void* x, int64_t ldx, const void* w, int64_t ldw, const void* a, int64_t lda,
+                                 const void* b, int64_t ldb, const void* bias, void* out, int64_t ldo, int64_t M,
+                                 int64_t N, int64_t K, int64_t R, float scale, int dtype, void* stream) {
+  if (x == nullptr || w == nullptr || out == nullptr) return LORA_ERR_ARG;
+  if (R > 0 && (a == nullptr || b == nullptr)) return LORA_ERR_ARG;
+  if (dtype != LORA_BF16 && dtype != LORA_F16) return LORA_ERR_DTYPE;
+  if (M < 0 || N < 0 || K < 0 || R < 0 || M > kSkinnyMaxM || R > 128) return LORA_ERR_SHAPE;
+  if (N > INT32_MAX || K > INT32_MAX || ldx < K || ldw < K || ldo < N) return LORA_ERR_SHAPE;
+  if (R > 0 && (lda < K || ldb < R)) return LORA_ERR_SHAPE;
+  if (M == 0 || N == 0) return LORA_OK;
+  const int dev = current_device();
+  if (dev < 0 || !device_info(dev).is_sm100) return LORA_ERR_DEVICE;
+  const DeviceInfo& info = device_info(dev);
+  return launch_skinny_linear(x, ldx, w, ldw, nullptr, 0, 0, R > 0 ? a : nullptr, lda, b, ldb, bias, out, ldo, M, N,
+                              K, R, scale, dtype, 0, info.num_sms, info.smem_per_sm, info.err_word, stream);
+}

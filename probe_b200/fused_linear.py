@@ -201,7 +201,11 @@ def _hybrid(x, weight, bias, a, b, scale):
 
 
 def _decode(x, weight, bias, a, b, scale):
-    """Small-M path: fp32 shrink then the W-streaming decode kernel with the expand as a K tail."""
+    """Small-M path: one kernel streaming W with the shrink fused and the expand
+    as a K tail; shapes outside it take the fp32 shrink then the decode kernel."""
+    out = kernels.linear_small(x, weight, a, b, bias, scale)
+    if out is not None:
+        return out
     z = kernels.shrink(x, a, 1.0, z_dtype=torch.float32)
     return kernels.decode_linear(x, weight, z, b, bias, scale)
 

@@ -183,15 +183,47 @@ def decode_linear(x: torch.Tensor, w: torch.Tensor, z: torch.Tensor | None, b: t
     if bias is not None:
         bias = bias.contiguous()
     lib = _lib.load()
-    if split_k <= 0:
-        split_k = lib.lora_decode_pick_split_k(m, n, k)
-    ws_bytes = lib.lora_decode_workspace_size(m, n, split_k)
+    # the workspace covers the register path's split; split_k = 0 lets each path plan its own
+    ws_split = split_k if split_k > 0 else lib.lora_decode_pick_split_k(m, n, k)
+    ws_bytes = lib.lora_decode_workspace_size(m, n, ws_split)
     ws = _lib.WORKSPACE.get(ws_bytes, x.device, "decode")
     _lib.call("lora_decode_linear", _lib.ptr(x), _lib.ld(x), _lib.ptr(w), _lib.ld(w),
               _lib.ptr(z) if r > 0 else None, _lib.ld(z) if r > 0 else 0,
               _lib.dtype_code(z.dtype) if r > 0 else _dt(x), _lib.ptr(b) if r > 0 else None,
               _lib.ld(b) if r > 0 else 0, _lib.ptr(bias), _lib.ptr(out), out.stride(0), m, n, k, r, float(scale),
               _dt(x), int(split_k), _lib.ptr(ws), ws.numel(), _lib.stream_handle(x.device))
+    return out
+
+
+def linear_small(x: torch.Tensor, w: torch.Tensor, a: torch.Tensor | None, b: torch.Tensor | None,
+                 bias: torch.Tensor | None, scale: float, out: torch.Tensor | None = None) -> torch.Tensor | None:
+    """``x @ w.T + scale * (x @ a.T) @ b.T + bias`` for M <= 256 in ONE kernel (the
+    shrink fused into the W stream).  Returns None when the shape or alignment is
+    outside that kernel (then use shrink + decode_linear)."""
+    _lib.require_cuda(x, w, where="linear_small")
+    _check_half(x, "linear_small")
+    x = _lib.row_major(x)
+    w = _lib.row_major(w)
+    m, k = x.shape
+    n = w.shape[0]
+    r = 0 if a is None or scale == 0 else a.shape[0]
+    if m > 256 or r > 128:
+        return None
+    if r > 0:
+        a = _lib.row_major(a)
+        b = _lib.row_major(b)
+    if bias is not None:
+        bias = bias.contiguous()
+    if out is None:
+        out = torch.empty((m, n), device=x.device, dtype=x.dtype)
+    lib = _lib.load()
+    rc = lib.lora_linear_small(_lib.ptr(x), _lib.ld(x), _lib.ptr(w), _lib.ld(w), _lib.ptr(a) if r else None,
+                               _lib.ld(a) if r else 0, _lib.ptr(b) if r else None, _lib.ld(b) if r else 0,
+                               _lib.ptr(bias), _lib.ptr(out), out.stride(0), m, n, k, r, float(scale), _dt(x),
+                               _lib.stream_handle(x.device))
+    if rc == _lib.LORA_ERR_UNSUPPORTED:
+        return None
+    _lib.check(rc, "lora_linear_small")
     return out
 
 

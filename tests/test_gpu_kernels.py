@@ -162,6 +162,32 @@ def test_decode_linear_tensor_core_path(m, k, n, r, split):
     assert _lib.device_error() == 0
 
 
+@pytest.mark.parametrize("m,k,n,r", [(1, 4096, 11008, 16), (4, 320, 1000, 7), (16, 4096, 4096, 64), (17, 1536, 512, 65),
+                                     (64, 4096, 11008, 16), (65, 512, 384, 128), (128, 4096, 4096, 16),
+                                     (200, 1024, 1000, 40), (256, 4096, 4096, 16), (3, 64, 96, 1), (33, 256, 130, 0)])
+def test_linear_small_fused_shrink(m, k, n, r):
+    """One kernel: W streamed once, x . A^T accumulated beside it and reduced over
+    the cluster, the expand as the last slice's tail (lora_linear_small)."""
+    dtype = torch.bfloat16
+    x = randn((m, k), 1.0, dtype, seed=m + 3)
+    w = randn((n, k), 1 / math.sqrt(k), dtype, seed=n + 3)
+    bias = randn((n,), 1.0, dtype, seed=11)
+    a = randn((r, k), 1 / math.sqrt(k), dtype, seed=12) if r else None
+    b = randn((n, r), 1 / math.sqrt(max(r, 1)), dtype, seed=13) if r else None
+    out = kernels.linear_small(x, w, a, b, bias, 0.9)
+    assert out is not None
+    want = orc.naive_linear(np64(x), np64(w), np64(bias), np64(a) if r else None, np64(b) if r else None, 0.9)
+    assert_parity(out, want, dtype)
+    assert torch.equal(out, kernels.linear_small(x, w, a, b, bias, 0.9))
+    assert _lib.device_error() == 0
+
+
+def test_linear_small_declines_unaligned():
+    x = randn((4, 257), 1.0, seed=1)
+    w = randn((64, 257), 0.05, seed=2)
+    assert kernels.linear_small(x, w, None, None, None, 0.0) is None
+
+
 def test_decode_zero_rank_is_base():
     x = randn((4, 1536), 1.0, seed=1)
     w = randn((512, 1536), 1 / 40, seed=2)
