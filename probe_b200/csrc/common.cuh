@@ -322,6 +322,20 @@ LORA_DEVINL float4 ld_dsmem_f4(uint32_t cluster_addr) {
 LORA_DEVINL void mbar_arrive_cluster(uint32_t cluster_addr) {
   asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
 }
+// Bulk copy of `bytes` (multiple of 16) from this CTA's shared memory into the
+// shared memory of a CTA of the cluster; the bytes complete on the mbarrier at
+// `bar_cluster_addr` in that CTA.  Shared-to-shared push, no multicast.
+LORA_DEVINL void bulk_push_to_peer(uint32_t dst_cluster_addr, const void* src_smem, uint32_t bytes,
+                                   uint32_t bar_cluster_addr) {
+  asm volatile("cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   dst_cluster_addr),
+               "r"(smem_u32(src_smem)), "r"(bytes), "r"(bar_cluster_addr)
+               : "memory");
+}
+// Named barrier over `count` threads (a multiple of 32), id 1..15.
+LORA_DEVINL void named_bar_sync(int id, int count) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
+}
 // TMA tile load into this CTA's shared memory whose transaction bytes are
 // counted on the mbarrier at `bar_cluster_addr` (the leader's barrier).
 LORA_DEVINL void tma_load_2d_pair(const CUtensorMap* map, void* smem_dst, uint32_t bar_cluster_addr, int32_t c0,

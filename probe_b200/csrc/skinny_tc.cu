@@ -48,11 +48,12 @@ constexpr int kSkThreads = 192;
 constexpr int kSkABytes = kSkBM * kSkBK * 2;  // 16 KB
 
 struct SkinnyLayout {
-  int nb, stages, rch, r16, fz;
+  int nb, stages, rch, r16, fz, cs;
   int b_bytes, at_bytes;                            // x tile, A tile (fused shrink) per stage
-  int at_off, a_off, b_off, bl_off, z_off, zr_off, bar_off, bytes;
-  __host__ __device__ SkinnyLayout(int nb_, int stages_, int rch_, int r16_ = 0, int fz_ = 0)
-      : nb(nb_), stages(stages_), rch(rch_), r16(r16_), fz(fz_) {
+  int rpr, slice_bytes, zpush_bytes;                // rows per owner, partial slice pushed to an owner, z partial
+  int at_off, a_off, b_off, bl_off, z_off, rst_off, zr_off, zst_off, bar_off, bytes;
+  __host__ __device__ SkinnyLayout(int nb_, int stages_, int rch_, int r16_ = 0, int fz_ = 0, int cs_ = 1)
+      : nb(nb_), stages(stages_), rch(rch_), r16(r16_), fz(fz_), cs(cs_) {
     b_bytes = nb * kSkBK * 2;
     at_bytes = fz ? r16 * kSkBK * 2 : 0;
     at_off = 0;                                     // [stages][r16 x 64]: lora_A rows (fused shrink)
@@ -65,15 +66,26 @@ struct SkinnyLayout {
     const int z_bytes = rch * 2 * b_bytes;
     const bool z_alias = fz && z_bytes <= bl_off;
     z_off = z_alias ? 0 : bl_off + rch * kSkABytes;
-    // After the mainloop (and the tail) the fp32 partial tile [128][nb + 4]
-    // reuses the space from offset 0; the z partials [r16][nb + 4] of the
-    // fused shrink, which cluster peers read while other CTAs already write
-    // their partial tiles, and the barriers sit above it.
+    const int end_a = z_alias ? bl_off + rch * kSkABytes : z_off + z_bytes;  // in use during the mainloop
+    // After the mainloop and the tail, every CTA writes its fp32 partial tile
+    // [128][nb + 4] at offset 0 and pushes row slices to their owners, which
+    // receive them in rst: (cs - 1) slices of rpr rows, above the tile.
     const int red_bytes = kSkBM * (nb + 4) * 4;
-    const int end = z_alias ? bl_off + rch * kSkABytes : z_off + z_bytes;
-    zr_off = ((end > red_bytes ? end : red_bytes) + 1023) & ~1023;
-    const int zr_bytes = fz ? ((r16 * (nb + 4) * 4 + 1023) & ~1023) : 0;
-    bar_off = zr_off + zr_bytes;
+    rpr = ((kSkBM + cs - 1) / cs + 7) & ~7;  // multiple of 8: 16-byte output stores
+    slice_bytes = rpr * (nb + 4) * 4;
+    rst_off = (red_bytes + 1023) & ~1023;
+    const int rst_end = rst_off + (cs - 1) * slice_bytes;
+    // Fused shrink: this CTA's z partial (zr) and, in the last CTA, the other
+    // CTAs' z partials pushed to it (zst) -- written while mainloops still run,
+    // so above everything the mainloop uses.  [r16][nb + 4] (lora_A rows as the
+    // MMA's M), or [128][r16 + 4] with 128-token tiles.
+    const int zr_floats = nb == 128 ? kSkBM * (r16 + 4) : r16 * (nb + 4);
+    zpush_bytes = fz ? zr_floats * 4 : 0;
+    const int zr_bytes = fz ? ((zpush_bytes + 1023) & ~1023) : 0;
+    int top = end_a > rst_end ? end_a : rst_end;
+    zr_off = (top + 1023) & ~1023;
+    zst_off = zr_off + zr_bytes;
+    bar_off = zst_off + (fz ? (cs - 1) * zr_bytes : 0);
     bytes = bar_off + 256 + 1024;                   // barriers, tmem slot, flags + alignment slack
   }
 };
@@ -81,14 +93,19 @@ struct SkinnyLayout {
 }  // namespace
 
 template <int NB, typename T>
-__global__ void __launch_bounds__(kSkThreads) skinny_linear_kernel(const __grid_constant__ CUtensorMap tm_w,
+__global__ void __launch_bounds__(kSkThreads, 1) skinny_linear_kernel(const __grid_constant__ CUtensorMap tm_w,
                                                                    const __grid_constant__ CUtensorMap tm_x,
                                                                    const __grid_constant__ CUtensorMap tm_a,
                                                                    const SkinnyArgs p) {
   constexpr int kNbc = NB < 16 ? 16 : NB;
   constexpr uint32_t kIdesc = umma_idesc_f16(kSkBM, NB, std::is_same<T, __nv_bfloat16>::value ? 1 : 0);
   constexpr int kRS = NB + 4;  // partial-tile row stride (floats)
-  const SkinnyLayout L(NB, p.stages, p.rch, p.r16, p.fuse);
+  // Fused shrink with 128-token tiles: tokens are the MMA's 128 rows and the
+  // r16 lora_A rows its N (8x less tensor work than padding A to 128 rows).
+  constexpr bool kZSwap = (NB == 128);
+  const SkinnyLayout L(NB, p.stages, p.rch, p.r16, p.fuse, p.split);
+  const uint32_t kIdescZ = umma_idesc_f16(kSkBM, p.r16 > 0 ? p.r16 : 16, std::is_same<T, __nv_bfloat16>::value ? 1 : 0);
+  const int zrs = kZSwap ? p.r16 + 4 : NB + 4;  // z-partial row stride (floats)
   const uint32_t tmem_cols = p.fuse ? (2 * kNbc <= 32 ? 32u : static_cast<uint32_t>(2 * kNbc))
                                     : (kNbc <= 32 ? 32u : static_cast<uint32_t>(kNbc));
 
@@ -106,7 +123,9 @@ __global__ void __launch_bounds__(kSkThreads) skinny_linear_kernel(const __grid_
   uint64_t* acc_full = empty + 8;
   uint64_t* z_ready = acc_full + 1;
   uint64_t* tail_full = z_ready + 1;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tail_full + 1);
+  uint64_t* zpull = tail_full + 1;  // last CTA: the other CTAs' z partials have arrived
+  uint64_t* rpull = zpull + 1;      // every CTA: the other CTAs' slices of its rows have arrived
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(rpull + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -131,8 +150,17 @@ __global__ void __launch_bounds__(kSkThreads) skinny_linear_kernel(const __grid_
     mbar_init(acc_full, 1);
     mbar_init(z_ready, 128);
     mbar_init(tail_full, 1);
+    mbar_init(zpull, 1);
+    mbar_init(rpull, 1);
     *abort_flag = 0;
     fence_mbar_init();
+    // Arm the receive barriers now: peers' bulk pushes may complete their bytes
+    // before this CTA reaches its wait.
+    if (cs > 1) {
+      if (p.fuse && tail) mbar_arrive_expect_tx(zpull, static_cast<uint32_t>((cs - 1) * L.zpush_bytes));
+      const int my_rows = min(kSkBM, (ks + 1) * L.rpr) - min(kSkBM, ks * L.rpr);
+      mbar_arrive_expect_tx(rpull, static_cast<uint32_t>((cs - 1) * my_rows * kRS * 4));
+    }
   }
   if (warp == 0 && lane == 0) {
     tma_prefetch_desc(&tm_w);
@@ -146,6 +174,7 @@ __global__ void __launch_bounds__(kSkThreads) skinny_linear_kernel(const __grid_
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
+  if (cs > 1) cluster_sync_all();  // every CTA's receive barriers exist before any push
   const uint32_t tmem_base = *tmem_slot;
   const uint32_t tmem_z = tmem_base + static_cast<uint32_t>(kNbc);  // fused shrink accumulator
   bool acc_ok = false;  // epilogue: the accumulator is complete
@@ -164,13 +193,12 @@ __global__ void __launch_bounds__(kSkThreads) skinny_linear_kernel(const __grid_
       bool ok = true;
       for (int i = 0; ok && i < n_main; i += kg) {
         const int cnt = min(kg, n_main - i);
-        int st[8];
+        const int st0 = stage;  // the group fills stages st0, st0+1, ... (mod stages)
         for (int j = 0; j < cnt; ++j) {
           if (!mbar_wait_bounded(&empty[stage], phase ^ 1, abort_flag, p.err, kDevErrTimeoutEmpty)) {
             ok = false;
             break;
           }
-          st[j] = stage;
           mbar_arrive_expect_tx(&full[stage], stage_tx);
           if (++stage == L.stages) {
             stage = 0;
@@ -180,15 +208,17 @@ __global__ void __launch_bounds__(kSkThreads) skinny_linear_kernel(const __grid_
         if (!ok) break;
         for (int r0 = 0; r0 < kSkBM; r0 += br)
           for (int j = 0; j < cnt; ++j) {
+            const int sj = (st0 + j) % L.stages;
             const int ii = i + j;
             const int kb = kb0 + (ii + rot < n_main ? ii + rot : ii + rot - n_main);
-            tma_load_2d(&tm_w, smem + L.a_off + st[j] * kSkABytes + r0 * 128, &full[st[j]], kb * kSkBK, n0 + r0);
+            tma_load_2d(&tm_w, smem + L.a_off + sj * kSkABytes + r0 * 128, &full[sj], kb * kSkBK, n0 + r0);
           }
         for (int j = 0; j < cnt; ++j) {
+          const int sj = (st0 + j) % L.stages;
           const int ii = i + j;
           const int kb = kb0 + (ii + rot < n_main ? ii + rot : ii + rot - n_main);
-          tma_load_2d(&tm_x, smem + L.b_off + st[j] * L.b_bytes, &full[st[j]], kb * kSkBK, tok0);
-          if (p.fuse) tma_load_2d(&tm_a, smem + L.at_off + st[j] * L.at_bytes, &full[st[j]], kb * kSkBK, 0);
+          tma_load_2d(&tm_x, smem + L.b_off + sj * L.b_bytes, &full[sj], kb * kSkBK, tok0);
+          if (p.fuse) tma_load_2d(&tm_a, smem + L.at_off + sj * L.at_bytes, &full[sj], kb * kSkBK, 0);
         }
       }
     }
@@ -212,12 +242,20 @@ __global__ void __launch_bounds__(kSkThreads) skinny_linear_kernel(const __grid_
           tc_mma_f16(tmem_base, adesc + static_cast<uint64_t>(2 * k), bdesc + static_cast<uint64_t>(2 * k), kIdesc,
                      (accumulate | static_cast<uint32_t>(k)) ? 1u : 0u);
         if (p.fuse) {
-          // z^T[A rows, tokens] += A[r16 (of 128) x 64] . x[NB x 64]^T; rows >= r16 are never read back
           const uint64_t zdesc = umma_desc_sw128(smem_u32(smem + L.at_off + stage * L.at_bytes));
+          if (kZSwap) {
+            // z[tokens, r16] += x[128 x 64] . A[r16 x 64]^T
 #pragma unroll
-          for (int k = 0; k < 4; ++k)
-            tc_mma_f16(tmem_z, zdesc + static_cast<uint64_t>(2 * k), bdesc + static_cast<uint64_t>(2 * k), kIdesc,
-                       (accumulate | static_cast<uint32_t>(k)) ? 1u : 0u);
+            for (int k = 0; k < 4; ++k)
+              tc_mma_f16(tmem_z, bdesc + static_cast<uint64_t>(2 * k), zdesc + static_cast<uint64_t>(2 * k), kIdescZ,
+                         (accumulate | static_cast<uint32_t>(k)) ? 1u : 0u);
+          } else {
+            // z^T[A rows, tokens] += A[r16 (of 128) x 64] . x[NB x 64]^T; rows >= r16 are never read back
+#pragma unroll
+            for (int k = 0; k < 4; ++k)
+              tc_mma_f16(tmem_z, zdesc + static_cast<uint64_t>(2 * k), bdesc + static_cast<uint64_t>(2 * k), kIdesc,
+                         (accumulate | static_cast<uint32_t>(k)) ? 1u : 0u);
+          }
         }
         accumulate = 1;
         tc_commit(&empty[stage]);
@@ -232,31 +270,45 @@ __global__ void __launch_bounds__(kSkThreads) skinny_linear_kernel(const __grid_
     // ------------------------------------------------ epilogue warps, phase A
     const int et = threadIdx.x - 64;  // 0..127
     if (tail) {
-      // lora_B rows n0 .. n0+128, ranks c*64 .. c*64+64 (zero beyond N and R), SW128 K-major
+      // lora_B rows n0 .. n0+128, ranks c*64 .. c*64+64 (zero beyond N and R), SW128 K-major.
+      // 16-byte rows: every chunk is one cp.async (zero-filled past R), all in
+      // flight together; other row pitches take element loads.
       const T* bsrc = static_cast<const T*>(p.b);
-      for (int idx = et; idx < p.rch * kSkBM * 8; idx += 128) {
-        const int c = idx / (kSkBM * 8);
-        const int rem = idx - c * kSkBM * 8;
-        const int row = rem >> 3, ch = rem & 7;
-        const int n = n0 + row;
-        const int j0 = c * kSkBK + ch * 8;
-        union {
-          uint4 u;
-          T e[8];
-        } v;
-        v.u = make_uint4(0u, 0u, 0u, 0u);
-        if (n < p.N && j0 < p.R) {
-          const T* src = bsrc + static_cast<int64_t>(n) * p.ldb + j0;
-          if (p.b_vec && j0 + 8 <= p.R) {
-            v.u = *reinterpret_cast<const uint4*>(src);
-          } else {
+      if (p.b_vec) {
+        for (int idx = et; idx < p.rch * kSkBM * 8; idx += 128) {
+          const int c = idx / (kSkBM * 8);
+          const int rem = idx - c * kSkBM * 8;
+          const int row = rem >> 3, ch = rem & 7;
+          const int n = n0 + row;
+          const int j0 = c * kSkBK + ch * 8;
+          const int nbytes = (n < p.N && j0 < p.R) ? 2 * min(8, p.R - j0) : 0;
+          cp_async16(smem + L.bl_off + c * kSkABytes + row * 128 + ((ch ^ (row & 7)) << 4),
+                     nbytes ? bsrc + static_cast<int64_t>(n) * p.ldb + j0 : bsrc, static_cast<uint32_t>(nbytes));
+        }
+        cp_async_commit();
+        cp_async_wait<0>();
+      } else {
+        for (int idx = et; idx < p.rch * kSkBM * 8; idx += 128) {
+          const int c = idx / (kSkBM * 8);
+          const int rem = idx - c * kSkBM * 8;
+          const int row = rem >> 3, ch = rem & 7;
+          const int n = n0 + row;
+          const int j0 = c * kSkBK + ch * 8;
+          union {
+            uint4 u;
+            T e[8];
+          } v;
+          v.u = make_uint4(0u, 0u, 0u, 0u);
+          if (n < p.N && j0 < p.R) {
+            const T* src = bsrc + static_cast<int64_t>(n) * p.ldb + j0;
 #pragma unroll
             for (int e = 0; e < 8; ++e)
               if (j0 + e < p.R) v.e[e] = src[e];
           }
+          *reinterpret_cast<uint4*>(smem + L.bl_off + c * kSkABytes + row * 128 + ((ch ^ (row & 7)) << 4)) = v.u;
         }
-        *reinterpret_cast<uint4*>(smem + L.bl_off + c * kSkABytes + row * 128 + ((ch ^ (row & 7)) << 4)) = v.u;
       }
+      if (p.fuse) fence_proxy_async_smem();  // the z path below fences once for both
       if (!p.fuse) {
         pdl_wait();  // z may be written by the kernel launched just before this one
         // [hi | lo] of scale * z for tokens tok0 .. tok0+NB, ranks c*64 .. c*64+64, SW128 K-major
@@ -295,12 +347,26 @@ __global__ void __launch_bounds__(kSkThreads) skinny_linear_kernel(const __grid_
     acc_ok = mbar_wait_bounded(acc_full, 0, abort_flag, p.err, kDevErrTimeoutAccFull);
     tc_fence_after();
     if (p.fuse) {
-      // this CTA's partial z^T (TMEM lanes = lora_A rows) -> zred[row][token]
       const int quad = warp & 3;
-      if (quad * 32 < p.r16) {
+      float* zred = reinterpret_cast<float*>(smem + L.zr_off);
+      if (kZSwap) {
+        // this CTA's partial z (TMEM lanes = tokens) -> zred[token][rank]
         __syncwarp();
         const int row = quad * 32 + lane;
-        float* zred = reinterpret_cast<float*>(smem + L.zr_off);
+        for (int c = 0; c < p.r16; c += 16) {
+          uint32_t r[16];
+          tmem_ld_32x32b_x16(tmem_z + (static_cast<uint32_t>(quad * 32) << 16) + static_cast<uint32_t>(c), r);
+          tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 16; i += 4)
+            *reinterpret_cast<float4*>(zred + row * zrs + c + i) =
+                make_float4(__uint_as_float(r[i]), __uint_as_float(r[i + 1]), __uint_as_float(r[i + 2]),
+                            __uint_as_float(r[i + 3]));
+        }
+      } else if (quad * 32 < p.r16) {
+        // this CTA's partial z^T (TMEM lanes = lora_A rows) -> zred[rank][token]
+        __syncwarp();
+        const int row = quad * 32 + lane;
 #pragma unroll
         for (int c = 0; c < NB; c += 16) {
           uint32_t r[16];
@@ -309,50 +375,95 @@ __global__ void __launch_bounds__(kSkThreads) skinny_linear_kernel(const __grid_
           if (row < p.r16) {
 #pragma unroll
             for (int i = 0; i < 16; i += 4)
-              *reinterpret_cast<float4*>(zred + row * kRS + c + i) =
+              *reinterpret_cast<float4*>(zred + row * zrs + c + i) =
                   make_float4(__uint_as_float(r[i]), __uint_as_float(r[i + 1]), __uint_as_float(r[i + 2]),
                               __uint_as_float(r[i + 3]));
           }
+        }
+      }
+      if (cs > 1 && !tail) {
+        // push this CTA's z partial into the last CTA's slot [ks]
+        fence_proxy_async_smem();
+        named_bar_sync(1, 128);
+        if (threadIdx.x == 64) {
+          const uint32_t last = static_cast<uint32_t>(cs - 1);
+          const uint32_t zr_bytes = static_cast<uint32_t>((L.zpush_bytes + 1023) & ~1023);
+          bulk_push_to_peer(mapa_shared(smem_u32(smem + L.zst_off) + static_cast<uint32_t>(ks) * zr_bytes, last),
+                            smem + L.zr_off, static_cast<uint32_t>(L.zpush_bytes), mapa_shared(smem_u32(zpull), last));
         }
       }
     }
   }
 
   // ================================================================ phase B
-  if (p.fuse) {
-    __syncwarp();
-    cluster_sync_all();  // every CTA's partial z is in its shared memory
-  }
   if (tail) {
     if (p.fuse && warp >= 2) {
-      // z[t, j] = scale * sum over the cluster (rank order) -> [hi | lo] operand tiles
+      // z[t, j] = scale * sum over the cluster (rank order) -> [hi | lo] operand tiles;
+      // the other CTAs' partials were pushed into zst, slot s = rank s
       const int et = threadIdx.x - 64;
-      const uint32_t zr_addr = smem_u32(smem + L.zr_off);
-      for (int idx = et; idx < p.rch * kSkBK * (NB / 4); idx += 128) {
-        const int j = idx / (NB / 4);          // rank (0 .. rch*64)
-        const int t4 = (idx % (NB / 4)) * 4;   // first of 4 tokens
-        float4 sum = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (j < p.R) {
-          const uint32_t off = zr_addr + static_cast<uint32_t>((j * kRS + t4) * 4);
-          for (int s = 0; s < cs; ++s) {
-            const float4 v = ld_dsmem_f4(mapa_shared(off, static_cast<uint32_t>(s)));
-            sum.x += v.x;
-            sum.y += v.y;
-            sum.z += v.z;
-            sum.w += v.w;
-          }
+      if (cs > 1) acc_ok = mbar_wait_bounded(zpull, 0, abort_flag, p.err, kDevErrTimeoutFull) && acc_ok;
+      const float* zown = reinterpret_cast<const float*>(smem + L.zr_off);
+      const float* zst = reinterpret_cast<const float*>(smem + L.zst_off);
+      const int zslot = ((L.zpush_bytes + 1023) & ~1023) / 4;  // floats per slot
+      auto zsum4 = [&](int off) {
+        float4 sm = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int s = 0; s < cs; ++s) {
+          const float4 v = *reinterpret_cast<const float4*>((s == cs - 1 ? zown : zst + s * zslot) + off);
+          sm.x += v.x;
+          sm.y += v.y;
+          sm.z += v.z;
+          sm.w += v.w;
         }
-        const float vals[4] = {sum.x, sum.y, sum.z, sum.w};
-        const int c = j / kSkBK, jj = j % kSkBK, ch = jj >> 3, e = jj & 7;
+        return sm;
+      };
+      if (kZSwap) {
+        // one item = token t, 8 ranks (one 16-byte chunk of the hi and of the lo tile)
+        const int items = NB * p.rch * 8;
+        for (int idx = et; idx < items; idx += 128) {
+          const int t = idx / (p.rch * 8);
+          const int j8 = (idx % (p.rch * 8)) * 8;  // first of 8 ranks
+          float v[8];
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          const int row = t4 + q;  // token row of the operand tile
-          const float v = (tok0 + row < p.M) ? p.scale * vals[q] : 0.f;
-          const T hi = from_f32<T>(v);
-          const T lo = from_f32<T>(v - to_f32(hi));
-          const uint32_t off = static_cast<uint32_t>(row * 128 + ((ch ^ (row & 7)) << 4) + e * 2);
-          *reinterpret_cast<T*>(smem + L.z_off + (2 * c) * L.b_bytes + off) = hi;
-          *reinterpret_cast<T*>(smem + L.z_off + (2 * c + 1) * L.b_bytes + off) = lo;
+          for (int e = 0; e < 8; ++e) v[e] = 0.f;
+          if (j8 < p.R && tok0 + t < p.M) {
+            const float4 a0 = zsum4(t * zrs + j8), a1 = zsum4(t * zrs + j8 + 4);
+            v[0] = a0.x; v[1] = a0.y; v[2] = a0.z; v[3] = a0.w;
+            v[4] = a1.x; v[5] = a1.y; v[6] = a1.z; v[7] = a1.w;
+          }
+          uint32_t hw[4], lw[4];
+#pragma unroll
+          for (int e = 0; e < 8; ++e) v[e] = (j8 + e < p.R) ? p.scale * v[e] : 0.f;
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const T h0 = from_f32<T>(v[2 * e]), h1 = from_f32<T>(v[2 * e + 1]);
+            hw[e] = pack2<T>(to_f32(h0), to_f32(h1));
+            lw[e] = pack2<T>(v[2 * e] - to_f32(h0), v[2 * e + 1] - to_f32(h1));
+          }
+          const int c = j8 / kSkBK, ch = (j8 % kSkBK) >> 3;
+          const uint32_t off = static_cast<uint32_t>(t * 128 + ((ch ^ (t & 7)) << 4));
+          *reinterpret_cast<uint4*>(smem + L.z_off + (2 * c) * L.b_bytes + off) = make_uint4(hw[0], hw[1], hw[2], hw[3]);
+          *reinterpret_cast<uint4*>(smem + L.z_off + (2 * c + 1) * L.b_bytes + off) =
+              make_uint4(lw[0], lw[1], lw[2], lw[3]);
+        }
+      } else {
+        const int items = p.rch * kSkBK * (NB / 4);
+        for (int idx = et; idx < items; idx += 128) {
+          const int j = idx / (NB / 4);          // rank (0 .. rch*64)
+          const int t4 = (idx % (NB / 4)) * 4;   // first of 4 tokens
+          float4 sum = make_float4(0.f, 0.f, 0.f, 0.f);
+          if (j < p.R) sum = zsum4(j * zrs + t4);
+          const float vals[4] = {sum.x, sum.y, sum.z, sum.w};
+          const int c = j / kSkBK, jj = j % kSkBK, ch = jj >> 3, e = jj & 7;
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const int row = t4 + q;  // token row of the operand tile
+            const float v = (tok0 + row < p.M) ? p.scale * vals[q] : 0.f;
+            const T hi = from_f32<T>(v);
+            const T lo = from_f32<T>(v - to_f32(hi));
+            const uint32_t off = static_cast<uint32_t>(row * 128 + ((ch ^ (row & 7)) << 4) + e * 2);
+            *reinterpret_cast<T*>(smem + L.z_off + (2 * c) * L.b_bytes + off) = hi;
+            *reinterpret_cast<T*>(smem + L.z_off + (2 * c + 1) * L.b_bytes + off) = lo;
+          }
         }
       }
       fence_proxy_async_smem();
@@ -417,38 +528,59 @@ __global__ void __launch_bounds__(kSkThreads) skinny_linear_kernel(const __grid_
                           __uint_as_float(r[i + 3]));
       }
     }
+    if (cs > 1) fence_proxy_async_smem();  // the partial tile is read by bulk copies below
   }
   if (cs > 1) {
     __syncwarp();
-    cluster_sync_all();  // every partial tile of the cluster is in shared memory
-    // rows [ks*rpr, ...) of the band: sum the cluster's partials in rank order
-    const int rpr = (kSkBM + cs - 1) / cs;
-    const int r0 = ks * rpr, r1 = min(kSkBM, r0 + rpr);
-    const uint32_t red_addr = smem_u32(red);
-    for (int idx = threadIdx.x; idx < (r1 - r0) * (NB / 4); idx += kSkThreads) {
-      const int c4 = (idx / (r1 - r0)) * 4;
-      const int row = r0 + idx % (r1 - r0);
-      const int n = n0 + row;
-      if (n >= p.N || tok0 + c4 >= p.M) continue;
-      float4 sum = make_float4(0.f, 0.f, 0.f, 0.f);
-      const uint32_t off = red_addr + static_cast<uint32_t>((row * kRS + c4) * 4);
-      for (int s = 0; s < cs; ++s) {
-        const float4 v = ld_dsmem_f4(mapa_shared(off, static_cast<uint32_t>(s)));
-        sum.x += v.x;
-        sum.y += v.y;
-        sum.z += v.z;
-        sum.w += v.w;
+    cluster_sync_all();  // every CTA's partial tile is written and every mainloop is over
+    // Push rows [o*rpr, (o+1)*rpr) of this CTA's partial tile to owner o (slot = this rank,
+    // skipping o's own), one bulk copy per owner.
+    if (threadIdx.x < cs && threadIdx.x != ks) {
+      const int o = threadIdx.x;
+      const int q0 = min(kSkBM, o * L.rpr), q1 = min(kSkBM, q0 + L.rpr);
+      if (q1 > q0) {
+        const int slot = ks < o ? ks : ks - 1;
+        bulk_push_to_peer(
+            mapa_shared(smem_u32(smem + L.rst_off) + static_cast<uint32_t>(slot * L.slice_bytes), static_cast<uint32_t>(o)),
+            red + q0 * kRS, static_cast<uint32_t>((q1 - q0) * kRS * 4), mapa_shared(smem_u32(rpull), static_cast<uint32_t>(o)));
       }
-      const float bv = bias != nullptr ? to_f32(bias[n]) : 0.f;
-      const float vals[4] = {sum.x, sum.y, sum.z, sum.w};
+    }
+    // this CTA's rows: its own partial plus the pushed slices, summed in rank order
+    const int r0 = min(kSkBM, ks * L.rpr), r1 = min(kSkBM, r0 + L.rpr);
+    const bool got = mbar_wait_bounded(rpull, 0, abort_flag, p.err, kDevErrTimeoutFull);
+    const float* rst = reinterpret_cast<const float*>(smem + L.rst_off);
+    // one item = token t, 8 consecutive features (one 16-byte store of out)
+    const bool vec_out = (p.ldo % 8 == 0) && ((reinterpret_cast<uintptr_t>(out) & 15u) == 0);
+    const int groups = (r1 - r0) / 8;
+    const int items = NB * groups;
+    for (int idx = threadIdx.x; got && idx < items; idx += kSkThreads) {
+      const int t = idx % NB;            // consecutive threads: consecutive tokens (conflict-free columns)
+      const int lr = (idx / NB) * 8;     // first of 8 rows within the slice
+      const int n = n0 + r0 + lr;
+      if (n >= p.N || tok0 + t >= p.M) continue;
+      float v[8];
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const int t = tok0 + c4 + e;
-        if (t < p.M) out[static_cast<int64_t>(t) * p.ldo + n] = from_f32<T>(vals[e] + bv);
+      for (int e = 0; e < 8; ++e) v[e] = 0.f;
+      for (int s = 0; s < cs; ++s) {
+        const float* src = (s == ks ? red + (r0 + lr) * kRS : rst + (s < ks ? s : s - 1) * (L.slice_bytes / 4) + lr * kRS) + t;
+#pragma unroll
+        for (int e = 0; e < 8; ++e) v[e] += src[e * kRS];
+      }
+      T* dst = out + static_cast<int64_t>(tok0 + t) * p.ldo + n;
+      if (vec_out && n + 8 <= p.N) {
+        float bv[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) bv[e] = bias != nullptr ? to_f32(bias[n + e]) : 0.f;
+        *reinterpret_cast<uint4*>(dst) = make_uint4(pack2<T>(v[0] + bv[0], v[1] + bv[1]), pack2<T>(v[2] + bv[2], v[3] + bv[3]),
+                                                    pack2<T>(v[4] + bv[4], v[5] + bv[5]), pack2<T>(v[6] + bv[6], v[7] + bv[7]));
+      } else {
+#pragma unroll
+        for (int e = 0; e < 8; ++e)
+          if (n + e < p.N) dst[e] = from_f32<T>(v[e] + (bias != nullptr ? to_f32(bias[n + e]) : 0.f));
       }
     }
     __syncwarp();
-    cluster_sync_all();  // peers are done reading this CTA's partial tile
+    cluster_sync_all();  // every push has landed: no CTA's partial tile is read any more
   }
 
   tc_fence_before();
@@ -520,18 +652,19 @@ int rotate_env() {
 SkinnyPlan plan_skinny(int nb, int rch, int r16, int fz, int64_t tiles, int64_t steps, int num_sms, int smem_per_sm,
                        int split_req) {
   const SkinnyPlan f = forced_plan();
-  if (f.stages >= 2 && f.split >= 1 && SkinnyLayout(nb, f.stages, rch, r16, fz).bytes <= 227 * 1024) {
+  if (f.stages >= 2 && f.split >= 1 && SkinnyLayout(nb, f.stages, rch, r16, fz, f.split).bytes <= 227 * 1024) {
     const int s = static_cast<int>(std::min<int64_t>(std::min(f.split, kSkinnyMaxSplit), steps));
     return SkinnyPlan{std::min(f.stages, 8), s};
   }
   SkinnyPlan best{2, 1};
   double best_cost = 1e300;
   for (int st = 2; st <= 6; ++st) {
-    const SkinnyLayout L(nb, st, rch, r16, fz);
-    if (L.bytes > 227 * 1024) break;
-    const int c = ctas_per_sm(L, smem_per_sm);
-    const int64_t slots = static_cast<int64_t>(num_sms) * c;
+    if (SkinnyLayout(nb, st, rch, r16, fz, 1).bytes > 227 * 1024) break;
     for (int s = 1; s <= kSkinnyMaxSplit && s <= steps; ++s) {
+      const SkinnyLayout L(nb, st, rch, r16, fz, s);
+      if (L.bytes > 227 * 1024) continue;
+      const int c = ctas_per_sm(L, smem_per_sm);
+      const int64_t slots = static_cast<int64_t>(num_sms) * c;
       if (split_req > 0 && s != std::min<int64_t>(split_req, std::min<int64_t>(kSkinnyMaxSplit, steps))) continue;
       const int64_t per = (steps + s - 1) / s;
       if ((steps + per - 1) / per != s) continue;  // no empty slice
@@ -611,11 +744,11 @@ int launch_skinny_linear(const void* x, int64_t ldx, const void* w, int64_t ldw,
   const int64_t tiles = ((N + kSkBM - 1) / kSkBM) * ((M + nb - 1) / nb);
   const SkinnyPlan plan = plan_skinny(nb, rch, r16, fuse, tiles, num_kb, num_sms, smem_per_sm, split);
   const int stages = plan.stages;
-  const SkinnyLayout L(nb, stages, rch, r16, fuse);
-  if (L.bytes > 227 * 1024) return LORA_ERR_UNSUPPORTED;
   split = plan.split;
   const int kb_per = (num_kb + split - 1) / split;
   split = (num_kb + kb_per - 1) / kb_per;
+  const SkinnyLayout L(nb, stages, rch, r16, fuse, split);
+  if (L.bytes > 227 * 1024) return LORA_ERR_UNSUPPORTED;
 
   // W box rows (128: one box per k-block; smaller boxes measured slower on B200)
   const int box_rows_pre = tune_env("LORA_B200_SKINNY_BR", 128);
