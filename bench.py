@@ -42,8 +42,8 @@ M_TOKENS = 32760
 CPU_SAMPLE_TOKENS = 4096
 # DRAM read + write of one fused-GEMM launch (C5 q projection), from the full
 # ncu capture at M = 16384 committed under profiles/, scaled linearly to M:
-# 678.7 MB read + 155.2 MB write per launch at M = 16384.
-NCU_TRAFFIC_Q_16384 = 833.9e6
+# 773.1 MB read + 155.1 MB write per launch at M = 16384 (CTA-pair kernel).
+NCU_TRAFFIC_Q_16384 = 928.2e6
 
 
 def parse():
