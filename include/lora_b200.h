@@ -238,6 +238,16 @@ LORA_API int lora_sgmv_shrink(const void* x, int64_t ldx, const void* a_flat, in
                      const int32_t* tiles, const int64_t* rows, void* z, int64_t ldz, int z_dtype, int64_t z_width,
                      int64_t T, int64_t S, int64_t K, int64_t r_max, float scale, int dtype,
                      int split_k, void* workspace, size_t workspace_bytes, void* stream);
+/* lora_sgmv_shrink with the row count of a_flat ([a_rows, K]): knowing the
+ * table's extent lets the tensor-core form (128-token blocks, adapter rows
+ * gathered by TMA) bound its reads, so it is used when rows == NULL and the
+ * rows are 16-byte aligned.  No counterpart in the reference (its shrink is
+ * the Triton kernel of segmented_branch.py:12-28). */
+LORA_API int lora_sgmv_shrink_ex(const void* x, int64_t ldx, const void* a_flat, int64_t lda, int64_t a_rows,
+                        const int64_t* offsets, const int64_t* ranks, int64_t n_adapters,
+                        const int32_t* tiles, const int64_t* rows, void* z, int64_t ldz, int z_dtype,
+                        int64_t z_width, int64_t T, int64_t S, int64_t K, int64_t r_max, float scale, int dtype,
+                        int split_k, void* workspace, size_t workspace_bytes, void* stream);
 
 /* out[t, :] = y[t, :] + scale * z[t, :r] . B_{a(t)}^T ; y may be NULL.
  * rows (optional): logical token t uses row rows[t] of y, z and out. */

@@ -69,6 +69,8 @@ SIGNATURES = {
     "lora_sgmv_pick_split_k": (_I, [_I64, _I64, _I64]),
     "lora_sgmv_shrink": (_I, [_P, _I64, _P, _I64, _P, _P, _I64, _P, _P, _P, _I64, _I, _I64, _I64, _I64, _I64, _I64,
                               _F, _I, _I, _P, _SZ, _P]),
+    "lora_sgmv_shrink_ex": (_I, [_P, _I64, _P, _I64, _I64, _P, _P, _I64, _P, _P, _P, _I64, _I, _I64, _I64, _I64,
+                                 _I64, _I64, _F, _I, _I, _P, _SZ, _P]),
     "lora_sgmv_expand": (_I, [_P, _I64, _P, _I64, _I, _P, _I64, _I64, _P, _P, _I64, _P, _P, _P, _I64, _I64, _I64,
                               _I64, _I64, _F, _I, _P]),
 }

@@ -74,4 +74,12 @@ struct SgmvExpandBlockArgs {
 };
 int launch_sgmv_expand_block(const SgmvExpandBlockArgs& p, int dtype, int z_dtype, void* stream);
 
+// Tensor-core segmented shrink (sgmv_tc.cu): 128-token blocks, every adapter of
+// a block in one MMA chain, K slices reduced over a cluster.  Needs the row
+// count of a_flat (bounds of its TMA reads), no row indirection, aligned rows.
+int launch_sgmv_shrink_tc(const void* x, int64_t ldx, const void* a_flat, int64_t lda, int64_t a_rows,
+                          const int64_t* offsets, const int64_t* ranks, const int32_t* tiles, void* z, int64_t ldz,
+                          int z_dtype, int64_t z_width, int64_t T, int64_t K, int64_t r_max, float scale, int dtype,
+                          int num_sms, int* err, void* stream);
+
 }  // namespace lora

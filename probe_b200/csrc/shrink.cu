@@ -417,12 +417,12 @@ extern "C" size_t lora_sgmv_shrink_workspace_size(int64_t T, int64_t S, int64_t 
   return kCounterBytes + round256(partial);
 }
 
-extern "C" int lora_sgmv_shrink(const void* x, int64_t ldx, const void* a_flat, int64_t lda, const int64_t* offsets,
-                                const int64_t* ranks, int64_t n_adapters, const int32_t* tiles, const int64_t* rows,
-                                void* z, int64_t ldz,
-                                int z_dtype, int64_t z_width, int64_t T, int64_t S, int64_t K, int64_t r_max,
-                                float scale, int dtype, int split_k, void* workspace, size_t workspace_bytes,
-                                void* stream) {
+namespace {
+int sgmv_shrink_impl(const void* x, int64_t ldx, const void* a_flat, int64_t lda, int64_t a_rows,
+                     const int64_t* offsets, const int64_t* ranks, int64_t n_adapters, const int32_t* tiles,
+                     const int64_t* rows, void* z, int64_t ldz, int z_dtype, int64_t z_width, int64_t T, int64_t S,
+                     int64_t K, int64_t r_max, float scale, int dtype, int split_k, void* workspace,
+                     size_t workspace_bytes, void* stream) {
   if (x == nullptr || a_flat == nullptr || offsets == nullptr || ranks == nullptr || tiles == nullptr || z == nullptr)
     return LORA_ERR_ARG;
   if (dtype != LORA_BF16 && dtype != LORA_F16) return LORA_ERR_DTYPE;
@@ -443,8 +443,15 @@ extern "C" int lora_sgmv_shrink(const void* x, int64_t ldx, const void* a_flat, 
     if (sgmv_max_tiles(T, S) > kMaxCounters) return LORA_ERR_SHAPE;
   }
 
-  // Dense 64-token blocks first (sgmv_block.cu); the per-tile kernel below
-  // covers the layouts that path does not take (unaligned rows, r_max > 128).
+  // Tensor cores first (sgmv_tc.cu: 128-token blocks, TMA-fed, needs the row
+  // count of a_flat and no row indirection), then dense 64-token blocks on
+  // mma.sync (sgmv_block.cu); the per-tile kernel below covers the layouts
+  // neither takes (unaligned rows, r_max > 128).
+  if (rows == nullptr && a_rows > 0 && r_max > 0 && K > 0) {
+    const int rc = launch_sgmv_shrink_tc(x, ldx, a_flat, lda, a_rows, offsets, ranks, tiles, z, ldz, z_dtype, z_width,
+                                         T, K, r_max, scale, dtype, info.num_sms, info.err_word, stream);
+    if (rc != LORA_ERR_UNSUPPORTED) return rc;
+  }
   if (r_max > 0 && K > 0) {
     SgmvShrinkBlockArgs bp{};
     bp.x = x;
@@ -505,6 +512,26 @@ extern "C" int lora_sgmv_shrink(const void* x, int64_t ldx, const void* a_flat, 
       max_tiles, std::max<int64_t>(1, (4 * static_cast<int64_t>(info.num_sms) + split_k - 1) / split_k));
   dim3 grid(static_cast<unsigned>(gx), static_cast<unsigned>(split_k));
   return launch_shrink(p, dtype, z_dtype, aligned, grid, s);
+}
+}  // namespace
+
+extern "C" int lora_sgmv_shrink(const void* x, int64_t ldx, const void* a_flat, int64_t lda, const int64_t* offsets,
+                                const int64_t* ranks, int64_t n_adapters, const int32_t* tiles, const int64_t* rows,
+                                void* z, int64_t ldz, int z_dtype, int64_t z_width, int64_t T, int64_t S, int64_t K,
+                                int64_t r_max, float scale, int dtype, int split_k, void* workspace,
+                                size_t workspace_bytes, void* stream) {
+  return sgmv_shrink_impl(x, ldx, a_flat, lda, 0, offsets, ranks, n_adapters, tiles, rows, z, ldz, z_dtype, z_width, T,
+                          S, K, r_max, scale, dtype, split_k, workspace, workspace_bytes, stream);
+}
+
+extern "C" int lora_sgmv_shrink_ex(const void* x, int64_t ldx, const void* a_flat, int64_t lda, int64_t a_rows,
+                                   const int64_t* offsets, const int64_t* ranks, int64_t n_adapters,
+                                   const int32_t* tiles, const int64_t* rows, void* z, int64_t ldz, int z_dtype,
+                                   int64_t z_width, int64_t T, int64_t S, int64_t K, int64_t r_max, float scale,
+                                   int dtype, int split_k, void* workspace, size_t workspace_bytes, void* stream) {
+  if (a_rows < 0) return LORA_ERR_SHAPE;
+  return sgmv_shrink_impl(x, ldx, a_flat, lda, a_rows, offsets, ranks, n_adapters, tiles, rows, z, ldz, z_dtype,
+                          z_width, T, S, K, r_max, scale, dtype, split_k, workspace, workspace_bytes, stream);
 }
 
 // ---------------------------------------------------------------------------

@@ -278,8 +278,9 @@ def sgmv_shrink(x: torch.Tensor, a_flat: torch.Tensor, offsets: torch.Tensor, ra
     ranks = _i64(ranks, x.device)
     if rows is not None:
         rows = _i64(rows, x.device)
-    _lib.call("lora_sgmv_shrink", _lib.ptr(x), _lib.ld(x), _lib.ptr(a_flat), _lib.ld(a_flat), _lib.ptr(offsets),
-              _lib.ptr(ranks), offsets.numel(), _lib.ptr(tiles), _lib.ptr(rows), _lib.ptr(out), out.stride(0),
+    _lib.call("lora_sgmv_shrink_ex", _lib.ptr(x), _lib.ld(x), _lib.ptr(a_flat), _lib.ld(a_flat), a_flat.shape[0],
+              _lib.ptr(offsets), _lib.ptr(ranks), offsets.numel(), _lib.ptr(tiles), _lib.ptr(rows), _lib.ptr(out),
+              out.stride(0),
               _lib.dtype_code(out.dtype), width, t, s, k, int(r_max), float(scale), _dt(x), int(split_k),
               _lib.ptr(ws), ws.numel(), _lib.stream_handle(x.device))
     return out

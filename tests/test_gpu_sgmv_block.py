@@ -138,3 +138,30 @@ def test_fallback_layouts_match_block_path():
         z = kernels.sgmv_shrink(x, a, offs, rk, tiles, s, 16)
         out = kernels.sgmv_expand(y, z, b, n, 1, offs, rk, tiles, s, n, 16)
         assert_parity(out, _want_out(y, np64(z), b, offs, rk, ids))
+
+
+@pytest.mark.parametrize("t,k,ranks", [(300, 520, [128, 96, 5]), (129, 4096, [64, 16, 4, 32, 8]),
+                                       (4096, 1024, [4, 8, 16, 32, 64] * 4)])
+def test_tensor_core_shrink_matches_oracle(t, k, ranks):
+    """The tcgen05 segmented shrink (128-token blocks, adapter rows gathered by
+    TMA, passes when a block's adapters exceed 256 rows, cluster split-K)."""
+    n = 64
+    a, b, offs, rk = _tables(ranks, k, n, seed=t)
+    gen = torch.Generator().manual_seed(t + 1)
+    lens = torch.randint(1, 90, (t,), generator=gen)
+    seg = [0]
+    while seg[-1] < t:
+        seg.append(min(t, seg[-1] + int(lens[len(seg)])))
+    seg_start = torch.tensor(seg, device=DEV)
+    seg_ad = torch.randint(0, len(ranks), (len(seg) - 1,), generator=gen).to(DEV)
+    ids = orc.segments_to_ids(seg_start.cpu().numpy(), seg_ad.cpu().numpy())
+    x = randn((t, k), 1.0, seed=t + 2)
+    tiles, s = kernels.sgmv_schedule(t, len(ranks), seg_start=seg_start, seg_adapter=seg_ad)
+    r_max = max(ranks)
+    for zdt in (torch.float32, torch.bfloat16):
+        z = kernels.sgmv_shrink(x, a, offs, rk, tiles, s, r_max, scale=0.5, z_dtype=zdt)
+        want = _want_z(x, a, offs, rk, ids, r_max, scale=0.5)
+        tol = 2e-4 if zdt == torch.float32 else 1e-2
+        assert np.abs(np64(z) - want).max() < tol * max(1.0, np.abs(want).max())
+        assert torch.equal(z, kernels.sgmv_shrink(x, a, offs, rk, tiles, s, r_max, scale=0.5, z_dtype=zdt))
+    assert _lib.device_error() == 0
