@@ -704,7 +704,9 @@ bool use_pair_tiles(int64_t M, int64_t N, int num_sms) {
   if (force != nullptr && std::strcmp(force, "1sm") == 0) return false;
   const int64_t tiles = ((M + 255) / 256) * ((N + 255) / 256);
   if (force != nullptr && std::strcmp(force, "2sm") == 0) return N > 128;
-  return N >= 256 && tiles >= num_sms;
+  // Outputs wider than 128 columns (the rank-224 shrink included: one 256-wide
+  // pair tile reads x once instead of twice) once the grid fills a wave of pairs.
+  return N > 128 && tiles >= num_sms / 2;
 }
 
 }  // namespace

@@ -381,10 +381,12 @@ __global__ void __launch_bounds__(kSkThreads, 1) skinny_linear_kernel(const __gr
           }
         }
       }
+      // Every epilogue warp's rows of zred are written before any thread reads
+      // them (the last CTA sums them in phase B, the others push them).
+      fence_proxy_async_smem();
+      named_bar_sync(1, 128);
       if (cs > 1 && !tail) {
         // push this CTA's z partial into the last CTA's slot [ks]
-        fence_proxy_async_smem();
-        named_bar_sync(1, 128);
         if (threadIdx.x == 64) {
           const uint32_t last = static_cast<uint32_t>(cs - 1);
           const uint32_t zr_bytes = static_cast<uint32_t>((L.zpush_bytes + 1023) & ~1023);

@@ -182,6 +182,29 @@ def test_linear_small_fused_shrink(m, k, n, r):
     assert _lib.device_error() == 0
 
 
+@pytest.mark.parametrize("r", [65, 67, 33])
+def test_linear_small_odd_rank_pitch_repeated(r):
+    """lora_B with an odd row pitch is staged element by element, which runs the
+    last CTA's warps out of step; ranks above 64 need two rank chunks and the
+    K split a cluster of several CTAs.  Repeated with other kernels in between
+    and the output pre-filled with NaN, so no result can come from memory a
+    previous launch left behind."""
+    m, k, n = 17, 1536, 512
+    dtype = torch.bfloat16
+    x = randn((m, k), 1.0, dtype, seed=41)
+    w = randn((n, k), 1 / math.sqrt(k), dtype, seed=42)
+    a = randn((r, k), 1 / math.sqrt(k), dtype, seed=43)
+    b = randn((n, r), 1 / math.sqrt(r), dtype, seed=44)
+    assert b.stride(0) == r
+    want = orc.naive_linear(np64(x), np64(w), None, np64(a), np64(b), 0.9)
+    for _ in range(6):
+        torch.empty(1 << 27, dtype=torch.uint8, device="cuda").fill_(0xAB)
+        out = torch.full((m, n), float("nan"), device="cuda", dtype=dtype)
+        kernels.linear_small(x, w, a, b, None, 0.9, out=out)
+        assert_parity(out, want, dtype)
+    assert _lib.device_error() == 0
+
+
 def test_linear_small_declines_unaligned():
     x = randn((4, 257), 1.0, seed=1)
     w = randn((64, 257), 0.05, seed=2)
@@ -209,6 +232,24 @@ def test_gemm_hi_lo_epilogue():
     assert_parity(z[:, :n], want)
     _, fro = orc.parity(np64(z[:, :n]) + np64(z[:, n:]), want)
     assert fro < 2e-5, fro
+
+
+def test_pair_gemm_narrow_wide_output():
+    """A 224-wide output with the hi/lo epilogue on CTA-pair tiles (the rank
+    shrink of a stacked r = 224 adapter at large M): one 256-wide tile per pair,
+    columns 224..255 and rows past M clipped."""
+    m, n, k = 19000, 224, 256
+    x = randn((m, k), 1.0, seed=31)
+    w = randn((n, k), 1 / math.sqrt(k), seed=32)
+    z = torch.empty((m, 2 * n), dtype=torch.bfloat16, device="cuda")
+    kernels.gemm(x, w, alpha=0.5, out=z[:, :n], lo_offset=n)
+    rows = np.r_[0:64, 9000:9100, m - 70:m]
+    want = 0.5 * (np64(x)[rows] @ np64(w).T)
+    got = np64(z[:, :n])[rows] + np64(z[:, n:])[rows]
+    _, fro = orc.parity(got, want)
+    assert fro < 2e-5, fro
+    assert_parity(z[:, :n][torch.as_tensor(rows, device="cuda")], want)
+    assert _lib.device_error() == 0
 
 
 def test_workspace_reuse_across_shapes():
