@@ -184,18 +184,26 @@ LORA_API int lora_decode_linear(const void* x, int64_t ldx, const void* w, int64
 /* ---------------------------------------------------------------------------
  * Small-M LoRA linear in one kernel: out[M,N] = x . w^T + scale * (x . a^T) . b^T + bias
  * a is lora_A.weight [R,K], b is lora_B.weight [N,R]; R == 0 (a, b NULL) gives
- * the base linear.  The shrink is computed inside the W-streaming kernel (z
- * never written to memory) and scale * z enters the expand as a hi/lo pair of
- * the input dtype.  M <= 256, R <= 128; K, ldx, ldw, lda multiples of 8 and
- * x, w, a 16-byte aligned, else LORA_ERR_UNSUPPORTED (use lora_shrink +
- * lora_decode_linear).  No workspace.
+ * the base linear.  The shrink is computed inside the kernel that streams W
+ * (z never written to memory).  M <= 256, R <= 128; K, ldx, ldw, lda
+ * multiples of 8 and x, w, a 16-byte aligned, else LORA_ERR_UNSUPPORTED (use
+ * lora_shrink + lora_decode_linear).
+ * Up to 128 tokens (and ranks above 32) run the W-streaming skinny kernel,
+ * where scale * z enters the expand as a hi/lo pair of the input dtype.  Above
+ * 128 tokens with R <= 32 a split-K CTA-pair kernel runs instead (256-token
+ * tiles, K split over a cluster, z kept in fp32); it exchanges partial tiles
+ * through `workspace`, which must hold lora_linear_small_workspace_size(M, N, R)
+ * bytes (16-byte aligned) and must not be used by a concurrent launch.  With a
+ * smaller or NULL workspace the skinny kernel runs.
  * Replaces: decode_lora_linear (decode_linear.py:81-100) and the small-M
  * fused_lora_linear (fused_linear.py:527-551) -- shrink, expand and base in
  * one launch, where the reference re-derives x . A^T in every output tile.
  * ------------------------------------------------------------------------- */
+LORA_API size_t lora_linear_small_workspace_size(int64_t M, int64_t N, int64_t R);
 LORA_API int lora_linear_small(const void* x, int64_t ldx, const void* w, int64_t ldw, const void* a, int64_t lda,
                                const void* b, int64_t ldb, const void* bias, void* out, int64_t ldo, int64_t M,
-                               int64_t N, int64_t K, int64_t R, float scale, int dtype, void* stream);
+                               int64_t N, int64_t K, int64_t R, float scale, int dtype, void* workspace,
+                               size_t workspace_bytes, void* stream);
 
 /* ---------------------------------------------------------------------------
  * Segmented multi-adapter LoRA (SGMV / BGMV).

@@ -61,8 +61,9 @@ SIGNATURES = {
     "lora_decode_pick_split_k": (_I, [_I64, _I64, _I64]),
     "lora_decode_linear": (_I, [_P, _I64, _P, _I64, _P, _I64, _I, _P, _I64, _P, _P, _I64, _I64, _I64, _I64, _I64,
                                 _F, _I, _I, _P, _SZ, _P]),
+    "lora_linear_small_workspace_size": (_SZ, [_I64, _I64, _I64]),
     "lora_linear_small": (_I, [_P, _I64, _P, _I64, _P, _I64, _P, _I64, _P, _P, _I64, _I64, _I64, _I64, _I64, _F,
-                               _I, _P]),
+                               _I, _P, _SZ, _P]),
     "lora_sgmv_tiles_size": (_SZ, [_I64, _I64]),
     "lora_sgmv_schedule": (_I, [_P, _P, _P, _I64, _I64, _I64, _P, _SZ, _P]),
     "lora_sgmv_shrink_workspace_size": (_SZ, [_I64, _I64, _I64, _I]),

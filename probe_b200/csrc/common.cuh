@@ -141,6 +141,9 @@ LORA_DEVINL void ldmatrix_x4_trans(uint32_t (&r)[4], uint32_t saddr) {
 // Make this thread's generic-proxy shared-memory writes visible to the async
 // proxy (TMA, tcgen05.mma operand reads).
 LORA_DEVINL void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+// Orders this thread's generic-proxy global accesses with later async-proxy
+// (bulk copy / TMA) accesses of the same global memory.
+LORA_DEVINL void fence_proxy_async_global() { asm volatile("fence.proxy.async.global;" ::: "memory"); }
 
 // Programmatic dependent launch: let the next kernel in the stream start its
 // prologue, and wait for the previous kernel's results.
@@ -217,6 +220,16 @@ LORA_DEVINL void tma_load_2d(const CUtensorMap* map, void* smem_dst, uint64_t* b
       "[%0], [%1, {%3, %4}], [%2];" ::"r"(smem_u32(smem_dst)),
       "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(c0), "r"(c1)
       : "memory");
+}
+
+// Bulk copy (no tensor map, no multicast) of `bytes` (a multiple of 16, both
+// addresses 16-byte aligned) from global into this CTA's shared memory; the
+// bytes complete on `bar`.
+LORA_DEVINL void bulk_load_g2s(void* smem_dst, const void* gsrc, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   smem_u32(smem_dst)),
+               "l"(reinterpret_cast<uint64_t>(gsrc)), "r"(bytes), "r"(smem_u32(bar))
+               : "memory");
 }
 
 // ---------------------------------------------------------------- tcgen05
@@ -322,6 +335,13 @@ LORA_DEVINL float4 ld_dsmem_f4(uint32_t cluster_addr) {
 LORA_DEVINL void mbar_arrive_cluster(uint32_t cluster_addr) {
   asm volatile("mbarrier.arrive.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
 }
+// Arrive with release semantics at cluster scope: this thread's earlier
+// writes are visible to a thread of another CTA that waits on the barrier and
+// then fences at cluster scope (fence_acq_rel_cluster).
+LORA_DEVINL void mbar_arrive_cluster_release(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+LORA_DEVINL void fence_acq_rel_cluster() { asm volatile("fence.acq_rel.cluster;" ::: "memory"); }
 // Bulk copy of `bytes` (multiple of 16) from this CTA's shared memory into the
 // shared memory of a CTA of the cluster; the bytes complete on the mbarrier at
 // `bar_cluster_addr` in that CTA.  Shared-to-shared push, no multicast.

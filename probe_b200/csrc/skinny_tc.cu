@@ -36,6 +36,7 @@
 
 #include "common.cuh"
 #include "runtime.h"
+#include "gemm_split.h"
 #include "skinny.h"
 
 namespace lora {
@@ -643,6 +644,14 @@ int tune_env(const char* name, int fallback) {
   return (v != nullptr && v[0] >= '0' && v[0] <= '9') ? std::atoi(v) : fallback;
 }
 
+// Token counts above this go to the split-K CTA-pair kernel (gemm_split.cu):
+// 256-token tiles read x once per 256 W rows instead of once per 128.
+// LORA_B200_SPLIT_MIN_M overrides the threshold (tuning sweeps).
+int split_min_rows() {
+  static const int m = tune_env("LORA_B200_SPLIT_MIN_M", 128);
+  return m;
+}
+
 int rotate_env() {
   static const int r = [] {
     const char* v = std::getenv("LORA_B200_SKINNY_ROTATE");
@@ -810,9 +819,14 @@ int launch_skinny_linear(const void* x, int64_t ldx, const void* w, int64_t ldw,
 
 using namespace lora;
 
+extern "C" size_t lora_linear_small_workspace_size(int64_t M, int64_t N, int64_t R) {
+  return M > split_min_rows() ? split_pair_workspace_bytes(M, N, R) : 0;
+}
+
 extern "C" int lora_linear_small(const void* x, int64_t ldx, const void* w, int64_t ldw, const void* a, int64_t lda,
                                  const void* b, int64_t ldb, const void* bias, void* out, int64_t ldo, int64_t M,
-                                 int64_t N, int64_t K, int64_t R, float scale, int dtype, void* stream) {
+                                 int64_t N, int64_t K, int64_t R, float scale, int dtype, void* workspace,
+                                 size_t workspace_bytes, void* stream) {
   if (x == nullptr || w == nullptr || out == nullptr) return LORA_ERR_ARG;
   if (R > 0 && (a == nullptr || b == nullptr)) return LORA_ERR_ARG;
   if (dtype != LORA_BF16 && dtype != LORA_F16) return LORA_ERR_DTYPE;
@@ -823,6 +837,11 @@ extern "C" int lora_linear_small(const void* x, int64_t ldx, const void* w, int6
   const int dev = current_device();
   if (dev < 0 || !device_info(dev).is_sm100) return LORA_ERR_DEVICE;
   const DeviceInfo& info = device_info(dev);
+  if (M > split_min_rows()) {  // 256-token CTA-pair tiles, K split over a cluster
+    const int rc = launch_linear_split(x, ldx, w, ldw, a, lda, b, ldb, bias, out, ldo, M, N, K, scale != 0.f ? R : 0,
+                                       scale, dtype, workspace, workspace_bytes, static_cast<cudaStream_t>(stream));
+    if (rc != LORA_ERR_UNSUPPORTED) return rc;
+  }
   return launch_skinny_linear(x, ldx, w, ldw, nullptr, 0, 0, R > 0 ? a : nullptr, lda, b, ldb, bias, out, ldo, M, N,
                               K, R, scale, dtype, 0, info.num_sms, info.smem_per_sm, info.err_word, stream);
 }

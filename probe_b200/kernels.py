@@ -217,10 +217,12 @@ def linear_small(x: torch.Tensor, w: torch.Tensor, a: torch.Tensor | None, b: to
     if out is None:
         out = torch.empty((m, n), device=x.device, dtype=x.dtype)
     lib = _lib.load()
+    ws_bytes = lib.lora_linear_small_workspace_size(m, n, r)
+    ws = _lib.WORKSPACE.get(ws_bytes, x.device, "small") if ws_bytes else None
     rc = lib.lora_linear_small(_lib.ptr(x), _lib.ld(x), _lib.ptr(w), _lib.ld(w), _lib.ptr(a) if r else None,
                                _lib.ld(a) if r else 0, _lib.ptr(b) if r else None, _lib.ld(b) if r else 0,
                                _lib.ptr(bias), _lib.ptr(out), out.stride(0), m, n, k, r, float(scale), _dt(x),
-                               _lib.stream_handle(x.device))
+                               _lib.ptr(ws), ws_bytes, _lib.stream_handle(x.device))
     if rc == _lib.LORA_ERR_UNSUPPORTED:
         return None
     _lib.check(rc, "lora_linear_small")
