@@ -9,8 +9,10 @@
 // so a single MMA chain multiplies every token by every adapter present in
 // its block; each token then takes its own adapter's columns from TMEM.  The
 // wasted products are free -- the kernel streams x once and the tensor pipe
-// is otherwise idle.  Blocks whose adapters need more than 256 rows run in
-// passes.  The K slices of a block are the CTAs of a cluster: each writes its
+// is otherwise idle.  A pass holds up to 512 adapter rows (two MMAs of N <= 256
+// into the two halves of TMEM); the stage stride is sized at run time to the
+// block's widest pass, so narrow blocks keep more stages in flight.  Blocks
+// whose adapters need more rows than one pass holds run in passes.  The K slices of a block are the CTAs of a cluster: each writes its
 // per-token results to shared memory, pushes row slices to their owners with
 // bulk shared::cluster copies, and each owner sums its rows in rank order
 // (deterministic, no workspace) and writes z.
@@ -33,14 +35,16 @@ namespace {
 
 constexpr int kTcBM = 128;         // tokens per CTA
 constexpr int kTcBK = 64;          // K per stage
-constexpr int kTcNmax = 256;       // adapter rows per pass (MMA N)
+constexpr int kTcMmaN = 256;       // adapter rows per MMA (N)
+constexpr int kTcPassMax = 512;    // adapter rows per pass (two MMAs, 512 TMEM columns)
+constexpr int kTcMaxStages = 8;
 constexpr int kTcThreads = 192;
 constexpr int kTcMaxTiles = 128;   // a 128-token block holds at most 128 tiles
 constexpr int kTcXBytes = kTcBM * kTcBK * 2;    // 16 KB
-constexpr int kTcABytes = kTcNmax * kTcBK * 2;  // 32 KB
 
 struct TcTiles {
   int n, npass;
+  int stride, stages;                     // stage ring geometry for this block
   int lo[kTcMaxTiles], hi[kTcMaxTiles];  // rows [lo, hi) of the block
   int r[kTcMaxTiles];                     // rank used (0 = nothing)
   int srow[kTcMaxTiles];                  // first operand row within its pass
@@ -50,15 +54,16 @@ struct TcTiles {
   int row_tile[kTcBM];                    // tile of each row, -1 = none
 };
 
+// Shared memory: [stage ring][red][tile table][barriers].  Each stage is the
+// x tile (16 KB) followed by the pass's adapter rows (128 B each), its stride
+// rounded to 1 KB (swizzle atoms stay aligned).
 struct TcLayout {
-  int stages, rs, cs;
-  int x_off, a_off, red_off, tab_off, bar_off, bytes;
+  int ring, rs, cs;
+  int red_off, tab_off, bar_off, bytes;
   int rpr, slice_bytes;
-  __host__ __device__ TcLayout(int stages_, int rmax16, int cs_) : stages(stages_), cs(cs_) {
+  __host__ __device__ TcLayout(int ring_, int rmax16, int cs_) : ring(ring_), cs(cs_) {
     rs = rmax16 + 4;  // per-token result row (floats)
-    x_off = 0;
-    a_off = stages * kTcXBytes;
-    red_off = a_off + stages * kTcABytes;   // [128][rs] fp32, written pass by pass during the mainloop
+    red_off = ring;   // [128][rs] fp32, written pass by pass during the mainloop
     // slices pushed by the other CTAs land at offset 0 (stage buffers, idle by then)
     rpr = ((kTcBM + cs - 1) / cs + 7) & ~7;
     slice_bytes = rpr * rs * 4;
@@ -67,6 +72,8 @@ struct TcLayout {
     bytes = bar_off + 256 + 1024;
   }
 };
+
+__host__ __device__ inline int tc_stage_stride(int rows) { return (kTcXBytes + rows * 128 + 1023) & ~1023; }
 
 }  // namespace
 
@@ -85,7 +92,7 @@ struct SgmvTcArgs {
   int* err;
   int64_t ldz;
   int T, K, R, z_width, z_f32;
-  int num_kb, kb_per, split, stages, rmax16;
+  int num_kb, kb_per, split, ring, rmax16, pass_cap;
   float scale;
 };
 
@@ -93,8 +100,8 @@ template <typename T>
 __global__ void __launch_bounds__(kTcThreads, 1) sgmv_shrink_tc_kernel(const __grid_constant__ CUtensorMap tm_x,
                                                                        const __grid_constant__ TcAMaps tm_a,
                                                                        const SgmvTcArgs p) {
-  constexpr uint32_t kTmemCols = kTcNmax;
-  const TcLayout L(p.stages, p.rmax16, p.split);
+  constexpr uint32_t kTmemCols = kTcPassMax;
+  const TcLayout L(p.ring, p.rmax16, p.split);
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
@@ -104,8 +111,8 @@ __global__ void __launch_bounds__(kTcThreads, 1) sgmv_shrink_tc_kernel(const __g
   }
   TcTiles& tb = *reinterpret_cast<TcTiles*>(smem + L.tab_off);
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + L.bar_off);
-  uint64_t* empty = full + 8;
-  uint64_t* acc_full = empty + 8;
+  uint64_t* empty = full + kTcMaxStages;
+  uint64_t* acc_full = empty + kTcMaxStages;
   uint64_t* acc_empty = acc_full + 1;
   uint64_t* rpull = acc_empty + 1;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(rpull + 1);
@@ -151,15 +158,16 @@ __global__ void __launch_bounds__(kTcThreads, 1) sgmv_shrink_tc_kernel(const __g
     named_bar_sync(1, 128);
     if (et == 0) {
       tb.n = n;
-      int pass = 0, used = 0;
+      int pass = 0, used = 0, widest = 16;
       for (int i = 0; i < n; ++i) {
         const int r16 = (tb.r[i] + 15) & ~15;
         if (r16 == 0) {
           tb.pass[i] = -1;
           continue;
         }
-        if (used + r16 > kTcNmax) {
+        if (used + r16 > p.pass_cap) {
           tb.pass_rows[pass] = used;
+          widest = max(widest, used);
           ++pass;
           used = 0;
         }
@@ -168,7 +176,11 @@ __global__ void __launch_bounds__(kTcThreads, 1) sgmv_shrink_tc_kernel(const __g
         used += r16;
       }
       if (used > 0) tb.pass_rows[pass] = used;
+      widest = max(widest, used);
       tb.npass = used > 0 ? pass + 1 : 0;
+      tb.stride = tc_stage_stride(widest);
+      // at least 2: the host caps a pass at the rows two stages of the ring hold
+      tb.stages = min(kTcMaxStages, L.ring / tb.stride);
     }
     named_bar_sync(1, 128);
     for (int i = et; i < n; i += 128)
@@ -176,7 +188,7 @@ __global__ void __launch_bounds__(kTcThreads, 1) sgmv_shrink_tc_kernel(const __g
         for (int row = tb.lo[i]; row < tb.hi[i]; ++row) tb.row_tile[row] = i;
   }
   if (threadIdx.x == 0) {
-    for (int s = 0; s < L.stages; ++s) {
+    for (int s = 0; s < kTcMaxStages; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
@@ -222,15 +234,16 @@ __global__ void __launch_bounds__(kTcThreads, 1) sgmv_shrink_tc_kernel(const __g
           }
           const int kc = (kb0 + i) * kTcBK;
           mbar_arrive_expect_tx(&full[stage], tx);
-          tma_load_2d(&tm_x, smem + L.x_off + stage * kTcXBytes, &full[stage], kc, t0);
-          uint8_t* as = smem + L.a_off + stage * kTcABytes;
+          uint8_t* xs = smem + stage * tb.stride;
+          tma_load_2d(&tm_x, xs, &full[stage], kc, t0);
+          uint8_t* as = xs + kTcXBytes;
           for (int ti = 0; ti < tb.n; ++ti) {
             if (tb.pass[ti] != pass) continue;
             const int r16 = (tb.r[ti] + 15) & ~15;
             tma_load_2d(&tm_a.m[(r16 >> 4) - 1], as + tb.srow[ti] * 128, &full[stage], kc,
                         static_cast<int32_t>(tb.arow[ti]));
           }
-          if (++stage == L.stages) {
+          if (++stage == tb.stages) {
             stage = 0;
             phase ^= 1;
           }
@@ -248,21 +261,31 @@ __global__ void __launch_bounds__(kTcThreads, 1) sgmv_shrink_tc_kernel(const __g
           if (!mbar_wait_bounded(acc_empty, (pass - 1) & 1, abort_flag, p.err, kDevErrTimeoutAccEmpty)) break;
           tc_fence_after();
         }
-        const uint32_t idesc = idesc_base | (static_cast<uint32_t>(tb.pass_rows[pass] >> 3) << 17);
+        // rows [0, 256) into TMEM columns [0, 256), the rest into [256, 512)
+        const int rows = tb.pass_rows[pass];
+        const int n0 = min(rows, kTcMmaN), n1 = rows - n0;
+        const uint32_t idesc0 = idesc_base | (static_cast<uint32_t>(n0 >> 3) << 17);
+        const uint32_t idesc1 = idesc_base | (static_cast<uint32_t>((n1 > 0 ? n1 : 16) >> 3) << 17);
         for (int i = 0; i < n_main; ++i) {
           if (!mbar_wait_bounded(&full[stage], phase, abort_flag, p.err, kDevErrTimeoutFull)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint64_t xd = umma_desc_sw128(smem_u32(smem + L.x_off + stage * kTcXBytes));
-          const uint64_t ad = umma_desc_sw128(smem_u32(smem + L.a_off + stage * kTcABytes));
+          const uint32_t xs = smem_u32(smem + stage * tb.stride);
+          const uint64_t xd = umma_desc_sw128(xs);
+          const uint64_t ad0 = umma_desc_sw128(xs + kTcXBytes);
+          const uint64_t ad1 = umma_desc_sw128(xs + kTcXBytes + kTcMmaN * 128);
 #pragma unroll
-          for (int k = 0; k < 4; ++k)
-            tc_mma_f16(tmem_base, xd + static_cast<uint64_t>(2 * k), ad + static_cast<uint64_t>(2 * k), idesc,
+          for (int k = 0; k < 4; ++k) {
+            tc_mma_f16(tmem_base, xd + static_cast<uint64_t>(2 * k), ad0 + static_cast<uint64_t>(2 * k), idesc0,
                        (i > 0 || k > 0) ? 1u : 0u);
+            if (n1 > 0)
+              tc_mma_f16(tmem_base + kTcMmaN, xd + static_cast<uint64_t>(2 * k), ad1 + static_cast<uint64_t>(2 * k),
+                         idesc1, (i > 0 || k > 0) ? 1u : 0u);
+          }
           tc_commit(&empty[stage]);
-          if (++stage == L.stages) {
+          if (++stage == tb.stages) {
             stage = 0;
             phase ^= 1;
           }
@@ -309,6 +332,24 @@ __global__ void __launch_bounds__(kTcThreads, 1) sgmv_shrink_tc_kernel(const __g
   const int my_r0 = min(kTcBM, ks * L.rpr), my_r1 = min(kTcBM, my_r0 + L.rpr);
   auto write_row_range = [&](int r0, int r1, auto&& value) {
     const int w = p.z_width;
+    if (p.z_f32 && (w & 3) == 0 && (p.ldz & 3) == 0 && (reinterpret_cast<uintptr_t>(p.z) & 15) == 0) {
+      // four columns per thread, 16-byte stores
+      const int w4 = w >> 2;
+      for (int idx = threadIdx.x; idx < (r1 - r0) * w4; idx += kTcThreads) {
+        const int lr = idx / w4, j = (idx - lr * w4) * 4;
+        const int row = r0 + lr;
+        if (row >= ntok) continue;
+        const int ti = tb.row_tile[row];
+        const int r = ti >= 0 ? tb.r[ti] : 0;
+        float4 v;
+        v.x = j < r ? p.scale * value(lr, j) : 0.f;
+        v.y = j + 1 < r ? p.scale * value(lr, j + 1) : 0.f;
+        v.z = j + 2 < r ? p.scale * value(lr, j + 2) : 0.f;
+        v.w = j + 3 < r ? p.scale * value(lr, j + 3) : 0.f;
+        *reinterpret_cast<float4*>(static_cast<float*>(p.z) + static_cast<int64_t>(t0 + row) * p.ldz + j) = v;
+      }
+      return;
+    }
     for (int idx = threadIdx.x; idx < (r1 - r0) * w; idx += kTcThreads) {
       const int lr = idx / w, j = idx - lr * w;
       const int row = r0 + lr;
@@ -417,10 +458,12 @@ int launch_sgmv_shrink_tc(const void* x, int64_t ldx, const void* a_flat, int64_
   split = std::max(1, std::min(split, std::max(1, num_kb / 4)));
   const int kb_per = (num_kb + split - 1) / split;
   split = (num_kb + kb_per - 1) / kb_per;
-  int stages = 4;
-  while (stages > 2 && TcLayout(stages, rmax16, split).bytes > 227 * 1024) --stages;
-  const TcLayout L(stages, rmax16, split);
-  if (L.bytes > 227 * 1024 || L.slice_bytes * (split - 1) > L.red_off) return LORA_ERR_UNSUPPORTED;
+  // the stage ring takes what the result rows, the table and the barriers leave
+  const int ring = (227 * 1024 - (TcLayout(0, rmax16, split).bytes)) & ~2047;
+  const TcLayout L(ring, rmax16, split);
+  // a pass holds as many adapter rows as two stages of the ring can carry
+  const int pass_cap = std::min(kTcPassMax, ((ring / 2 - kTcXBytes) / 128) & ~15);
+  if (L.bytes > 227 * 1024 || L.slice_bytes * (split - 1) > L.ring || pass_cap < 128) return LORA_ERR_UNSUPPORTED;
   if (nblk > INT32_MAX) return LORA_ERR_SHAPE;
 
   CUtensorMap tx;
@@ -449,7 +492,8 @@ int launch_sgmv_shrink_tc(const void* x, int64_t ldx, const void* a_flat, int64_
   p.num_kb = num_kb;
   p.kb_per = kb_per;
   p.split = split;
-  p.stages = stages;
+  p.ring = ring;
+  p.pass_cap = pass_cap;
   p.rmax16 = rmax16;
   p.scale = scale;
   dim3 grid(static_cast<unsigned>(nblk), static_cast<unsigned>(split), 1);

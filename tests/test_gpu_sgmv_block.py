@@ -165,3 +165,23 @@ def test_tensor_core_shrink_matches_oracle(t, k, ranks):
         assert np.abs(np64(z) - want).max() < tol * max(1.0, np.abs(want).max())
         assert torch.equal(z, kernels.sgmv_shrink(x, a, offs, rk, tiles, s, r_max, scale=0.5, z_dtype=zdt))
     assert _lib.device_error() == 0
+
+
+@pytest.mark.parametrize("ranks", [[64] * 12, [128, 96, 64, 128, 32, 128, 80, 128]])
+def test_tensor_core_shrink_wide_blocks(ranks):
+    """8-token segments cycling over many wide adapters: a 128-token block needs
+    more than 256 adapter rows (two MMAs per pass) and more than one pass."""
+    t, k, n = 384, 1024, 64
+    a, b, offs, rk = _tables(ranks, k, n, seed=len(ranks))
+    seg = list(range(0, t, 8)) + [t]
+    seg_start = torch.tensor(seg, device=DEV)
+    seg_ad = torch.tensor([i % len(ranks) for i in range(len(seg) - 1)], device=DEV)
+    ids = orc.segments_to_ids(seg_start.cpu().numpy(), seg_ad.cpu().numpy())
+    x = randn((t, k), 1.0, seed=17)
+    tiles, s = kernels.sgmv_schedule(t, len(ranks), seg_start=seg_start, seg_adapter=seg_ad)
+    r_max = max(ranks)
+    z = kernels.sgmv_shrink(x, a, offs, rk, tiles, s, r_max, scale=0.25, z_dtype=torch.float32)
+    want = _want_z(x, a, offs, rk, ids, r_max, scale=0.25)
+    assert np.abs(np64(z) - want).max() < 2e-4 * max(1.0, np.abs(want).max())
+    assert torch.equal(z, kernels.sgmv_shrink(x, a, offs, rk, tiles, s, r_max, scale=0.25, z_dtype=torch.float32))
+    assert _lib.device_error() == 0
