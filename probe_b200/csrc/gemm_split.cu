@@ -30,6 +30,13 @@
 // The exchange goes through L2 rather than distributed shared memory: the
 // SM-to-SM network moved these ~90 KB per CTA several times slower on B200.
 // No TMA multicast and no atomics: results are deterministic.
+//
+// Launched with programmatic stream serialization: every CTA signals its
+// dependents at once, and the producer loads the weight tiles (W, lora_A) of
+// the first stages before griddepcontrol.wait, so in a chain of linears the
+// next launch's prologue and weight prefetch overlap this one's tail.  x and
+// every global write (workspace, out) come after the wait: only the weights,
+// which no kernel of this library writes, are read early.
 #include <cudaTypedefs.h>
 
 #include <algorithm>
@@ -171,6 +178,7 @@ __global__ void __launch_bounds__(kSpThreads, 1)
     tma_prefetch_desc(&tm_w);
     if (RZ > 0) tma_prefetch_desc(&tm_a);
   }
+  if (threadIdx.x == 0) pdl_launch_dependents();
   if (warp == 2) {
     tmem_alloc_pair(tmem_slot, kTmemCols);
     tmem_relinquish_pair();
@@ -188,7 +196,23 @@ __global__ void __launch_bounds__(kSpThreads, 1)
       uint32_t phase = 0;
       const int row_a = mt * 256 + static_cast<int>(half) * 128;
       const int row_b = nt * 256 + static_cast<int>(half) * 128;
-      for (int kb = kb0; kb < kb1; ++kb) {
+      // weights of the first stages before the grid dependency resolves, x after it
+      const int npre = min(kSpStages, kb1 - kb0);
+      for (int i = 0; i < npre; ++i) {
+        if (half == 0) mbar_arrive_expect_tx(&full[i], 2 * L::kStage);
+        const uint32_t bar = mapa_shared(smem_u32(&full[i]), leader_rank);
+        uint8_t* st = smem + i * L::kStage;
+        const int kc = (kb0 + i) * kSpBK;
+        tma_load_2d_pair(&tm_w, st + L::kX, bar, kc, row_b);
+        if (RZ > 0) tma_load_2d_pair(&tm_a, st + L::kX + L::kW, bar, kc, static_cast<int>(half) * (kSpZN / 2));
+      }
+      pdl_wait();
+      for (int i = 0; i < npre; ++i)
+        tma_load_2d_pair(&tm_x, smem + i * L::kStage, mapa_shared(smem_u32(&full[i]), leader_rank),
+                         (kb0 + i) * kSpBK, row_a);
+      stage = npre % kSpStages;
+      phase = npre == kSpStages ? 1u : 0u;
+      for (int kb = kb0 + npre; kb < kb1; ++kb) {
         if (!mbar_wait_bounded(&empty[stage], phase ^ 1, abort_flag, args.err, kDevErrTimeoutEmpty)) break;
         if (half == 0) mbar_arrive_expect_tx(&full[stage], 2 * L::kStage);
         const uint32_t bar = mapa_shared(smem_u32(&full[stage]), leader_rank);
@@ -514,8 +538,11 @@ int launch_t(const CUtensorMap& tx, const CUtensorMap& tw, const CUtensorMap& ta
   if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SplitSmem<S, RZ>::kBytes) !=
       cudaSuccess)
     return LORA_ERR_CUDA;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   cudaLaunchConfig_t cfg = make_config<S, RZ, T>(tiles, stream, attr);
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
+  cfg.numAttrs = 2;
   return cudaLaunchKernelEx(&cfg, kernel, tx, tw, ta, a) == cudaSuccess ? LORA_OK : LORA_ERR_CUDA;
 }
 

@@ -168,6 +168,7 @@ __global__ void __launch_bounds__(kSkThreads, 1) skinny_linear_kernel(const __gr
     tma_prefetch_desc(&tm_x);
     if (p.fuse) tma_prefetch_desc(&tm_a);
   }
+  if (threadIdx.x == 0 && p.early) pdl_launch_dependents();
   if (warp == 1) {
     tmem_alloc(tmem_slot, tmem_cols);
     tmem_relinquish();
@@ -192,7 +193,30 @@ __global__ void __launch_bounds__(kSkThreads, 1) skinny_linear_kernel(const __gr
       // slower on B200).
       const int kg = p.kgroup, br = p.box_rows;
       bool ok = true;
-      for (int i = 0; ok && i < n_main; i += kg) {
+      int i0 = 0;
+      if (p.early && kg == 1) {
+        // Launched behind another linear: the weights (W, lora_A) of the first
+        // stages load before the grid dependency resolves, x after it.
+        const int npre = min(L.stages, n_main);
+        for (int j = 0; j < npre; ++j) {
+          mbar_arrive_expect_tx(&full[j], stage_tx);
+          const int kb = kb0 + (j + rot < n_main ? j + rot : j + rot - n_main);
+          for (int r0 = 0; r0 < kSkBM; r0 += br)
+            tma_load_2d(&tm_w, smem + L.a_off + j * kSkABytes + r0 * 128, &full[j], kb * kSkBK, n0 + r0);
+          if (p.fuse) tma_load_2d(&tm_a, smem + L.at_off + j * L.at_bytes, &full[j], kb * kSkBK, 0);
+        }
+        pdl_wait();
+        for (int j = 0; j < npre; ++j) {
+          const int kb = kb0 + (j + rot < n_main ? j + rot : j + rot - n_main);
+          tma_load_2d(&tm_x, smem + L.b_off + j * L.b_bytes, &full[j], kb * kSkBK, tok0);
+        }
+        stage = npre % L.stages;
+        phase = npre == L.stages ? 1u : 0u;
+        i0 = npre;
+      } else if (p.early) {
+        pdl_wait();
+      }
+      for (int i = i0; ok && i < n_main; i += kg) {
         const int cnt = min(kg, n_main - i);
         const int st0 = stage;  // the group fills stages st0, st0+1, ... (mod stages)
         for (int j = 0; j < cnt; ++j) {
@@ -714,7 +738,7 @@ int launch_nb(const CUtensorMap& tw, const CUtensorMap& tx, const CUtensorMap& t
   attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = pdl ? 2 : 1;  // only the z-consuming form overlaps the kernel before it
+  cfg.numAttrs = pdl ? 2 : 1;
   return cudaLaunchKernelEx(&cfg, kernel, tw, tx, ta, p) == cudaSuccess ? LORA_OK : LORA_ERR_CUDA;
 }
 
@@ -810,7 +834,12 @@ int launch_skinny_linear(const void* x, int64_t ldx, const void* w, int64_t ldw,
   if (bands > INT32_MAX || ttiles > 65535) return LORA_ERR_SHAPE;
   dim3 grid(static_cast<unsigned>(bands), static_cast<unsigned>(split), static_cast<unsigned>(ttiles));
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  const bool pdl = !fuse && R > 0;
+  // Every form runs with programmatic serialization: the z-consuming form waits
+  // before reading z (the shrink launched just before it); the others prefetch
+  // the weights of their first stages before waiting and signal their own
+  // dependents at once.
+  p.early = (fuse || R == 0) ? 1 : 0;
+  const bool pdl = true;
   if (dtype == LORA_BF16) return launch_t<__nv_bfloat16>(nb, tw, tx, ta, p, grid, L.bytes, pdl, s);
   return launch_t<__half>(nb, tw, tx, ta, p, grid, L.bytes, pdl, s);
 }
