@@ -87,6 +87,9 @@ __global__ void __launch_bounds__(1024) sgmv_schedule_kernel(AdapterLookup look,
   __shared__ int s_adapter[kSchedSmemSegs];
   const int tid = threadIdx.x, nth = blockDim.x;
   const int T = look.T;
+  // the segmented shrink launched next may set up (barriers, TMEM) meanwhile;
+  // it waits for this grid before reading the table
+  if (tid == 0) pdl_launch_dependents();
   if (look.ids == nullptr && look.S <= kSchedSmemSegs) {
     for (int i = tid; i <= look.S; i += nth) {
       s_start[i] = clamp_start(look.seg_start[i], T);

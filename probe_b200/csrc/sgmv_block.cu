@@ -331,6 +331,12 @@ __global__ void __launch_bounds__(128) sgmv_expand_block_kernel(const SgmvExpand
   const T* b = static_cast<const T*>(p.b);
   const int row_a = 16 * warp + g, row_b = row_a + 8;
 
+  // Launched with programmatic serialization behind the shrink that writes z:
+  // the tile table (read-only tables) is built first, y, z and the rows table
+  // after griddepcontrol.wait, every global write after that.
+  load_block_tiles(bt, p.tiles, p.offsets, p.ranks, p.R, block, tbase, ntok);
+  pdl_wait();
+
   // ---- y of the block (rows (tid >> 4) + 8 i, chunk tid & 15)
   const int ch = tid & 15;
   const bool col_in = n0 + ch * 8 < p.N;
@@ -373,8 +379,6 @@ __global__ void __launch_bounds__(128) sgmv_expand_block_kernel(const SgmvExpand
       }
     }
   }
-
-  load_block_tiles(bt, p.tiles, p.offsets, p.ranks, p.R, block, tbase, ntok);
 
   float acc[kExpBN / 8][4];
 #pragma unroll
@@ -502,8 +506,17 @@ int launch_expand_rz(const SgmvExpandBlockArgs& p, dim3 grid, cudaStream_t s) {
   if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)) !=
       cudaSuccess)
     return LORA_ERR_CUDA;
-  kernel<<<grid, 128, smem, s>>>(p);
-  return cudaGetLastError() == cudaSuccess ? LORA_OK : LORA_ERR_CUDA;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(128);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, p) == cudaSuccess ? LORA_OK : LORA_ERR_CUDA;
 }
 
 template <typename T, typename TZ>

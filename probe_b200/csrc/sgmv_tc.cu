@@ -127,8 +127,16 @@ __global__ void __launch_bounds__(kTcThreads, 1) sgmv_shrink_tc_kernel(const __g
   const int n_main = max(kb1 - kb0, 0);
   const int rs = L.rs;
 
+  // Launched with programmatic serialization behind the schedule: barriers and
+  // TMEM are set up while it finishes; every global read of the table, x and
+  // a_flat comes after griddepcontrol.wait (the producer's loads follow the
+  // table through the block barrier).  The expand launched next may start its
+  // own set-up at once.
+  if (threadIdx.x == 0) pdl_launch_dependents();
+
   // ---- tile table of the block (warps 2..5), barriers (thread 0), TMEM (warp 1)
   if (warp >= 2) {
+    pdl_wait();
     const int et = threadIdx.x - 64;
     const int nt_all = sgmv_num_tiles(p.tiles);
     const int32_t* first = sgmv_block_first(p.tiles);
@@ -431,13 +439,15 @@ int launch_tc_t(const CUtensorMap& tx, const TcAMaps& ta, const SgmvTcArgs& p, d
   cfg.blockDim = dim3(kTcThreads);
   cfg.dynamicSmemBytes = smem;
   cfg.stream = s;
-  cudaLaunchAttribute attr[1];
+  cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = 1;
   attr[0].val.clusterDim.y = grid.y;
   attr[0].val.clusterDim.z = 1;
+  attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = 2;
   return cudaLaunchKernelEx(&cfg, kernel, tx, ta, p) == cudaSuccess ? LORA_OK : LORA_ERR_CUDA;
 }
 
