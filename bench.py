@@ -129,6 +129,32 @@ class ClockSampler:
         except (OSError, FileNotFoundError):
             self.proc = None
 
+    def _rows(self):
+        rows = []
+        try:
+            for line in open(self.path):
+                parts = [s.strip() for s in line.split(",")]
+                if len(parts) >= 9:
+                    rows.append(parts)
+        except OSError:
+            pass
+        return rows
+
+    def wait_first(self, timeout: float = 5.0):
+        """Block until nvidia-smi has written its first sample (it can take
+        longer to start than a short timed region lasts); samples taken before
+        this point are left out of the statistics."""
+        self.skip = 0
+        if self.proc is None:
+            return
+        t0 = time.time()
+        while time.time() - t0 < timeout:
+            n = len(self._rows())
+            if n:
+                self.skip = n
+                return
+            time.sleep(0.02)
+
     def stop(self):
         if self.proc is None:
             return None
@@ -137,15 +163,14 @@ class ClockSampler:
             self.proc.wait(timeout=5)
         except subprocess.TimeoutExpired:
             self.proc.kill()
-        rows = []
-        for line in open(self.path):
-            parts = [s.strip() for s in line.split(",")]
-            if len(parts) >= 9:
-                rows.append(parts)
+        rows = self._rows()
         try:
             self.path.unlink()
         except OSError:
             pass
+        skip = getattr(self, "skip", 0)
+        if len(rows) > skip:
+            rows = rows[skip:]  # the samples taken during the timed region
         if not rows:
             return None
         sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
@@ -212,6 +237,7 @@ def run_gpu(args):
         dist.barrier()
     torch.cuda.synchronize()
     clocks.start()
+    clocks.wait_first()
     start.record()
     for s in range(args.steps):
         step(ev[s])
