@@ -483,6 +483,51 @@ class _ToyMLP(nn.Module):
         return self.down_proj(torch.nn.functional.silu(self.gate_proj(x)) * self.up_proj(x))
 
 
+class _ToyAttention(nn.Module):
+    """q, k, v read the same x; k and v narrower (grouped-query attention), q and v with biases."""
+
+    def __init__(self, dtype, width=256, kv=128):
+        super().__init__()
+        self.q_proj = _FakeLoraLinear(nn.Linear(width, width, bias=True).to(DEV, dtype), 16, 16, dtype)
+        self.k_proj = _FakeLoraLinear(nn.Linear(width, kv, bias=False).to(DEV, dtype), 8, 16, dtype)
+        self.v_proj = _FakeLoraLinear(nn.Linear(width, kv, bias=True).to(DEV, dtype), 16, 32, dtype)
+
+    def forward(self, x):
+        return self.q_proj(x), self.k_proj(x), self.v_proj(x)
+
+
+def test_peft_grouped_attention():
+    """q/k/v packed into one linear (opt-in): same outputs as the individual
+    forwards, any call order, and an x modified in place between the calls
+    takes the individual path instead of the cached outputs."""
+    import copy
+
+    from probe_b200 import enable_loraforge_peft, peft_plan_report
+
+    torch.manual_seed(11)
+    dtype = torch.bfloat16
+    model = _ToyAttention(dtype).eval()
+    reference = copy.deepcopy(model)
+    enable_loraforge_peft(model, group_attention=True)
+    assert model._loraforge_grouped_attention_count == 1
+    with torch.no_grad():
+        for rows in (1, 8, 200, 300):  # 200 rows with summed rank 40: the individual forwards
+            x = torch.randn(rows, 256, device=DEV, dtype=dtype)
+            for got, want in zip(model(x), reference(x)):
+                rel = float((got.float() - want.float()).abs().max() / want.float().abs().max())
+                assert rel < 4e-2, (rows, rel)
+        x = torch.randn(2, 5, 256, device=DEV, dtype=dtype)
+        v = model.v_proj(x)  # another member first
+        q = model.q_proj(x)
+        assert v.shape == (2, 5, 128) and q.shape == (2, 5, 256)
+        assert float((q.float() - reference.q_proj(x).float()).abs().max()) < 0.1
+        x.add_(1.0)  # in place: the cached k must not be used
+        k = model.k_proj(x)
+        want = reference.k_proj(x)
+        assert float((k.float() - want.float()).abs().max() / want.float().abs().max()) < 4e-2
+    assert peft_plan_report(model)["grouped_attention_modules"] == 1
+
+
 def test_peft_bridge():
     from probe_b200 import enable_loraforge_peft, peft_plan_report
 
