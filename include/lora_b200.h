@@ -188,9 +188,9 @@ LORA_API int lora_decode_linear(const void* x, int64_t ldx, const void* w, int64
  * (z never written to memory).  M <= 256, R <= 128; K, ldx, ldw, lda
  * multiples of 8 and x, w, a 16-byte aligned, else LORA_ERR_UNSUPPORTED (use
  * lora_shrink + lora_decode_linear).
- * Up to 128 tokens (and ranks above 32) run the W-streaming skinny kernel,
+ * Up to 128 tokens (and ranks above 64) run the W-streaming skinny kernel,
  * where scale * z enters the expand as a hi/lo pair of the input dtype.  Above
- * 128 tokens with R <= 32 a split-K CTA-pair kernel runs instead (256-token
+ * 128 tokens with R <= 64 a split-K CTA-pair kernel runs instead (256-token
  * tiles, K split over a cluster, z kept in fp32); it exchanges partial tiles
  * through `workspace`, which must hold lora_linear_small_workspace_size(M, N, R)
  * bytes (16-byte aligned) and must not be used by a concurrent launch.  With a

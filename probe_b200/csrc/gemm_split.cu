@@ -1,6 +1,6 @@
 // Split-K CTA-pair LoRA linear for outputs with few 256x256 tiles (128 < M <= 256).
 //
-//   out[M,N] = x[M,K] . W[N,K]^T + bias[N] + scale * (x . A[R,K]^T) . B[N,R]^T   (R <= 32)
+//   out[M,N] = x[M,K] . W[N,K]^T + bias[N] + scale * (x . A[R,K]^T) . B[N,R]^T   (R <= 64)
 //
 // A 256x4096 output (the reference's single fused linear at 256 tokens,
 // fused_linear.py:296-317 / :652-677 for a 256-row batch) has only 16 tiles of
@@ -9,12 +9,12 @@
 // N = 256 output columns) for each of S contiguous K slices.
 //
 //   warp 0      TMA producer: per k-block this CTA's 128 x-rows, its 128 W-rows
-//               and (R > 0) its 16 lora_A rows, 128-byte swizzle
+//               and (R > 0) its 16 (32 for R > 32) lora_A rows, 128-byte swizzle
 //   warp 1      MMA issuer in the even CTA of each pair: D (256x256, TMEM
-//               columns 0..255) and the shrink D2 = x . A^T (256x32, columns
-//               256..287) from the same x tile; then the expand of this K
-//               slice, D += [hi | lo](scale * D2) . [B | B]^T, as two or four
-//               more MMAs (the expand is linear, so each slice adds its own
+//               columns 0..255) and the shrink D2 = x . A^T (256x32 or
+//               256x64, columns from 256) from the same x tile; then the
+//               expand of this K slice, D += [hi | lo](scale * D2) . [B | B]^T,
+//               as two, four or eight more MMAs (the expand is linear, so each slice adds its own
 //               part and no shrink partial ever leaves its CTA)
 //   warps 2..5  epilogue, one thread per accumulator row; they stage [B | B]
 //               in the swizzled operand layout while the mainloop runs
@@ -55,8 +55,15 @@ namespace {
 
 constexpr int kSpThreads = 192;
 constexpr int kSpBK = 64;
-constexpr int kSpStages = 6;
-constexpr int kSpZN = 32;  // N of the shrink MMA (16 lora_A rows per CTA of the pair)
+// Pipeline depth and shrink width by the fused rank RZ: N of the shrink MMA
+// is 32 (16 lora_A rows per CTA of the pair), 64 for ranks above 32, where the
+// wider stages and two-atom expand operands leave room for 5 stages.
+template <int RZ>
+struct SplitCfg {
+  static constexpr int kStages = RZ > 32 ? 5 : 6;
+  static constexpr int kZN = RZ > 32 ? 64 : 32;
+  static constexpr int kAtoms = RZ > 32 ? 2 : 1;  // 64-wide K atoms of [hi | lo] and [B | B]
+};
 
 struct SplitArgs {
   void* out;
@@ -75,18 +82,19 @@ template <int S, int RZ>
 struct SplitSmem {
   static constexpr int kX = 128 * kSpBK * 2;
   static constexpr int kW = 128 * kSpBK * 2;
-  static constexpr int kA = RZ > 0 ? (kSpZN / 2) * kSpBK * 2 : 0;
+  static constexpr int kStages = SplitCfg<RZ>::kStages;
+  static constexpr int kA = RZ > 0 ? (SplitCfg<RZ>::kZN / 2) * kSpBK * 2 : 0;
   static constexpr int kStage = kX + kW + kA;  // multiple of 1024 (swizzle atoms stay aligned)
   // K split j owns output columns [col_lo(j), col_lo(j + 1)): the 16 groups of
   // 16 columns divided as evenly as S allows (S = 3: 80, 80, 96 columns).
   static constexpr LORA_DEVINL int col_lo(int j) { return (16 * j / S) * 16; }
   static constexpr int kCols = ((16 + S - 1) / S) * 16;  // widest owned slice
-  static constexpr int kMain = kSpStages * kStage;
+  static constexpr int kMain = kStages * kStage;
   // Expand operands (R > 0), 128 rows x 128 bytes each in the 128-byte swizzle
   // layout: [B | B | 0] for this CTA's 128 output columns after the stage
   // buffers, [hi | lo | 0](scale * z) for its 128 rows in the last 16 KB of the
   // stage buffers (free once the mainloop's MMAs are complete).
-  static constexpr int kTile = 128 * 128;
+  static constexpr int kTile = 128 * 128 * SplitCfg<RZ>::kAtoms;  // atoms 16 KB apart
   static constexpr int kBt = kMain;
   static constexpr int kZt = kMain - kTile;
   static constexpr int kBarOffset = kMain + (RZ > 0 ? kTile : 0);
@@ -123,7 +131,7 @@ LORA_DEVINL void store_row16(T* out_row, int col0, int N, bool vec_ok, const flo
   }
 }
 
-// RZ = 0: plain linear; RZ = 16 / 32: fused shrink of rank <= RZ.
+// RZ = 0: plain linear; RZ = 16 / 32 / 64: fused shrink of rank <= RZ.
 template <int S, int RZ, typename T>
 __global__ void __launch_bounds__(kSpThreads, 1)
     gemm_split_pair_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_w,
@@ -134,6 +142,8 @@ __global__ void __launch_bounds__(kSpThreads, 1)
   constexpr uint32_t kTmemCols = 512;
   constexpr int kBf = std::is_same<T, __nv_bfloat16>::value ? 1 : 0;
   constexpr uint32_t kIdesc = umma_idesc_f16(256, 256, kBf);
+  constexpr int kSpStages = L::kStages;
+  constexpr int kSpZN = SplitCfg<RZ>::kZN;
   constexpr uint32_t kIdescZ = umma_idesc_f16(256, kSpZN, kBf);
 
   extern __shared__ uint8_t smem_raw[];
@@ -263,11 +273,13 @@ __global__ void __launch_bounds__(kSpThreads, 1)
         // this slice's expand: D += [hi | lo](scale * z_s) . [B | B]^T, K = 2 * RZ
         fence_acq_rel_cluster();  // both CTAs' operand writes (released by their arrivals) are visible
         tc_fence_after();
-        const uint64_t adesc = umma_desc_sw128(smem_u32(smem + L::kZt));
-        const uint64_t bdesc = umma_desc_sw128(smem_u32(smem + L::kBt));
-        for (int k = 0; k < 2 * RZ / 16; ++k)
-          tc_mma_f16_pair(tmem_base, adesc + static_cast<uint64_t>(2 * k), bdesc + static_cast<uint64_t>(2 * k),
+        for (int k = 0; k < 2 * RZ / 16; ++k) {
+          const int atom = k >> 2, kk = k & 3;
+          const uint64_t adesc = umma_desc_sw128(smem_u32(smem + L::kZt + atom * 16384));
+          const uint64_t bdesc = umma_desc_sw128(smem_u32(smem + L::kBt + atom * 16384));
+          tc_mma_f16_pair(tmem_base, adesc + static_cast<uint64_t>(2 * kk), bdesc + static_cast<uint64_t>(2 * kk),
                           kIdesc, 1u);
+        }
         tc_commit_pair(exp_full, pair_mask);
       }
     }
@@ -286,9 +298,8 @@ __global__ void __launch_bounds__(kSpThreads, 1)
       T vals[RZ];
 #pragma unroll
       for (int j = 0; j < RZ; ++j) vals[j] = (n < args.N && j < args.R) ? brow[j] : from_f32<T>(0.f);
-      uint8_t* bt = smem + L::kBt + r * 128;
 #pragma unroll
-      for (int c = 0; c < 8; ++c) {
+      for (int c = 0; c < 8 * SplitCfg<RZ>::kAtoms; ++c) {  // 16-byte chunk c: K = 8c .. 8c + 7
         uint32_t w[4];
 #pragma unroll
         for (int e = 0; e < 4; ++e) {
@@ -297,7 +308,8 @@ __global__ void __launch_bounds__(kSpThreads, 1)
           const float hi = k0 + 1 < 2 * RZ ? to_f32(vals[(k0 + 1) % RZ]) : 0.f;
           w[e] = pack2<T>(lo, hi);
         }
-        *reinterpret_cast<uint4*>(bt + ((c ^ (r & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
+        uint8_t* bt = smem + L::kBt + (c >> 3) * 16384 + r * 128;
+        *reinterpret_cast<uint4*>(bt + (((c & 7) ^ (r & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
       }
       fence_proxy_async_smem();
     }
@@ -324,16 +336,16 @@ __global__ void __launch_bounds__(kSpThreads, 1)
           part[j] = h;
           part[RZ + j] = z[j] - h;
         }
-        uint8_t* zt = smem + L::kZt + row_local * 128;
 #pragma unroll
-        for (int c = 0; c < 8; ++c) {
+        for (int c = 0; c < 8 * SplitCfg<RZ>::kAtoms; ++c) {
           uint32_t w[4];
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
             const int k0 = c * 8 + 2 * e;
             w[e] = pack2<T>(k0 < 2 * RZ ? part[k0] : 0.f, k0 + 1 < 2 * RZ ? part[k0 + 1] : 0.f);
           }
-          *reinterpret_cast<uint4*>(zt + ((c ^ (row_local & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
+          uint8_t* zt = smem + L::kZt + (c >> 3) * 16384 + row_local * 128;
+          *reinterpret_cast<uint4*>(zt + (((c & 7) ^ (row_local & 7)) << 4)) = make_uint4(w[0], w[1], w[2], w[3]);
         }
         fence_proxy_async_smem();
         tc_fence_before();
@@ -497,38 +509,47 @@ int resident_clusters(int dev) {
 
 template <int RZ>
 int resident_for(int S, int dtype, int dev) {
-  if (dtype == LORA_BF16)
-    return S == 4 ? resident_clusters<4, RZ, __nv_bfloat16>(dev)
-                  : (S == 3 ? resident_clusters<3, RZ, __nv_bfloat16>(dev) : resident_clusters<2, RZ, __nv_bfloat16>(dev));
-  return S == 4 ? resident_clusters<4, RZ, __half>(dev)
-                : (S == 3 ? resident_clusters<3, RZ, __half>(dev) : resident_clusters<2, RZ, __half>(dev));
+  if (dtype == LORA_BF16) {
+    if (S == 4) return resident_clusters<4, RZ, __nv_bfloat16>(dev);
+    if (S == 3) return resident_clusters<3, RZ, __nv_bfloat16>(dev);
+    if (S == 2) return resident_clusters<2, RZ, __nv_bfloat16>(dev);
+    return resident_clusters<1, RZ, __nv_bfloat16>(dev);
+  }
+  if (S == 4) return resident_clusters<4, RZ, __half>(dev);
+  if (S == 3) return resident_clusters<3, RZ, __half>(dev);
+  if (S == 2) return resident_clusters<2, RZ, __half>(dev);
+  return resident_clusters<1, RZ, __half>(dev);
 }
 
 int resident(int S, int rz, int dtype, int dev) {
   if (rz == 0) return resident_for<0>(S, dtype, dev);
   if (rz == 16) return resident_for<16>(S, dtype, dev);
-  return resident_for<32>(S, dtype, dev);
+  if (rz == 32) return resident_for<32>(S, dtype, dev);
+  return resident_for<64>(S, dtype, dev);
 }
 
 // K slices for a launch, or 0 (use another kernel): the most slices (4, 3, 2)
 // whose 2 x S CTAs per tile fit the machine with every cluster resident in one
 // wave (a second wave costs a whole extra mainloop), each slice keeping at
-// least 8 k-blocks.  LORA_B200_SPLIT_PAIR=0/2/3/4 forces the choice (for
-// tuning sweeps).
+// least 8 k-blocks.  Wider outputs take one slice (no exchange), in as many
+// waves of resident pairs as their tiles need: each wave costs about one
+// 256 x 256 tile's mainloop, still well under the W-streaming kernel's time
+// at these token counts.  LORA_B200_SPLIT_PAIR=0/1/2/3/4 forces the choice
+// (for tuning sweeps).
 int plan_slices(int64_t M, int64_t N, int64_t num_kb, int rz, int dtype, int dev, int num_sms) {
   if (M <= 0 || N <= 128 || num_kb <= 0) return 0;
   const int64_t tiles = ((M + 255) / 256) * ((N + 255) / 256);
   if (tiles > 65535) return 0;
   const int forced = env_slices();
   if (forced == 0) return 0;
-  if (forced >= 2 && forced <= 4)  // at least S k-blocks per slice, so that no slice is empty
+  if (forced >= 1 && forced <= 4)  // at least S k-blocks per slice, so that no slice is empty
     return (num_kb >= forced * forced && resident(forced, rz, dtype, dev) > 0) ? forced : 0;
   for (int S : {4, 3, 2}) {
     if (tiles * 2 * S > num_sms || num_kb < 8 * S) continue;
     if (tiles > resident(S, rz, dtype, dev)) continue;
     return S;
   }
-  return 0;
+  return (num_kb >= 8 && resident(1, rz, dtype, dev) > 0) ? 1 : 0;
 }
 
 template <int S, int RZ, typename T>
@@ -551,7 +572,8 @@ int launch_s(int S, const CUtensorMap& tx, const CUtensorMap& tw, const CUtensor
              int tiles, cudaStream_t stream) {
   if (S == 4) return launch_t<4, RZ, T>(tx, tw, ta, a, tiles, stream);
   if (S == 3) return launch_t<3, RZ, T>(tx, tw, ta, a, tiles, stream);
-  return launch_t<2, RZ, T>(tx, tw, ta, a, tiles, stream);
+  if (S == 2) return launch_t<2, RZ, T>(tx, tw, ta, a, tiles, stream);
+  return launch_t<1, RZ, T>(tx, tw, ta, a, tiles, stream);
 }
 
 template <int RZ>
@@ -567,10 +589,10 @@ size_t ws_bytes_s(int64_t tiles) {
 }
 
 size_t ws_bytes(int S, int64_t tiles) {
-  return S == 4 ? ws_bytes_s<4>(tiles) : (S == 3 ? ws_bytes_s<3>(tiles) : ws_bytes_s<2>(tiles));
+  return S == 4 ? ws_bytes_s<4>(tiles) : (S == 3 ? ws_bytes_s<3>(tiles) : (S == 2 ? ws_bytes_s<2>(tiles) : 0));
 }
 
-int rz_for(int64_t R) { return R <= 0 ? 0 : (R <= 16 ? 16 : 32); }
+int rz_for(int64_t R) { return R <= 0 ? 0 : (R <= 16 ? 16 : (R <= 32 ? 32 : 64)); }
 
 }  // namespace
 
@@ -600,9 +622,9 @@ int launch_linear_split(const void* x, int64_t ldx, const void* w, int64_t ldw, 
   CUtensorMap tx, tw, ta;
   if (!encode_map(&tx, x, dtype, K, M, ldx, kSpBK, 128)) return LORA_ERR_CUDA;
   if (!encode_map(&tw, w, dtype, K, N, ldw, kSpBK, 128)) return LORA_ERR_CUDA;
-  // lora_A [R, K]: 16 rows per CTA of the pair, rows >= R zero-filled
+  // lora_A [R, K]: RZ / 2 rows per CTA of the pair, rows >= R zero-filled
   if (R > 0) {
-    if (!encode_map(&ta, a, dtype, K, R, lda, kSpBK, kSpZN / 2)) return LORA_ERR_CUDA;
+    if (!encode_map(&ta, a, dtype, K, R, lda, kSpBK, rz > 32 ? 32 : 16)) return LORA_ERR_CUDA;
   } else {
     ta = tx;
   }
@@ -624,7 +646,8 @@ int launch_linear_split(const void* x, int64_t ldx, const void* w, int64_t ldw, 
   args.scale = scale;
   if (rz == 0) return launch_rz<0>(dtype, S, tx, tw, ta, args, tiles, stream);
   if (rz == 16) return launch_rz<16>(dtype, S, tx, tw, ta, args, tiles, stream);
-  return launch_rz<32>(dtype, S, tx, tw, ta, args, tiles, stream);
+  if (rz == 32) return launch_rz<32>(dtype, S, tx, tw, ta, args, tiles, stream);
+  return launch_rz<64>(dtype, S, tx, tw, ta, args, tiles, stream);
 }
 
 }  // namespace lora

@@ -10,14 +10,14 @@
 
 namespace lora {
 
-constexpr int kSplitMaxRank = 32;  // fused shrink: lora_A rows held in the second accumulator
+constexpr int kSplitMaxRank = 64;  // fused shrink: lora_A rows held in the second accumulator
 
 // Workspace the split kernel may need for this shape (0 if it never runs it).
 size_t split_pair_workspace_bytes(int64_t M, int64_t N, int64_t R);
 
 // out = x . W^T + bias + scale * (x . A^T) . B^T with the shrink accumulated
 // beside the base tile and the expand applied to each owned column slice in
-// fp32 (A = lora_A [R, K], B = lora_B [N, R] with row pitch ldb, R <= 32;
+// fp32 (A = lora_A [R, K], B = lora_B [N, R] with row pitch ldb, R <= 64;
 // R == 0: the plain linear).  Returns LORA_ERR_UNSUPPORTED when the shape,
 // alignment or workspace is outside this kernel, or another kernel fits it
 // better.

@@ -308,8 +308,8 @@ def _patch_grouped_siblings(parent, names, tag: str) -> bool:
             if not x2.is_contiguous():
                 x2 = x2.contiguous()
             rows = x2.shape[0]
-            if 128 < rows <= 256 and r_all > 32:
-                # the one-launch split-K linear of this row range takes ranks <= 32
+            if 128 < rows <= 256 and r_all > 64:
+                # the one-launch split-K linear of this row range takes ranks <= 64
                 # only: the individual projections measured faster here than the
                 # pack with its summed rank
                 return individual[i](x, *args, **kwargs)

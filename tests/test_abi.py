@@ -38,10 +38,11 @@ def test_workspace_sizes_are_host_only(lib):
     assert lib.lora_shrink_workspace_size(64, 16, 1) == 256
     assert lib.lora_shrink_workspace_size(64, 16, 4) >= 4 * 64 * 16 * 4
     assert lib.lora_decode_workspace_size(8, 11008, 3) >= 3 * 8 * 11008 * 4
-    # split-K pair kernel: only above 128 tokens and for ranks <= 32
+    # split-K pair kernel: only above 128 tokens and for ranks <= 64
     assert lib.lora_linear_small_workspace_size(256, 4096, 16) >= 16 * 2 * 4 * 3 * 128 * 64 * 4
     assert lib.lora_linear_small_workspace_size(128, 4096, 16) == 0
-    assert lib.lora_linear_small_workspace_size(256, 4096, 40) == 0
+    assert lib.lora_linear_small_workspace_size(256, 4096, 40) == lib.lora_linear_small_workspace_size(256, 4096, 16)
+    assert lib.lora_linear_small_workspace_size(256, 4096, 65) == 0
     assert lib.lora_sgmv_tiles_size(4096, 128) >= 4 * (2 + 2 * (64 + 128 + 1))
 
 

@@ -511,7 +511,7 @@ def test_peft_grouped_attention():
     enable_loraforge_peft(model, group_attention=True)
     assert model._loraforge_grouped_attention_count == 1
     with torch.no_grad():
-        for rows in (1, 8, 200, 300):  # 200 rows with summed rank 40: the individual forwards
+        for rows in (1, 8, 200, 300):  # 200 rows, summed rank 40: the split-K linear at rank 64
             x = torch.randn(rows, 256, device=DEV, dtype=dtype)
             for got, want in zip(model(x), reference(x)):
                 rel = float((got.float() - want.float()).abs().max() / want.float().abs().max())

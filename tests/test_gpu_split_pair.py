@@ -1,12 +1,14 @@
 """Split-K CTA-pair GEMM (GPU): few 256x256 output tiles, K split over a cluster.
 
-Reached through lora_linear_small for 128 < M <= 256 with rank <= 32 (the
+Reached through lora_linear_small for 128 < M <= 256 with rank <= 64 (the
 shrink accumulated beside the base tile, the partial tiles exchanged through
 the caller's workspace).  Each case is checked against the float64 oracle
 (oracle/lora_oracle.py); the slice count is forced both ways through
-LORA_B200_SPLIT_PAIR so that the 2-, 3- and 4-slice reductions all run.  Shapes
+LORA_B200_SPLIT_PAIR so that the 2-, 3- and 4-slice reductions and the
+single-slice form (no exchange; chosen on its own for wide outputs) all run.  Shapes
 cover partial token tiles (M not a multiple of 256), output widths that are
-not multiples of 256 or of 8, ranks 1, 16, 17 and 32, bias and no bias, fp16.
+not multiples of 256 or of 8, ranks 1, 16, 17, 32, 48 and 64 (the wider
+shrink accumulator), bias and no bias, fp16.
 """
 
 import math
@@ -30,9 +32,10 @@ def _case(m, n, k, r, dtype, seed):
     return x, w, bias, a, b
 
 
-@pytest.mark.parametrize("slices", ["2", "3", "4", ""])
+@pytest.mark.parametrize("slices", ["1", "2", "3", "4", ""])
 @pytest.mark.parametrize("m,n,k,r", [(256, 4096, 4096, 16), (129, 1000, 2048, 1), (200, 1002, 1024, 17),
-                                     (256, 512, 4096, 32), (160, 4096, 1536, 0)])
+                                     (256, 512, 4096, 32), (160, 4096, 1536, 0), (256, 4096, 4096, 64),
+                                     (231, 1000, 2048, 48), (129, 4096, 1024, 33), (256, 12288, 1024, 48)])
 def test_linear_split_fused_shrink(monkeypatch, slices, m, n, k, r):
     monkeypatch.setenv("LORA_B200_SPLIT_PAIR", slices)
     dtype = torch.bfloat16
@@ -42,6 +45,33 @@ def test_linear_split_fused_shrink(monkeypatch, slices, m, n, k, r):
     want = orc.naive_linear(np64(x), np64(w), np64(bias), np64(a) if r else None, np64(b) if r else None, 1.7)
     assert_parity(out, want, dtype)
     assert torch.equal(out, kernels.linear_small(x, w, a, b, bias, 1.7))  # deterministic reduction
+    assert _lib.device_error() == 0
+
+
+def test_linear_split_single_slice_waves():
+    """An output of 112 tiles of 256 x 256: more CTA pairs than SMs, so the
+    single-slice form runs in two waves."""
+    m, n, k, r = 256, 28672, 1024, 16
+    dtype = torch.bfloat16
+    x, w, bias, a, b = _case(m, n, k, r, dtype, seed=21)
+    out = kernels.linear_small(x, w, a, b, bias, 0.75)
+    assert out is not None
+    want = orc.naive_linear(np64(x), np64(w), np64(bias), np64(a), np64(b), 0.75)
+    assert_parity(out, want, dtype)
+    assert _lib.device_error() == 0
+
+
+def test_linear_split_rank64_fp16_strided():
+    """fp16 at rank 64 (two 64-wide K atoms in the expand), lora_B with a row
+    pitch wider than its rank, no bias."""
+    m, n, k, r = 256, 1536, 4096, 64
+    dtype = torch.float16
+    x, w, _, a, _ = _case(m, n, k, r, dtype, seed=9)
+    b = randn((n, 72), 1 / math.sqrt(r), dtype, seed=10)[:, :r]
+    res = kernels.linear_small(x, w, a, b, None, 0.25)
+    assert res is not None
+    want = orc.naive_linear(np64(x), np64(w), None, np64(a), np64(b), 0.25)
+    assert_parity(res, want, dtype)
     assert _lib.device_error() == 0
 
 
