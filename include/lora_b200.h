@@ -15,7 +15,16 @@
  *     goes on it and no entry point synchronises the host;
  *   - the return value is a lora_status; no exception crosses the ABI;
  *   - dtype is LORA_F16 or LORA_BF16 for activations and weights; some
- *     intermediate z buffers may be LORA_F32 where stated.
+ *     intermediate z buffers may be LORA_F32 where stated;
+ *   - most kernels launch with programmatic dependent launch and may start
+ *     while the kernel launched just before them on `stream` is still running.
+ *     Until that kernel has completed they read only weights (w, a, b,
+ *     lora_A / lora_B tables, offsets, ranks); activations, z, tile tables and
+ *     every write come after.  So a kernel that WRITES a weight must not be the
+ *     launch immediately before an entry point that reads it (any other launch,
+ *     an event wait or a synchronisation in between is enough), or set the
+ *     environment variable LORA_B200_PDL=0 (read once per process) for plain
+ *     stream order throughout.
  *
  * Each declaration names the reference function (lishenghui/probe,
  * loraforge_kernels/, file:line) whose GPU work it replaces.

@@ -66,6 +66,11 @@ __global__ void __launch_bounds__(128) decode_kernel(const DecodeArgs p) {
   const T* x = static_cast<const T*>(p.x);
   const T* w = static_cast<const T*>(p.w);
 
+  // Launched with programmatic serialization: x (and z for the tail) may be
+  // written by the kernel launched just before this one, so the kernel waits
+  // for it before its first global access.
+  pdl_wait();
+
   // ---- stage x[:, k0:k1) (zero padded to TG*8 tokens and 64 columns)
   for (int idx = threadIdx.x; idx < TG * 8 * (kmain / 8); idx += blockDim.x) {
     const int m = idx / (kmain / 8);
@@ -171,7 +176,6 @@ __global__ void __launch_bounds__(128) decode_kernel(const DecodeArgs p) {
 
   // ---- LoRA tail on the last split: [hi(s.z) | lo(s.z)] against [B | B]
   if (has_tail) {
-    pdl_wait();  // z may come from the kernel launched just before this one
     const int r16 = p.r16;
     const int tcols = (2 * r16 + 63) & ~63;
     __syncthreads();
@@ -285,7 +289,7 @@ int launch_decode_tg(const DecodeArgs& p, dim3 grid, size_t smem, cudaStream_t s
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
   return cudaLaunchKernelEx(&cfg, kernel, p) == cudaSuccess ? LORA_OK : LORA_ERR_CUDA;
 }
 

@@ -563,7 +563,7 @@ int launch_t(const CUtensorMap& tx, const CUtensorMap& tw, const CUtensorMap& ta
   cudaLaunchConfig_t cfg = make_config<S, RZ, T>(tiles, stream, attr);
   attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[1].val.programmaticStreamSerializationAllowed = 1;
-  cfg.numAttrs = 2;
+  cfg.numAttrs = pdl_enabled() ? 2 : 1;
   return cudaLaunchKernelEx(&cfg, kernel, tx, tw, ta, a) == cudaSuccess ? LORA_OK : LORA_ERR_CUDA;
 }
 

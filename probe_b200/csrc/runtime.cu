@@ -1,4 +1,5 @@
 // Host runtime: device cache, error word, status strings, driver entry points.
+#include <cstdlib>
 #include <mutex>
 
 #include "common.cuh"
@@ -11,6 +12,14 @@ constexpr int kMaxDevices = 64;
 std::once_flag g_dev_once[kMaxDevices];
 DeviceInfo g_dev[kMaxDevices];
 }  // namespace
+
+bool pdl_enabled() {
+  static const bool on = [] {
+    const char* v = std::getenv("LORA_B200_PDL");
+    return !(v != nullptr && v[0] == '0');
+  }();
+  return on;
+}
 
 int current_device() {
   int dev = -1;

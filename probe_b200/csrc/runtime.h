@@ -29,4 +29,12 @@ PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder();
 
 int gemm_pick_bn(int64_t M, int64_t N, int num_sms);
 
+// Programmatic dependent launch for the kernels that support it (default on).
+// Such a kernel may start while the kernel launched just before it on the
+// stream is still running: it reads weights (W, lora_A, lora_B, the adapter
+// tables) before griddepcontrol.wait and activations, z, the tile table and
+// every global write after it.  LORA_B200_PDL=0 launches every kernel in plain
+// stream order (read once per process).
+bool pdl_enabled();
+
 }  // namespace lora

@@ -332,10 +332,11 @@ __global__ void __launch_bounds__(128) sgmv_expand_block_kernel(const SgmvExpand
   const int row_a = 16 * warp + g, row_b = row_a + 8;
 
   // Launched with programmatic serialization behind the shrink that writes z:
-  // the tile table (read-only tables) is built first, y, z and the rows table
-  // after griddepcontrol.wait, every global write after that.
-  load_block_tiles(bt, p.tiles, p.offsets, p.ranks, p.R, block, tbase, ntok);
+  // the kernel waits for it before its first global read (the tile table may
+  // come from a schedule launched just before, z from the shrink), so only its
+  // set-up overlaps the kernel before it.
   pdl_wait();
+  load_block_tiles(bt, p.tiles, p.offsets, p.ranks, p.R, block, tbase, ntok);
 
   // ---- y of the block (rows (tid >> 4) + 8 i, chunk tid & 15)
   const int ch = tid & 15;
@@ -486,7 +487,7 @@ int launch_shrink_nt(const SgmvShrinkBlockArgs& p, dim3 grid, cudaStream_t s) {
   attr[0].val.clusterDim.y = grid.y;
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
   return cudaLaunchKernelEx(&cfg, kernel, p) == cudaSuccess ? LORA_OK : LORA_ERR_CUDA;
 }
 

@@ -130,13 +130,14 @@ __global__ void __launch_bounds__(kTcThreads, 1) sgmv_shrink_tc_kernel(const __g
   // Launched with programmatic serialization behind the schedule: barriers and
   // TMEM are set up while it finishes; every global read of the table, x and
   // a_flat comes after griddepcontrol.wait (the producer's loads follow the
-  // table through the block barrier).  The expand launched next may start its
-  // own set-up at once.
-  if (threadIdx.x == 0) pdl_launch_dependents();
+  // table through the block barrier).  Dependents are signalled only after
+  // that wait: the expand launched next reads the tile table before its own
+  // wait, so the schedule that wrote it must be complete by then.
 
   // ---- tile table of the block (warps 2..5), barriers (thread 0), TMEM (warp 1)
   if (warp >= 2) {
     pdl_wait();
+    if (threadIdx.x == 64) pdl_launch_dependents();
     const int et = threadIdx.x - 64;
     const int nt_all = sgmv_num_tiles(p.tiles);
     const int32_t* first = sgmv_block_first(p.tiles);
@@ -447,7 +448,7 @@ int launch_tc_t(const CUtensorMap& tx, const TcAMaps& ta, const SgmvTcArgs& p, d
   attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 2;
+  cfg.numAttrs = pdl_enabled() ? 2 : 1;
   return cudaLaunchKernelEx(&cfg, kernel, tx, ta, p) == cudaSuccess ? LORA_OK : LORA_ERR_CUDA;
 }
 

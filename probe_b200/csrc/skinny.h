@@ -23,8 +23,8 @@ struct SkinnyArgs {
   int rotate;    // start each band's K slice at a different k-block
   int kgroup;    // stages filled together (W boxes interleaved across their k-blocks)
   int box_rows;  // rows per W box
-  int early;     // launched with programmatic serialization: weights of the first stages load before
-                 // griddepcontrol.wait, x and every global write after it
+  int early;     // signal dependents at the start (forms without a z input); every form loads the
+                 // weights of its first stages before griddepcontrol.wait, x and every global write after it
   float scale;
 };
 

@@ -194,8 +194,8 @@ __global__ void __launch_bounds__(kSkThreads, 1) skinny_linear_kernel(const __gr
       const int kg = p.kgroup, br = p.box_rows;
       bool ok = true;
       int i0 = 0;
-      if (p.early && kg == 1) {
-        // Launched behind another linear: the weights (W, lora_A) of the first
+      if (kg == 1) {
+        // Launched behind another kernel: the weights (W, lora_A) of the first
         // stages load before the grid dependency resolves, x after it.
         const int npre = min(L.stages, n_main);
         for (int j = 0; j < npre; ++j) {
@@ -213,7 +213,7 @@ __global__ void __launch_bounds__(kSkThreads, 1) skinny_linear_kernel(const __gr
         stage = npre % L.stages;
         phase = npre == L.stages ? 1u : 0u;
         i0 = npre;
-      } else if (p.early) {
+      } else {
         pdl_wait();
       }
       for (int i = i0; ok && i < n_main; i += kg) {
@@ -834,12 +834,12 @@ int launch_skinny_linear(const void* x, int64_t ldx, const void* w, int64_t ldw,
   if (bands > INT32_MAX || ttiles > 65535) return LORA_ERR_SHAPE;
   dim3 grid(static_cast<unsigned>(bands), static_cast<unsigned>(split), static_cast<unsigned>(ttiles));
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  // Every form runs with programmatic serialization: the z-consuming form waits
-  // before reading z (the shrink launched just before it); the others prefetch
-  // the weights of their first stages before waiting and signal their own
-  // dependents at once.
+  // Every form runs with programmatic serialization: the weights of the first
+  // stages load before griddepcontrol.wait, x after it, and the z-consuming
+  // form's epilogue waits again before reading z (the shrink launched just
+  // before it).  The forms without a z input signal their own dependents at once.
   p.early = (fuse || R == 0) ? 1 : 0;
-  const bool pdl = true;
+  const bool pdl = pdl_enabled();
   if (dtype == LORA_BF16) return launch_t<__nv_bfloat16>(nb, tw, tx, ta, p, grid, L.bytes, pdl, s);
   return launch_t<__half>(nb, tw, tx, ta, p, grid, L.bytes, pdl, s);
 }
