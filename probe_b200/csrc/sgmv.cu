@@ -82,13 +82,17 @@ struct AdapterLookup {
 }  // namespace
 
 __global__ void __launch_bounds__(1024) sgmv_schedule_kernel(AdapterLookup look, int32_t* tiles, int max_tiles) {
-  __shared__ int scan[1024];
+  __shared__ int warp_sum[32];
   __shared__ int s_start[kSchedSmemSegs + 1];
   __shared__ int s_adapter[kSchedSmemSegs];
   const int tid = threadIdx.x, nth = blockDim.x;
+  const int lane = tid & 31, warp = tid >> 5, nwarps = nth >> 5;
   const int T = look.T;
-  // the segmented shrink launched next may set up (barriers, TMEM) meanwhile;
-  // it waits for this grid before reading the table
+  // Launched with programmatic serialization: the segment table (and the tile
+  // buffer, which the kernel before may still read) wait for that kernel.  The
+  // segmented shrink launched next may set up (barriers, TMEM) meanwhile; it
+  // waits for this grid before reading the table.
+  pdl_wait();
   if (tid == 0) pdl_launch_dependents();
   if (look.ids == nullptr && look.S <= kSchedSmemSegs) {
     for (int i = tid; i <= look.S; i += nth) {
@@ -122,16 +126,28 @@ __global__ void __launch_bounds__(1024) sgmv_schedule_kernel(AdapterLookup look,
       pv = a;
     }
   }
-  scan[tid] = count;
-  __syncthreads();
-  for (int off = 1; off < nth; off <<= 1) {
-    const int v = tid >= off ? scan[tid - off] : 0;
-    __syncthreads();
-    scan[tid] += v;
-    __syncthreads();
+  // exclusive scan of the counts: within each warp by shuffles, then over the
+  // warp totals by warp 0 (two block barriers)
+  int incl = count;
+#pragma unroll
+  for (int off = 1; off < 32; off <<= 1) {
+    const int v = __shfl_up_sync(0xffffffffu, incl, off);
+    if (lane >= off) incl += v;
   }
-  const int total = scan[nth - 1];
-  int base = scan[tid] - count;
+  if (lane == 31) warp_sum[warp] = incl;
+  __syncthreads();
+  if (warp == 0) {
+    int w = lane < nwarps ? warp_sum[lane] : 0;
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+      const int v = __shfl_up_sync(0xffffffffu, w, off);
+      if (lane >= off) w += v;
+    }
+    warp_sum[lane] = w;  // inclusive over warps
+  }
+  __syncthreads();
+  const int total = warp_sum[nwarps - 1];
+  int base = incl - count + (warp > 0 ? warp_sum[warp - 1] : 0);
   int32_t* starts = tiles + 2;
   int32_t* adapters = tiles + 3 + max_tiles;
   int32_t* block_first = tiles + 3 + 2 * max_tiles;
@@ -180,6 +196,16 @@ extern "C" int lora_sgmv_schedule(const int64_t* ids, const int64_t* seg_start, 
   AdapterLookup look{ids, seg_start, seg_adapter, nullptr, nullptr, static_cast<int>(T), static_cast<int>(S),
                      static_cast<int>(std::min<int64_t>(n_adapters, INT32_MAX)), device_info(dev).err_word};
   const int64_t mt = sgmv_max_tiles(T, S);
-  sgmv_schedule_kernel<<<1, 1024, 0, static_cast<cudaStream_t>(stream)>>>(look, tiles, static_cast<int>(mt));
-  return cudaGetLastError() == cudaSuccess ? LORA_OK : LORA_ERR_CUDA;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(1);
+  cfg.blockDim = dim3(1024);
+  cfg.stream = static_cast<cudaStream_t>(stream);
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, sgmv_schedule_kernel, look, tiles, static_cast<int>(mt)) == cudaSuccess
+             ? LORA_OK
+             : LORA_ERR_CUDA;
 }
