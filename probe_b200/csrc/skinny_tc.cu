@@ -19,9 +19,11 @@
 // Fused shrink: every stage also brings the k-block of lora_A (r16 rows), and
 // a second set of MMAs (A rows as the 128-row operand, the same x tile as the
 // N operand) accumulates z^T over the CTA's K slice in a second TMEM region.
-// The cluster then sums those partial z tiles through distributed shared
-// memory, and the last CTA turns z into the [hi | lo] operand of its tail --
-// one kernel for base GEMV, shrink and expand; z never leaves the chip.
+// The expand is linear in z, so every CTA of the cluster turns its own partial
+// z (its K slice's share) into the [hi | lo] operand of its own tail, and the
+// partial tiles the cluster adds already carry the whole expand: no z partial
+// crosses the cluster and no CTA waits for another's shrink -- one kernel for
+// base GEMV, shrink and expand; z never leaves the chip.
 //
 // Roles (192 threads): warp 0 TMA producer, warp 1 TMEM owner and MMA issuer,
 // warps 2..5 z staging and epilogue (tcgen05.ld of their 32 TMEM lanes).
@@ -51,8 +53,8 @@ constexpr int kSkABytes = kSkBM * kSkBK * 2;  // 16 KB
 struct SkinnyLayout {
   int nb, stages, rch, r16, fz, cs;
   int b_bytes, at_bytes;                            // x tile, A tile (fused shrink) per stage
-  int rpr, slice_bytes, zpush_bytes;                // rows per owner, partial slice pushed to an owner, z partial
-  int at_off, a_off, b_off, bl_off, z_off, rst_off, zr_off, zst_off, bar_off, bytes;
+  int rpr, slice_bytes, zpush_bytes;                // rows per owner, partial slice pushed to an owner, z partial size
+  int at_off, a_off, b_off, bl_off, z_off, rst_off, zr_off, bar_off, bytes;
   __host__ __device__ SkinnyLayout(int nb_, int stages_, int rch_, int r16_ = 0, int fz_ = 0, int cs_ = 1)
       : nb(nb_), stages(stages_), rch(rch_), r16(r16_), fz(fz_), cs(cs_) {
     b_bytes = nb * kSkBK * 2;
@@ -76,17 +78,16 @@ struct SkinnyLayout {
     slice_bytes = rpr * (nb + 4) * 4;
     rst_off = (red_bytes + 1023) & ~1023;
     const int rst_end = rst_off + (cs - 1) * slice_bytes;
-    // Fused shrink: this CTA's z partial (zr) and, in the last CTA, the other
-    // CTAs' z partials pushed to it (zst) -- written while mainloops still run,
-    // so above everything the mainloop uses.  [r16][nb + 4] (lora_A rows as the
-    // MMA's M), or [128][r16 + 4] with 128-token tiles.
+    // Fused shrink: this CTA's z partial (zr), written after its own mainloop
+    // but while other CTAs' mainloops (and their pushes into rst) may still
+    // run, so above everything the mainloop and rst use.  [r16][nb + 4]
+    // (lora_A rows as the MMA's M), or [128][r16 + 4] with 128-token tiles.
     const int zr_floats = nb == 128 ? kSkBM * (r16 + 4) : r16 * (nb + 4);
     zpush_bytes = fz ? zr_floats * 4 : 0;
     const int zr_bytes = fz ? ((zpush_bytes + 1023) & ~1023) : 0;
     int top = end_a > rst_end ? end_a : rst_end;
     zr_off = (top + 1023) & ~1023;
-    zst_off = zr_off + zr_bytes;
-    bar_off = zst_off + (fz ? (cs - 1) * zr_bytes : 0);
+    bar_off = zr_off + zr_bytes;
     bytes = bar_off + 256 + 1024;                   // barriers, tmem slot, flags + alignment slack
   }
 };
@@ -124,8 +125,7 @@ __global__ void __launch_bounds__(kSkThreads, 1) skinny_linear_kernel(const __gr
   uint64_t* acc_full = empty + 8;
   uint64_t* z_ready = acc_full + 1;
   uint64_t* tail_full = z_ready + 1;
-  uint64_t* zpull = tail_full + 1;  // last CTA: the other CTAs' z partials have arrived
-  uint64_t* rpull = zpull + 1;      // every CTA: the other CTAs' slices of its rows have arrived
+  uint64_t* rpull = tail_full + 1;  // every CTA: the other CTAs' slices of its rows have arrived
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(rpull + 1);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
@@ -136,7 +136,9 @@ __global__ void __launch_bounds__(kSkThreads, 1) skinny_linear_kernel(const __gr
   const int cs = p.split;
   const int kb0 = ks * p.kb_per;
   const int kb1 = min(p.num_kb, kb0 + p.kb_per);
-  const bool tail = (ks == cs - 1) && p.R > 0;
+  // CTAs with a LoRA tail: every K slice with the fused shrink (each expands
+  // its own partial z), only the last one with a z input (the full z, once).
+  const bool tail = (p.fuse || ks == cs - 1) && p.R > 0;
   const int n_main = max(kb1 - kb0, 0);
   // Bands start their K slice at different k-blocks, so the W requests in flight
   // across the grid spread over many column offsets.
@@ -151,14 +153,12 @@ __global__ void __launch_bounds__(kSkThreads, 1) skinny_linear_kernel(const __gr
     mbar_init(acc_full, 1);
     mbar_init(z_ready, 128);
     mbar_init(tail_full, 1);
-    mbar_init(zpull, 1);
     mbar_init(rpull, 1);
     *abort_flag = 0;
     fence_mbar_init();
     // Arm the receive barriers now: peers' bulk pushes may complete their bytes
     // before this CTA reaches its wait.
     if (cs > 1) {
-      if (p.fuse && tail) mbar_arrive_expect_tx(zpull, static_cast<uint32_t>((cs - 1) * L.zpush_bytes));
       const int my_rows = min(kSkBM, (ks + 1) * L.rpr) - min(kSkBM, ks * L.rpr);
       mbar_arrive_expect_tx(rpull, static_cast<uint32_t>((cs - 1) * my_rows * kRS * 4));
     }
@@ -406,43 +406,19 @@ __global__ void __launch_bounds__(kSkThreads, 1) skinny_linear_kernel(const __gr
           }
         }
       }
-      // Every epilogue warp's rows of zred are written before any thread reads
-      // them (the last CTA sums them in phase B, the others push them).
-      fence_proxy_async_smem();
+      // Every epilogue warp's rows of zred are written before any thread
+      // reads them in phase B.
       named_bar_sync(1, 128);
-      if (cs > 1 && !tail) {
-        // push this CTA's z partial into the last CTA's slot [ks]
-        if (threadIdx.x == 64) {
-          const uint32_t last = static_cast<uint32_t>(cs - 1);
-          const uint32_t zr_bytes = static_cast<uint32_t>((L.zpush_bytes + 1023) & ~1023);
-          bulk_push_to_peer(mapa_shared(smem_u32(smem + L.zst_off) + static_cast<uint32_t>(ks) * zr_bytes, last),
-                            smem + L.zr_off, static_cast<uint32_t>(L.zpush_bytes), mapa_shared(smem_u32(zpull), last));
-        }
-      }
     }
   }
 
   // ================================================================ phase B
   if (tail) {
     if (p.fuse && warp >= 2) {
-      // z[t, j] = scale * sum over the cluster (rank order) -> [hi | lo] operand tiles;
-      // the other CTAs' partials were pushed into zst, slot s = rank s
+      // scale * (this K slice's partial z) -> [hi | lo] operand tiles
       const int et = threadIdx.x - 64;
-      if (cs > 1) acc_ok = mbar_wait_bounded(zpull, 0, abort_flag, p.err, kDevErrTimeoutFull) && acc_ok;
       const float* zown = reinterpret_cast<const float*>(smem + L.zr_off);
-      const float* zst = reinterpret_cast<const float*>(smem + L.zst_off);
-      const int zslot = ((L.zpush_bytes + 1023) & ~1023) / 4;  // floats per slot
-      auto zsum4 = [&](int off) {
-        float4 sm = make_float4(0.f, 0.f, 0.f, 0.f);
-        for (int s = 0; s < cs; ++s) {
-          const float4 v = *reinterpret_cast<const float4*>((s == cs - 1 ? zown : zst + s * zslot) + off);
-          sm.x += v.x;
-          sm.y += v.y;
-          sm.z += v.z;
-          sm.w += v.w;
-        }
-        return sm;
-      };
+      auto zsum4 = [&](int off) { return *reinterpret_cast<const float4*>(zown + off); };
       if (kZSwap) {
         // one item = token t, 8 ranks (one 16-byte chunk of the hi and of the lo tile)
         const int items = NB * p.rch * 8;
