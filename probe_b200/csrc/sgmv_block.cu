@@ -487,7 +487,7 @@ int launch_shrink_nt(const SgmvShrinkBlockArgs& p, dim3 grid, cudaStream_t s) {
   attr[0].val.clusterDim.y = grid.y;
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  cfg.numAttrs = 1;
   return cudaLaunchKernelEx(&cfg, kernel, p) == cudaSuccess ? LORA_OK : LORA_ERR_CUDA;
 }
 
@@ -516,7 +516,7 @@ int launch_expand_rz(const SgmvExpandBlockArgs& p, dim3 grid, cudaStream_t s) {
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
   return cudaLaunchKernelEx(&cfg, kernel, p) == cudaSuccess ? LORA_OK : LORA_ERR_CUDA;
 }
 

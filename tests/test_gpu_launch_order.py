@@ -157,7 +157,10 @@ def test_back_to_back_branches_with_different_segments():
 
 
 def test_plain_stream_order_switch_is_read():
-    """LORA_B200_PDL=0 (plain stream order) gives the same bits as the default."""
+    """LORA_B200_PDL=0 (plain stream order) gives the same bits as the default,
+    through the small-M linear, the decode kernel, the schedule, both
+    segmented shrinks (tensor-core, and the cluster block kernel reached with a
+    row indirection) and the segmented expand."""
     import os
     import subprocess
     import sys
@@ -172,7 +175,19 @@ def test_plain_stream_order_switch_is_read():
         "b = randn((1002, 16), 0.25, seed=4)\n"
         "w2 = randn((300, 1002), 1 / 32, seed=5)\n"
         "y = kernels.decode_linear(kernels.linear_small(x, w, a, b, None, 1.0), w2, None, None, None, 0.0)\n"
-        "torch.save(y.cpu(), __import__('sys').argv[1])\n"
+        "ranks = torch.tensor([4, 8, 16, 32, 64, 16], device='cuda')\n"
+        "offs = torch.cumsum(ranks, 0) - ranks\n"
+        "af = randn((140, 512), 1 / 23, seed=6)\n"
+        "bf = randn((140, 256), 0.2, seed=7)\n"
+        "xs = randn((700, 512), 1.0, seed=8)\n"
+        "ys = randn((700, 256), 1.0, seed=9)\n"
+        "seg = torch.tensor([0, 3, 90, 91, 300, 310, 512, 700], device='cuda')\n"
+        "sad = torch.tensor([1, 5, 0, 4, 2, 3, 4], device='cuda')\n"
+        "tiles, s = kernels.sgmv_schedule(700, 6, seg_start=seg, seg_adapter=sad)\n"
+        "z_tc = kernels.sgmv_shrink(xs, af, offs, ranks, tiles, s, 64)\n"
+        "z_blk = kernels.sgmv_shrink(xs, af, offs, ranks, tiles, s, 64, rows=torch.arange(700, device='cuda'))\n"
+        "o = kernels.sgmv_expand(ys, z_tc, bf, 256, 1, offs, ranks, tiles, s, 256, 64)\n"
+        "torch.save([t.cpu() for t in (y, z_tc, z_blk, o)], __import__('sys').argv[1])\n"
     )
     results = []
     for flag in ("1", "0"):
@@ -182,4 +197,5 @@ def test_plain_stream_order_switch_is_read():
                        cwd=os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
         results.append(torch.load(path))
         os.remove(path)
-    assert torch.equal(results[0], results[1])
+    for got, want in zip(results[1], results[0]):
+        assert torch.equal(got, want)
