@@ -292,10 +292,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 // barrier; the leader's commits arrive on the "empty" and "accumulator full"
 // barriers of both CTAs; both CTAs' epilogues arrive on the leader's
 // "accumulator empty" barrier.  No load uses cluster multicast.
-template <int STAGES>
+template <int STAGES, int NW>
 struct PairSmem {
   static constexpr int kABytes = 128 * kGemmBK * 2;
-  static constexpr int kBBytes = 128 * kGemmBK * 2;
+  static constexpr int kBBytes = NW * 128 * kGemmBK * 2;  // NW boxes of 128 W rows
   static constexpr int kStageBytes = kABytes + kBBytes;
   static constexpr int kBarOffset = STAGES * kStageBytes;
   static constexpr int kBytes = kBarOffset + 256 + 1024;
@@ -355,13 +355,21 @@ LORA_DEVINL void epilogue_store16(const GemmArgs& args, T* out_row, const T* bia
   }
 }
 
-template <int STAGES, typename T>
+// NW = 1: 256 x 256 tiles, two 256-column accumulators (the epilogue of one
+// tile overlaps the mainloop of the next).  NW = 2: 256 x 512 tiles, two
+// N = 256 MMAs per k-step sharing the x tile, so each SM takes in 48 KB per
+// 64-deep k-block for twice the products of a 32 KB NW = 1 k-block (operand
+// ingest per SM, not the tensor pipe, bounds the NW = 1 form on B200).  Both
+// accumulator halves belong to the one tile; the epilogue frees them one at a
+// time and the next tile's first MMAs into each half wait only for that half.
+template <int STAGES, int NW, typename T>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
     gemm_tc2_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_w,
                     const __grid_constant__ CUtensorMap tm_z, const __grid_constant__ CUtensorMap tm_b,
                     const GemmArgs args) {
-  using L = PairSmem<STAGES>;
+  using L = PairSmem<STAGES, NW>;
   constexpr uint32_t kTmemCols = 512;  // two 256-column fp32 accumulators
+  constexpr int kTileN = 256 * NW;
   constexpr uint32_t kIdesc = umma_idesc_f16(256, 256, std::is_same<T, __nv_bfloat16>::value ? 1 : 0);
   constexpr uint16_t kBoth = 0x3;
 
@@ -426,7 +434,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
         int mt, nt;
         gemm_tile_coords(tile, args, mt, nt);
         const int row_a = mt * 256 + static_cast<int>(rank) * 128;
-        const int row_b = nt * 256 + static_cast<int>(rank) * 128;
+        const int row_b = nt * kTileN + static_cast<int>(rank) * 128;  // + 256 for the second box
         for (int kb = 0; kb < num_kb; ++kb) {
           if (!mbar_wait_bounded(&empty[stage], phase ^ 1, abort_flag, args.err, kDevErrTimeoutEmpty)) {
             ok = false;
@@ -442,10 +450,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
             tma_load_2d_pair_hint(ma, sm_a + stage * L::kABytes, bar, kc, row_a, pol_stream);
           else
             tma_load_2d_pair(ma, sm_a + stage * L::kABytes, bar, kc, row_a);
-          if (args.l2_hints & 1)
-            tma_load_2d_pair_hint(mb, sm_b + stage * L::kBBytes, bar, kc, row_b, pol_keep);
-          else
-            tma_load_2d_pair(mb, sm_b + stage * L::kBBytes, bar, kc, row_b);
+#pragma unroll
+          for (int h = 0; h < NW; ++h) {
+            uint8_t* dst = sm_b + stage * L::kBBytes + h * (128 * kGemmBK * 2);
+            if (args.l2_hints & 1)
+              tma_load_2d_pair_hint(mb, dst, bar, kc, row_b + 256 * h, pol_keep);
+            else
+              tma_load_2d_pair(mb, dst, bar, kc, row_b + 256 * h);
+          }
           if (++stage == STAGES) {
             stage = 0;
             phase ^= 1;
@@ -461,8 +473,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
       int local = 0;
       bool ok = true;
       for (int tile = pair; ok && tile < args.num_tiles; tile += npairs, ++local) {
-        const int acc = local & 1;
-        const uint32_t acc_phase = (local >> 1) & 1;
+        // NW = 1: accumulator local & 1, its (local >> 1)-th use; NW = 2: both halves, every tile
+        const int acc = NW == 1 ? (local & 1) : 0;
+        const uint32_t acc_phase = NW == 1 ? ((local >> 1) & 1) : (local & 1);
         if (!mbar_wait_bounded(&acc_empty[acc], acc_phase ^ 1, abort_flag, args.err, kDevErrTimeoutAccEmpty))
           break;
         tc_fence_after();
@@ -479,6 +492,19 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
           for (int k = 0; k < nk; ++k)
             tc_mma_f16_pair(d_tmem, adesc + static_cast<uint64_t>(2 * k), bdesc + static_cast<uint64_t>(2 * k),
                             kIdesc, (kb > 0 || k > 0) ? 1u : 0u);
+          if constexpr (NW == 2) {
+            if (kb == 0) {  // the second half of the accumulator: free once the epilogue has drained it
+              if (!mbar_wait_bounded(&acc_empty[1], acc_phase ^ 1, abort_flag, args.err, kDevErrTimeoutAccEmpty)) {
+                ok = false;
+                break;
+              }
+              tc_fence_after();
+            }
+            const uint64_t bdesc1 = umma_desc_sw128(smem_u32(sm_b + stage * L::kBBytes + 128 * kGemmBK * 2));
+            for (int k = 0; k < nk; ++k)
+              tc_mma_f16_pair(tmem_base + 256, adesc + static_cast<uint64_t>(2 * k),
+                              bdesc1 + static_cast<uint64_t>(2 * k), kIdesc, (kb > 0 || k > 0) ? 1u : 0u);
+          }
           tc_commit_pair(&empty[stage], kBoth);
           if (++stage == STAGES) {
             stage = 0;
@@ -490,31 +516,38 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
     }
   } else {
     // ------------------------------------------------ epilogue (both CTAs)
+    // NW = 2: acc_full[0] per tile; the halves are released through
+    // acc_empty[0] and acc_empty[1] as they are drained.
     const int quad = warp & 3;
     const T* bias = static_cast<const T*>(args.bias);
     const bool vec_ok = (args.ldo % 8) == 0 && (reinterpret_cast<uintptr_t>(args.out) % 16) == 0;
     const uint64_t st_policy = l2_policy_evict_first();
     int local = 0;
     for (int tile = pair; tile < args.num_tiles; tile += npairs, ++local) {
-      const int acc = local & 1;
-      const uint32_t acc_phase = (local >> 1) & 1;
+      const int acc = NW == 1 ? (local & 1) : 0;
+      const uint32_t acc_phase = NW == 1 ? ((local >> 1) & 1) : (local & 1);
       int mt, nt;
       gemm_tile_coords(tile, args, mt, nt);
       if (!mbar_wait_bounded(&acc_full[acc], acc_phase, abort_flag, args.err, kDevErrTimeoutAccFull)) break;
       tc_fence_after();
       const int row = mt * 256 + static_cast<int>(rank) * 128 + quad * 32 + lane;
       T* out_row = static_cast<T*>(args.out) + static_cast<int64_t>(row) * args.ldo;
-      const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + static_cast<uint32_t>(acc * 256);
 #pragma unroll 1
-      for (int c = 0; c < 256; c += 16) {
-        uint32_t r[16];
-        tmem_ld_32x32b_x16(t_row + c, r);
-        tmem_wait_ld();
-        epilogue_store16<T>(args, out_row, bias, row, nt * 256 + c, vec_ok, r, st_policy);
+      for (int h = 0; h < NW; ++h) {
+        const int half = NW == 1 ? acc : h;  // TMEM accumulator drained in this round
+        const uint32_t t_row =
+            tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + static_cast<uint32_t>(half * 256);
+#pragma unroll 1
+        for (int c = 0; c < 256; c += 16) {
+          uint32_t r[16];
+          tmem_ld_32x32b_x16(t_row + c, r);
+          tmem_wait_ld();
+          epilogue_store16<T>(args, out_row, bias, row, nt * kTileN + h * 256 + c, vec_ok, r, st_policy);
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(&acc_empty[half]), 0));
       }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(&acc_empty[acc]), 0));
     }
   }
 
@@ -633,11 +666,11 @@ int env_int(const char* name, int fallback) {
   return parsed > 0 || std::strcmp(v, "0") == 0 ? parsed : fallback;
 }
 
-template <int STAGES, typename T>
+template <int STAGES, int NW, typename T>
 int launch_gemm_pair(const void* x, int64_t ldx, const void* w, int64_t ldw, const void* z, int64_t ldz,
                      const void* bw, int64_t ldbw, const void* bias, void* out, int64_t ldo, int64_t M, int64_t N,
                      int64_t K, int64_t R, float alpha, int64_t lo_offset, int dtype, cudaStream_t stream) {
-  using L = PairSmem<STAGES>;
+  using L = PairSmem<STAGES, NW>;
   const int dev = current_device();
   if (dev < 0) return LORA_ERR_DEVICE;
   const DeviceInfo& info = device_info(dev);
@@ -666,13 +699,13 @@ int launch_gemm_pair(const void* x, int64_t ldx, const void* w, int64_t ldw, con
   const int tail_rem = static_cast<int>(R - static_cast<int64_t>(a.num_kb_tail - 1) * kGemmBK);
   a.tail_last_k16 = a.num_kb_tail > 0 ? (tail_rem + 15) / 16 : 4;
   a.num_m_tiles = static_cast<int>((M + 255) / 256);
-  a.num_n_tiles = static_cast<int>((N + 255) / 256);
+  a.num_n_tiles = static_cast<int>((N + 256 * NW - 1) / (256 * NW));
   a.num_tiles = a.num_m_tiles * a.num_n_tiles;
   a.group_m = env_int("LORA_B200_GROUP_M", 8);
   a.l2_hints = env_int("LORA_B200_L2_HINTS", 0);
   a.alpha = alpha;
 
-  auto kernel = gemm_tc2_kernel<STAGES, T>;
+  auto kernel = gemm_tc2_kernel<STAGES, NW, T>;
   static std::once_flag once[64];
   static cudaError_t attr_err[64];
   static int max_clusters[64];
@@ -695,6 +728,23 @@ int launch_gemm_pair(const void* x, int64_t ldx, const void* w, int64_t ldw, con
   const int pairs = static_cast<int>(std::min<int64_t>(a.num_tiles, max_clusters[dev & 63]));
   kernel<<<2 * pairs, kGemmThreads, L::kBytes, stream>>>(tm_x, tm_w, tm_z, tm_b, a);
   return cudaGetLastError() == cudaSuccess ? LORA_OK : LORA_ERR_CUDA;
+}
+
+// 256 x 512 pair tiles (NW = 2) when they still give every SM pair enough
+// tiles: they need a third less operand ingest per product, the bound of the
+// 256 x 256 form, at the price of an epilogue that only half overlaps the next
+// tile.  Chosen when their waves of pairs, weighted by the tile's doubled work
+// and the ~10% faster products, cost less than the 256 x 256 waves.
+// LORA_B200_GEMM_WIDE=0 / 1 forces the choice (tuning sweeps).
+int pair_tile_width(int64_t M, int64_t N, int pairs) {
+  const char* force = std::getenv("LORA_B200_GEMM_WIDE");
+  if (force != nullptr && force[0] == '0') return 1;
+  if (N < 512) return 1;
+  if (force != nullptr && force[0] == '1') return 2;
+  const int64_t mt = (M + 255) / 256;
+  const int64_t w1 = (mt * ((N + 255) / 256) + pairs - 1) / pairs;
+  const int64_t w2 = (mt * ((N + 511) / 512) + pairs - 1) / pairs;
+  return 1.8 * static_cast<double>(w2) < static_cast<double>(w1) ? 2 : 1;
 }
 
 // Pair tiles when the output is wide and there are enough 256x256 tiles to
@@ -749,11 +799,18 @@ extern "C" int lora_gemm(const void* x, int64_t ldx, const void* w, int64_t ldw,
   const int bn = gemm_pick_bn(M, N, info.num_sms);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (use_pair_tiles(M, N, info.num_sms)) {
+    if (pair_tile_width(M, N, info.num_sms / 2) == 2) {
+      if (dtype == LORA_BF16)
+        return launch_gemm_pair<4, 2, __nv_bfloat16>(x, ldx, w, ldw, z, ldz, bw, ldbw, bias, out, ldo, M, N, K, R,
+                                                     alpha, lo_offset, dtype, s);
+      return launch_gemm_pair<4, 2, __half>(x, ldx, w, ldw, z, ldz, bw, ldbw, bias, out, ldo, M, N, K, R, alpha,
+                                            lo_offset, dtype, s);
+    }
     if (dtype == LORA_BF16)
-      return launch_gemm_pair<6, __nv_bfloat16>(x, ldx, w, ldw, z, ldz, bw, ldbw, bias, out, ldo, M, N, K, R, alpha,
-                                                lo_offset, dtype, s);
-    return launch_gemm_pair<6, __half>(x, ldx, w, ldw, z, ldz, bw, ldbw, bias, out, ldo, M, N, K, R, alpha,
-                                       lo_offset, dtype, s);
+      return launch_gemm_pair<6, 1, __nv_bfloat16>(x, ldx, w, ldw, z, ldz, bw, ldbw, bias, out, ldo, M, N, K, R,
+                                                   alpha, lo_offset, dtype, s);
+    return launch_gemm_pair<6, 1, __half>(x, ldx, w, ldw, z, ldz, bw, ldbw, bias, out, ldo, M, N, K, R, alpha,
+                                          lo_offset, dtype, s);
   }
   if (dtype == LORA_BF16)
     return dispatch_gemm<__nv_bfloat16>(bn, x, ldx, w, ldw, z, ldz, bw, ldbw, bias, out, ldo, M, N, K, R, alpha,
