@@ -43,8 +43,8 @@ M_TOKENS = 32760
 CPU_SAMPLE_TOKENS = 4096
 # DRAM read + write of one fused-GEMM launch (C5 q projection), from the full
 # ncu capture at M = 16384 committed under profiles/, scaled linearly to M:
-# 773.1 MB read + 155.1 MB write per launch at M = 16384 (CTA-pair kernel).
-NCU_TRAFFIC_Q_16384 = 928.2e6
+# 820.2 MB read + 152.6 MB write per launch at M = 16384 (CTA-pair kernel, 256x512 tiles).
+NCU_TRAFFIC_Q_16384 = 972.8e6
 
 
 def parse():
@@ -347,7 +347,8 @@ def run_gpu(args):
                    "parallelism": f"token-sharded x{world}, weights+adapters replicated, no collective",
                    "l2": "every input > 126 MB L2 (x >= 335 MB per projection); no flush needed"},
         "roofline": {"bound": "tensor", "kernel": ("gemm_tc_kernel<256,4,bf16>" if os.environ.get("LORA_B200_GEMM") == "1sm"
-                                else "gemm_tc2_kernel<6,bf16> (CTA pair)") + " fused base + LoRA K-slice",
+                                else "gemm_tc2_kernel<4,2,bf16> (CTA pair, 256x512 tiles)")
+                               + " fused base + LoRA K-slice",
                      "achieved": round(gemm_achieved, 2), "peak": peak, "unit": "TFLOP/s",
                      "frac": round(gemm_achieved / peak, 4), "peak_source": peak_src, "traffic": traffic,
                      "traffic_note": "bytes per q-projection launch (ncu capture at M=16384, scaled to M); "
