@@ -737,10 +737,12 @@ int launch_gemm_pair(const void* x, int64_t ldx, const void* w, int64_t ldw, con
 // and the ~10% faster products, cost less than the 256 x 256 waves.
 // LORA_B200_GEMM_WIDE=0 / 1 forces the choice (tuning sweeps).
 int pair_tile_width(int64_t M, int64_t N, int pairs) {
-  const char* force = std::getenv("LORA_B200_GEMM_WIDE");
-  if (force != nullptr && force[0] == '0') return 1;
-  if (N < 512) return 1;
-  if (force != nullptr && force[0] == '1') return 2;
+  static const int force = [] {  // -1: choose, 0 / 1: forced (read once)
+    const char* v = std::getenv("LORA_B200_GEMM_WIDE");
+    return (v != nullptr && (v[0] == '0' || v[0] == '1')) ? v[0] - '0' : -1;
+  }();
+  if (force == 0 || N < 512) return 1;
+  if (force == 1) return 2;
   const int64_t mt = (M + 255) / 256;
   const int64_t w1 = (mt * ((N + 255) / 256) + pairs - 1) / pairs;
   const int64_t w2 = (mt * ((N + 511) / 512) + pairs - 1) / pairs;
