@@ -10,11 +10,11 @@
 // band of W and one K slice; the K slices of a band are the CTAs of one
 // thread-block cluster, which add their fp32 partial tiles through
 // distributed shared memory in rank order -- no workspace, no atomics,
-// deterministic.  The LoRA expand is the cluster's last K slice: one TMA tile
-// of B (128 rows x 64 ranks, zero beyond R) multiplied by [hi | lo] of
-// scale * z, a bf16/f16 pair the epilogue warps write into shared memory once
-// z is ready (griddepcontrol.wait: z may come from the shrink launched just
-// before this kernel), so W streaming overlaps the shrink.
+// deterministic.  With a z input the LoRA expand is the cluster's last K
+// slice: the band's B rows (128 rows x 64 ranks, zero beyond R) multiplied by
+// [hi | lo] of scale * z, a bf16/f16 pair the epilogue warps write into shared
+// memory once z is ready (griddepcontrol.wait: z may come from the shrink
+// launched just before this kernel), so W streaming overlaps the shrink.
 //
 // Fused shrink: every stage also brings the k-block of lora_A (r16 rows), and
 // a second set of MMAs (A rows as the 128-row operand, the same x tile as the
