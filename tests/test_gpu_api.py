@@ -6,7 +6,6 @@ reference leaves untested.
 """
 
 import math
-import os
 
 import numpy as np
 import pytest

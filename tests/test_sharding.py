@@ -2,7 +2,6 @@
 
 import os
 import socket
-import traceback
 
 import pytest
 import torch
