@@ -241,6 +241,7 @@ def sgmv_schedule(t_total: int, n_adapters: int, ids: torch.Tensor | None = None
                   seg_start: torch.Tensor | None = None, seg_adapter: torch.Tensor | None = None,
                   device=None) -> tuple[torch.Tensor, int]:
     """Build the device tile list; returns (tiles int32 tensor, S) with S = 0 for ids."""
+    _lib.require_cuda(ids, seg_start, seg_adapter, where="sgmv_schedule")
     lib = _lib.load()
     if ids is not None:
         device = ids.device if device is None else device

@@ -71,3 +71,46 @@ def test_cpu_tensors_raise():
     b = torch.randn(8, 2, dtype=torch.bfloat16)
     with pytest.raises(RuntimeError, match="CUDA"):
         fused_lora_linear(x, w, None, a, b, 1.0)
+
+
+def _host_calls():
+    """Each drop-in surface called with host tensors; the reference raises the
+    same way (assertions on x.is_cuda in fused_lora.py / splitk_lora.py,
+    ValueError in decode_linear.py:89-99)."""
+    import importlib
+
+    import torch
+
+    fl = importlib.import_module("probe_b200.fused_lora")
+    from probe_b200 import decode_linear, fused_linear, multilora, ragged_branch, segmented_branch, splitk_lora, \
+        splitk_shrink
+
+    x = torch.randn(4, 64, dtype=torch.bfloat16)
+    w = torch.randn(32, 64, dtype=torch.bfloat16)
+    a = torch.randn(2, 64, dtype=torch.bfloat16)
+    b = torch.randn(32, 2, dtype=torch.bfloat16)
+    y = torch.randn(4, 32, dtype=torch.bfloat16)
+    z = torch.randn(4, 2, dtype=torch.bfloat16)
+    offs, ranks, ids = torch.tensor([0]), torch.tensor([2]), torch.zeros(4, dtype=torch.long)
+    bf = b.T.contiguous()
+    return {
+        "fused_lora": lambda: fl.fused_lora(x, a, b, y, 1.0),
+        "tiled_lora": lambda: fl.tiled_lora(x, a, b, y, 1.0),
+        "splitk_lora_shrink": lambda: splitk_lora.splitk_lora_shrink(x, a),
+        "persistent_expand_add": lambda: splitk_lora.persistent_expand_add(z, b, y, 1.0),
+        "shrink_partial": lambda: splitk_shrink.shrink_partial(x, a),
+        "shrink_ragged": lambda: multilora.shrink_ragged(x, a, offs, ranks, ids, 2),
+        "segmented_branch_varlen": lambda: segmented_branch.segmented_branch_varlen(
+            x, y, a, bf, offs, ranks, torch.tensor([0, 4]), torch.tensor([0]), 2),
+        "ragged_branch": lambda: ragged_branch.branch(x, y, a, bf, offs, ranks, ids, 2),
+        "decode_lora_linear": lambda: decode_linear.decode_lora_linear(x, w, None, a, b, 1.0),
+        "expand_add": lambda: fused_linear.expand_add(y, z, b, 1.0),
+        "fused_gemm": lambda: fused_linear.fused_gemm(x, w, None, a, b, 1.0),
+    }
+
+
+@pytest.mark.parametrize("name", sorted(_host_calls()))
+def test_every_drop_in_refuses_host_tensors(name):
+    """No CPU fallback anywhere on the product path: host tensors raise."""
+    with pytest.raises((RuntimeError, AssertionError, ValueError)):
+        _host_calls()[name]()
