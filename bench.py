@@ -70,8 +70,9 @@ def dist_env():
 
 
 # ------------------------------------------------------------------ CPU baseline
-def cpu_baseline(steps: int = 1, tokens: int = CPU_SAMPLE_TOKENS):
-    """Reference CPU path on a bounded sample: `tokens` rows of each C5 projection, fp32."""
+def cpu_baseline(steps: int = 1, tokens: int = CPU_SAMPLE_TOKENS, warmup: int = 1):
+    """Reference CPU path on a bounded sample: `tokens` rows of each C5 projection, fp32;
+    `warmup` untimed passes over the six projections, then `steps` timed ones."""
     import torch
 
     from oracle import lora_oracle as orc
@@ -81,8 +82,9 @@ def cpu_baseline(steps: int = 1, tokens: int = CPU_SAMPLE_TOKENS):
     torch.set_num_threads(cores)
     projs = workloads.c5(device="cpu", dtype=torch.float32, m=tokens)
     flops = sum(p.flops() for p in projs)
-    for p in projs:  # warm-up (2 calls, as BASELINE.md prescribes)
-        orc.naive_linear_torch(p.x, p.w, None, p.a, p.b, p.scale)
+    for _ in range(max(warmup, 1)):  # untimed passes
+        for p in projs:
+            orc.naive_linear_torch(p.x, p.w, None, p.a, p.b, p.scale)
     times = []
     for _ in range(max(steps, 1)):
         t0 = time.perf_counter()
@@ -371,15 +373,15 @@ def run_reference(args):
     rank, world, _ = dist_env()
     if rank != 0:
         return
-    cb = cpu_baseline(steps=max(1, min(args.steps, 3)))
+    cb = cpu_baseline(steps=max(args.steps, 1), warmup=max(args.warmup, 1))
     line = {
         "metric": METRIC,
         "impl": "reference",
         "value": round(cb["value"], 4),
         "unit": "TFLOP/s",
         "n_gpus": world,
-        "steps": max(1, min(args.steps, 3)),
-        "warmup": 2,
+        "steps": max(args.steps, 1),
+        "warmup": max(args.warmup, 1),
         "ms_per_step": round(cb["seconds_per_sample"] * 1e3, 2),
         "higher_is_better": True,
         "scaling": args.scaling,
