@@ -132,9 +132,9 @@ LORA_API int lora_shrink(const void* x, int64_t ldx, const void* a, int64_t lda,
                 void* stream);
 
 /* The same split-K shrink for callers that cannot allocate device memory:
- * code running while a CUDA graph is being captured, serving loops that cannot
- * afford cudaMalloc's implicit device synchronisation, or host frameworks that
- * own all device memory and forbid plugins from allocating.  It takes no
+ * serving loops that cannot afford cudaMalloc's implicit device
+ * synchronisation, or host frameworks that own all device memory and forbid
+ * plugins from allocating.  It takes no
  * workspace: the ticket counters and partial sums live in an 8 MiB array of
  * device memory that the library holds on every GPU that loads it, until the
  * process exits.  The caller still passes x, a and z.  Limit: with split_k > 1
@@ -142,8 +142,10 @@ LORA_API int lora_shrink(const void* x, int64_t ldx, const void* a, int64_t lda,
  * (lora_shrink_static_scratch_capacity()) and at most 4096 token tiles;
  * split_k == 0 picks the widest split that fits (down to 1, which needs no
  * scratch); an explicit split_k that does not fit returns LORA_ERR_WORKSPACE.
- * The first call on a device looks up the array's device address
- * (cudaGetSymbolAddress), so make that first call before any stream capture.
+ * The first call on a device that splits K looks up the array's device
+ * address (cudaGetSymbolAddress) and caches it; make that first call before
+ * any stream capture.  A failed lookup returns LORA_ERR_CUDA and is retried
+ * by the next call.  Device ordinals above 63 return LORA_ERR_DEVICE.
  * All calls share the one array: calls that overlap on the GPU (several
  * streams or threads) race and must be serialised on one stream.
  * No counterpart in the reference (its wrappers allocate per call). */

@@ -537,10 +537,9 @@ extern "C" int lora_sgmv_shrink_ex(const void* x, int64_t ldx, const void* a_fla
 // ---------------------------------------------------------------------------
 // Split-K shrink with library-held scratch.
 //
-// Some callers cannot call cudaMalloc: code that runs while a CUDA graph is
-// being captured, serving loops that cannot afford cudaMalloc's implicit
-// device synchronisation, and host frameworks that own all device memory and
-// forbid plugins from allocating.  lora_shrink_static_scratch takes no
+// Some callers cannot call cudaMalloc: serving loops that cannot afford
+// cudaMalloc's implicit device synchronisation, and host frameworks that own
+// all device memory and forbid plugins from allocating.  lora_shrink_static_scratch takes no
 // workspace: its ticket counters and fp32 partials live in the file-scope
 // array below, which every GPU that loads this library holds until exit.
 // Every call shares that array, so calls that overlap on the GPU (concurrent
@@ -553,19 +552,24 @@ constexpr size_t kStaticPartialBytes = kStaticScratchBytes - kStaticCounterBytes
 
 static __device__ __align__(256) unsigned char g_shrink_scratch[kStaticScratchBytes];
 
-// Device address of g_shrink_scratch, looked up once per device with that
-// device current (in host code the array's name is only a stand-in).
-std::once_flag g_scratch_once[64];
-void* g_scratch_addr[64];
-cudaError_t g_scratch_status[64];
+// Device address of g_shrink_scratch per device ordinal, looked up with that
+// device current (in host code the array's name is only a stand-in).  Only a
+// successful lookup is cached; a failed one is retried by the next call.
+constexpr int kStaticMaxDevices = 64;
+std::mutex g_scratch_mutex;
+void* g_scratch_addr[kStaticMaxDevices];
 
 int static_scratch(int dev, void** addr) {
-  std::call_once(g_scratch_once[dev], [dev] {
+  if (dev < 0 || dev >= kStaticMaxDevices) return LORA_ERR_DEVICE;
+  std::lock_guard<std::mutex> lock(g_scratch_mutex);
+  if (g_scratch_addr[dev] == nullptr) {
     void* p = nullptr;
-    g_scratch_status[dev] = cudaGetSymbolAddress(&p, g_shrink_scratch);
-    g_scratch_addr[dev] = (g_scratch_status[dev] == cudaSuccess) ? p : nullptr;
-  });
-  if (g_scratch_status[dev] != cudaSuccess || g_scratch_addr[dev] == nullptr) return LORA_ERR_CUDA;
+    if (cudaGetSymbolAddress(&p, g_shrink_scratch) != cudaSuccess || p == nullptr) {
+      (void)cudaGetLastError();  // leave no sticky status behind for the caller
+      return LORA_ERR_CUDA;
+    }
+    g_scratch_addr[dev] = p;
+  }
   *addr = g_scratch_addr[dev];
   return LORA_OK;
 }
@@ -594,8 +598,6 @@ extern "C" int lora_shrink_static_scratch(const void* x, int64_t ldx, const void
       cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
     return LORA_ERR_DEVICE;
   if (major != 10 || minor != 0) return LORA_ERR_DEVICE;
-  void* scratch = nullptr;
-  if (const int rc = static_scratch(dev, &scratch); rc != LORA_OK) return rc;
 
   const int wt = shrink_wt(M);
   const int64_t tiles = (M + 16 * wt - 1) / (16 * wt);
@@ -633,6 +635,8 @@ extern "C" int lora_shrink_static_scratch(const void* x, int64_t ldx, const void
   p.scale = scale;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (split_k > 1) {
+    void* scratch = nullptr;  // looked up only when the partials need it
+    if (const int rc = static_scratch(dev, &scratch); rc != LORA_OK) return rc;
     p.counters = static_cast<int*>(scratch);
     p.partial = reinterpret_cast<float*>(static_cast<char*>(scratch) + kStaticCounterBytes);
     // The tickets must start at zero; the array keeps whatever the last call left.

@@ -1,9 +1,8 @@
 """The shrink entry point that allocates nothing (GPU only).
 
-lora_shrink_static_scratch serves callers that cannot call cudaMalloc -- code
-running while a CUDA graph is being captured, serving loops that cannot pay
-cudaMalloc's device synchronisation, host frameworks that own all device
-memory.  Its scratch is an array the library holds on the device.  This test
+lora_shrink_static_scratch serves callers that cannot call cudaMalloc --
+serving loops that cannot pay cudaMalloc's device synchronisation, host
+frameworks that own all device memory.  Its scratch is an array the library holds on the device.  This test
 calls it through the C ABI and checks it against the workspace-taking
 lora_shrink on two calls in a row with different shapes, so a second call that
 found the first call's leftovers in the shared array would be caught.
@@ -67,3 +66,28 @@ def test_static_scratch_rejects_oversize_split():
         _lib.LORA_F32, r, 0, m, k, r, 1.0, _lib.LORA_BF16, 64,
         ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
     assert rc == _lib.LORA_ERR_WORKSPACE
+
+
+def test_static_scratch_allocates_nothing():
+    """After a first call has loaded the library's device code on this GPU,
+    further calls change neither torch's allocator nor the device's free memory."""
+    m, k, r = 128, 4096, 32
+    x = randn((m, k), 1.0, seed=3)
+    a = randn((r, k), 1 / 64, seed=4)
+    _static_shrink(x, a, 1.0, torch.float32, r, False, 4)  # loads the module and the array
+    lib = _lib.load()
+    z = torch.empty((m, r), device=x.device, dtype=torch.float32)
+    torch.cuda.synchronize()
+    allocated, reserved = torch.cuda.memory_allocated(), torch.cuda.memory_reserved()
+    free_before, _ = torch.cuda.mem_get_info()
+    for _ in range(2):
+        rc = lib.lora_shrink_static_scratch(
+            ctypes.c_void_p(x.data_ptr()), k, ctypes.c_void_p(a.data_ptr()), k, ctypes.c_void_p(z.data_ptr()), r,
+            _lib.LORA_F32, r, 0, m, k, r, 1.0, _lib.LORA_BF16, 4,
+            ctypes.c_void_p(torch.cuda.current_stream().cuda_stream))
+        assert rc == _lib.LORA_OK
+    torch.cuda.synchronize()
+    assert torch.cuda.memory_allocated() == allocated
+    assert torch.cuda.memory_reserved() == reserved
+    assert torch.cuda.mem_get_info()[0] == free_before
+    assert_parity(z, np64(x) @ np64(a).T, torch.bfloat16)
