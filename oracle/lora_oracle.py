@@ -175,21 +175,60 @@ def grouped_lora(x, a, b, y=None, scale=1.0):
     return out
 
 
-def stack_adapters(adapters, base_scale=None):
+def stack_adapters(adapters, base_scale=None, dtype=None):
     """attach_fused_lora stacking (runtime_lora.py:45-54).
 
     adapters: list of (down [r_i,K], up [N,r_i], alpha_i); the first one fixes
     the layer scale.  Returns (A_stack, B_stack, scale) with
     A_stack = [A_1; (a_2/a_1) A_2; ...], B_stack = [B_1 | B_2 | ...].
+    With ``dtype`` ("bf16" / "f16") each folded block is rounded to that dtype
+    after an fp32 multiply, as the reference does (``(alpha / target.scale) *
+    down.float()`` then ``.to(dtype)``, runtime_lora.py:49-53).
     """
     down0, up0, alpha0 = adapters[0]
     scale = alpha0 if base_scale is None else base_scale
     a_blocks = [np.asarray(down0, dtype=np.float64)]
     b_blocks = [np.asarray(up0, dtype=np.float64)]
     for down, up, alpha in adapters[1:]:
-        a_blocks.append((alpha / scale) * np.asarray(down, dtype=np.float64))
+        if dtype is None:
+            a_blocks.append((alpha / scale) * np.asarray(down, dtype=np.float64))
+        else:
+            folded = np.float32(alpha / scale) * np.asarray(down, dtype=np.float32)
+            a_blocks.append(round_dtype(folded, dtype).astype(np.float64))
         b_blocks.append(np.asarray(up, dtype=np.float64))
     return np.concatenate(a_blocks, axis=0), np.concatenate(b_blocks, axis=1), scale
+
+
+def row_sums(x, w, bias, a, b, scale):
+    """Row sums of ``naive_linear``'s output without forming it.
+
+    By linearity, ``sum_n out[i, n] = x[i] . (sum_n W[n] + scale * A^T (sum_n B[n]))
+    + sum(bias)``: one matrix-vector product over x, so the check covers every
+    row of an output too large to compute in float64 here."""
+    x, w, bias, a, b = _f64(x, w, bias, a, b)
+    v = w.sum(axis=0)
+    if a is not None and a.shape[0] > 0 and scale != 0:
+        v = v + scale * (a.T @ b.sum(axis=0))
+    out = x @ v
+    if bias is not None:
+        out = out + bias.sum()
+    return out
+
+
+def token_sketch(weights, x, w, bias, a, b, scale):
+    """``weights^T . out`` for ``out = naive_linear(x, ...)`` without forming out.
+
+    ``weights`` is one value per token; by linearity the result is
+    ``u W^T + scale (u A^T) B^T + sum(weights) bias`` with ``u = weights^T x``,
+    a length-N vector that mixes every row of the output into every column."""
+    weights, x, w, bias, a, b = _f64(weights, x, w, bias, a, b)
+    u = weights @ x
+    out = w @ u
+    if a is not None and a.shape[0] > 0 and scale != 0:
+        out = out + scale * (b @ (a @ u))
+    if bias is not None:
+        out = out + weights.sum() * bias
+    return out
 
 
 # ------------------------------------------------------------ multi adapter

@@ -17,8 +17,9 @@ error behaviour).  The implementations are this package's sm_100a kernels:
 ``hybrid``   tcgen05 base GEMM, shrink, expand-add epilogue (fused_linear.py:370-373).
 ``concat``   tcgen05 GEMM on ``[W; A; 0]`` then expand-add (fused_linear.py:336-367).
 
-``select_variant`` times the eligible candidates once per shape, as the
-reference does (fused_linear.py:445-465); ``LORAFORGE_VARIANT`` forces one.
+With ``LORAFORGE_TUNE=1`` ``select_variant`` races the eligible candidates
+once per shape, as the reference does (fused_linear.py:445-465); by default a
+shape rule picks; ``LORAFORGE_VARIANT`` forces one.
 Unlike the reference there is no CPU or cuBLAS path: CPU tensors raise.
 """
 
@@ -255,32 +256,93 @@ def eligible(variant, m, k, n, r, dtype, has_augmented):
 # Variant selection
 # --------------------------------------------------------------------------- #
 
-def _time_ms(fn, warmup=5, reps=15, use_graph=False):
-    """Median CUDA-event time of ``fn`` (fused_linear.py:413-433)."""
-    for _ in range(warmup):
-        fn()
-    torch.cuda.synchronize()
-    inner = 1
-    if use_graph:
+class _VariantRace:
+    """The per-shape timing race of ``LORAFORGE_TUNE=1`` (reference behaviour:
+    fused_linear.py:413-473 times every eligible variant once per shape and
+    keeps the fastest).
+
+    Candidates are timed round-robin -- each round runs every candidate once
+    between CUDA events -- so clock and power drift during the race touch all
+    of them alike; the median round decides.  With ``LORAFORGE_TUNE_MODE=graph``
+    shapes of at most 8 rows are timed as a captured chain of 20 calls (the
+    replay cost a graph-serving caller pays).  A candidate that raises drops
+    out.  Results are kept per key together with the candidate set and tune
+    mode they were measured under; a change of either re-runs the race.
+    """
+
+    ROUNDS = 15
+    WARMUP = 5
+    CHAIN = 20
+
+    def __init__(self):
+        self.results: dict[tuple, dict] = {}
+
+    @staticmethod
+    def _as_chain(fn, length):
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            fn()
+        torch.cuda.current_stream().wait_stream(side)
         graph = torch.cuda.CUDAGraph()
-        inner = 20
-        with torch.cuda.graph(graph):
-            for _ in range(inner):
+        with torch.cuda.graph(graph, stream=side):
+            for _ in range(length):
                 fn()
-        fn = graph.replay
-    samples = []
-    for _ in range(reps):
-        begin, end = torch.cuda.Event(True), torch.cuda.Event(True)
-        begin.record()
-        fn()
-        end.record()
-        end.synchronize()
-        samples.append(begin.elapsed_time(end) / inner)
-    return statistics.median(samples)
+        return graph.replay, graph
+
+    def _clock(self, runners: dict, graph_mode: bool) -> dict:
+        live, per_call, keep = {}, {}, []
+        for name, fn in runners.items():
+            try:
+                for _ in range(self.WARMUP):
+                    fn()
+                if graph_mode:
+                    replay, graph = self._as_chain(fn, self.CHAIN)
+                    keep.append(graph)
+                    live[name], per_call[name] = replay, self.CHAIN
+                else:
+                    live[name], per_call[name] = fn, 1
+            except Exception:  # noqa: BLE001 -- a failing variant is not a candidate
+                continue
+        torch.cuda.synchronize()
+        samples = {name: [] for name in live}
+        for _ in range(self.ROUNDS):
+            for name, fn in live.items():
+                t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                t0.record()
+                fn()
+                t1.record()
+                t1.synchronize()
+                samples[name].append(t0.elapsed_time(t1) / per_call[name])
+        del keep
+        return {name: statistics.median(v) for name, v in samples.items()}
+
+    def pick(self, runners: dict, key: tuple) -> str:
+        forced = _forced_variant()
+        if forced in runners:
+            return forced
+        if len(runners) == 1:
+            return next(iter(runners))
+        mode = os.environ.get("LORAFORGE_TUNE_MODE", "eager")
+        context = (tuple(sorted(runners)), mode)
+        known = self.results.get(key)
+        if known is not None and known["context"] == context:
+            return known["winner"]
+        timings = self._clock(runners, graph_mode=(mode == "graph" and key[0] <= 8))
+        if not timings:
+            raise RuntimeError(f"no LoRA variant ran for shape {key}")
+        winner = min(timings, key=timings.get)
+        self.results[key] = {"winner": winner, "timings_ms": timings, "context": context}
+        return winner
+
+    def report(self) -> dict:
+        out = {}
+        for (m, k, n, r, dtype, _device), res in self.results.items():
+            out[f"m{m}_k{k}_n{n}_r{r}_{str(dtype).split('.')[-1]}"] = res["winner"]
+        return out
 
 
-_SELECTION: dict[tuple, str] = {}
-_SELECTION_CONTEXT: dict[tuple, tuple] = {}
+_RACE = _VariantRace()
 
 
 def _forced_variant() -> str | None:
@@ -289,38 +351,13 @@ def _forced_variant() -> str | None:
 
 
 def select_variant(runners: dict, key: tuple) -> str:
-    """Time each legal implementation once for this shape and cache the winner."""
-    forced = _forced_variant()
-    if forced is not None and forced in runners:
-        return forced
-    if len(runners) == 1:
-        return next(iter(runners))
-    cached = _SELECTION.get(key)
-    context = (tuple(runners), os.environ.get("LORAFORGE_TUNE_MODE", "eager"))
-    if cached in runners and _SELECTION_CONTEXT.get(key) == context:
-        return cached
-    timings = {}
-    for variant, fn in runners.items():
-        try:
-            timings[variant] = _time_ms(
-                fn, use_graph=key[0] <= 8 and os.environ.get("LORAFORGE_TUNE_MODE", "eager") == "graph",
-            )
-        except Exception:  # a variant that fails simply drops out
-            continue
-    if not timings:
-        raise RuntimeError(f"no LoRA variant ran for shape {key}")
-    best = min(timings, key=timings.get)
-    _SELECTION[key] = best
-    _SELECTION_CONTEXT[key] = context
-    return best
+    """Name of the variant to run for shape ``key`` (forced, only, or raced once)."""
+    return _RACE.pick(runners, key)
 
 
 def selection_report() -> dict:
-    """Which variant won for each shape seen so far (fused_linear.py:468-473)."""
-    return {
-        f"m{m}_k{k}_n{n}_r{r}_{str(dtype).split('.')[-1]}": variant
-        for (m, k, n, r, dtype, _dev), variant in _SELECTION.items()
-    }
+    """Which variant won the race for each shape seen so far (fused_linear.py:468-473)."""
+    return _RACE.report()
 
 
 def _default_variant(rows, k, r):

@@ -1,20 +1,28 @@
 """Inference-only PEFT integration (drop-in for peft_integration.py:1-479).
 
-``enable_loraforge_peft(model)`` patches every PEFT LoRA ``Linear`` so that its
-forward runs the B200 kernels of this package.  As in the reference, a module
-is declined -- it keeps PEFT's own forward -- unless it has exactly one active
-adapter, no DoRA, an inactive dropout, CUDA fp16/bf16 tensors of one dtype and
-an ``nn.Linear`` base (peft_integration.py:41-63).  A plan is resolved once per
-(adapter, row count, scaling, dtype, device) and the last two are kept
-(peft_integration.py:199-232).
+``enable_loraforge_peft(model)`` reroutes the forward of every PEFT LoRA
+``Linear`` through this package's B200 kernels.  A module keeps PEFT's own
+forward unless it has exactly one active adapter, no DoRA, an inactive
+dropout, CUDA fp16/bf16 activations matching the base weight's dtype and an
+``nn.Linear`` base -- the same set of modules the reference accepts
+(peft_integration.py:41-63).  Calls with extra arguments, in training mode,
+on merged weights or with adapters disabled also take PEFT's forward.
 
-Grouping (``enable_grouping``): a transformer MLP's gate and up projections
-read the same x.  Their weights are packed once into ``[W_gate; W_up]`` with a
-block-diagonal ``[B_gate*s_g, 0; 0, B_up*s_u]`` sidecar, so one shrink and one
-GEMM (or one decode launch) serve both projections
-(the reference groups the decode sidecars only, peft_integration.py:270-411).
-With ``group_attention`` the same packing serves an attention block's q, k and
-v projections (an extension; the reference has no attention grouping).
+Plans.  Each patched module owns a :class:`_PlanCache`: a resolved callable
+per (active adapters, row count, scaling, dtype, device), holding at most two
+(a prefill shape and a decode shape, the usual pair), so a forward costs one
+key comparison once warm.  Scaling is part of the key, so a ``set_scale``
+between calls (a zero scale turns the module into its base linear) is seen.
+
+Grouping.  Sibling projections that read the same input are served by ONE
+packed linear (:class:`_SiblingGroup`): their base weights stacked along the
+output, their down factors stacked along the rank and a block-diagonal up
+factor with each member's scale folded in, so one shrink and one GEMM (or one
+small-M launch) read x once for all of them.  ``enable_grouping`` packs a
+transformer MLP's gate and up projections (the reference groups those for
+decode, peft_integration.py:270-411); ``group_attention`` (or
+``LORAFORGE_GROUPED_ATTN=1``) also packs an attention block's q, k and v.
+``LORAFORGE_GROUPED_MLP=individual`` turns the MLP grouping off.
 
 ``peft`` itself is optional: modules are recognised by PEFT's LoRA Linear
 attributes when the package is not importable.
@@ -24,7 +32,7 @@ from __future__ import annotations
 
 import os
 import types
-from collections import Counter
+from collections import Counter, OrderedDict
 
 import torch
 
@@ -35,370 +43,336 @@ try:  # pragma: no cover - exercised only where peft is installed
 except Exception:  # noqa: BLE001
     _PeftLoraLinear = None
 
-_GROUPED_MLP_CHOICE_CACHE: dict = {}
+_HALF = (torch.float16, torch.bfloat16)
+_PEFT_ATTRS = ("lora_A", "lora_B", "scaling", "base_layer", "active_adapters")
 
 
 def is_lora_linear(module) -> bool:
     """A PEFT LoRA Linear (or an object exposing the same attributes)."""
     if _PeftLoraLinear is not None and isinstance(module, _PeftLoraLinear):
         return True
-    d = module.__dict__
-    return all(hasattr(module, a) for a in ("lora_A", "lora_B", "scaling", "base_layer", "active_adapters")) and \
-        "_modules" in d and "lora_A" in d["_modules"]
+    if "lora_A" not in module.__dict__.get("_modules", {}):
+        return False
+    return all(hasattr(module, attr) for attr in _PEFT_ATTRS)
 
 
-def _inactive_dropout(dropout):
-    """Training dropout is an identity after eval(), regardless of saved p."""
-    return isinstance(dropout, torch.nn.Identity) or (
-        isinstance(dropout, torch.nn.Dropout) and not dropout.training
-    )
+def _dropout_is_identity(layer) -> bool:
+    """In eval mode a Dropout passes x through whatever its p (and Identity always does)."""
+    if isinstance(layer, torch.nn.Identity):
+        return True
+    return isinstance(layer, torch.nn.Dropout) and not layer.training
 
 
-def _sidecar(module, name):
-    """Return (A, B, scale) for one active adapter, or None if unsupported."""
-    use_dora = getattr(module, "use_dora", {}) or {}
-    if name not in module.lora_A or use_dora.get(name, False):
+def _bypassed(module) -> bool:
+    """States in which the module must run PEFT's own forward."""
+    return module.training or bool(getattr(module, "merged", False)) or bool(getattr(module, "disable_adapters", False))
+
+
+def _adapter_factors(module, adapter: str, dtype=None):
+    """(A [r, K], B [N, r], scale) of ``adapter`` when the kernels can serve it, else None."""
+    if adapter not in module.lora_A or adapter not in module.lora_B:
         return None
-    a = module.lora_A[name].weight
-    b = module.lora_B[name].weight
-    if a.ndim != 2 or b.ndim != 2:
+    if (getattr(module, "use_dora", None) or {}).get(adapter, False):
         return None
-    return a, b, float(module.scaling[name])
-
-
-def _supported(module, x, name):
-    base_layer = module.base_layer
-    sidecar = _sidecar(module, name)
-    if sidecar is None:
+    if not isinstance(module.base_layer, torch.nn.Linear) or not _dropout_is_identity(module.lora_dropout[adapter]):
         return None
-    a, b, scale = sidecar
-    ok = (
-        isinstance(base_layer, torch.nn.Linear)
-        and _inactive_dropout(module.lora_dropout[name])
-        and x.is_cuda
-        and x.dtype in (torch.float16, torch.bfloat16)
-        and x.dtype == base_layer.weight.dtype
-        and a.dtype == x.dtype
-        and b.dtype == x.dtype
-    )
-    return (a, b, scale) if ok else None
+    a, b = module.lora_A[adapter].weight, module.lora_B[adapter].weight
+    want = module.base_layer.weight.dtype if dtype is None else dtype
+    if a.ndim != 2 or b.ndim != 2 or want not in _HALF or module.base_layer.weight.dtype != want:
+        return None
+    if a.dtype != want or b.dtype != want:
+        return None
+    return a, b, float(module.scaling[adapter])
 
 
-def _build_plan(module, x, rows):
-    """Resolve everything that does not change between steps, once (peft_integration.py:41-96)."""
-    declined = (module._active_adapter, rows, None)
-    active = list(module.active_adapters)
-    if len(active) != 1:
+def _as_rows(x: torch.Tensor) -> torch.Tensor:
+    x2 = x.reshape(-1, x.shape[-1])
+    return x2 if x2.is_contiguous() else x2.contiguous()
+
+
+# ------------------------------------------------------------------ plans
+class _PlanCache:
+    """Resolved forwards of one module, most recently used last, at most ``size``."""
+
+    def __init__(self, size: int = 2):
+        self.size = size
+        self.entries: OrderedDict[tuple, object] = OrderedDict()
+        self.last_key = None
+        self.last_call = None
+
+    def lookup(self, key):
+        if key == self.last_key:
+            return self.last_call
+        call = self.entries.get(key)
+        if call is not None:
+            self.entries.move_to_end(key)
+            self.last_key, self.last_call = key, call
+        return call
+
+    def store(self, key, call):
+        self.entries[key] = call
+        self.entries.move_to_end(key)
+        while len(self.entries) > self.size:
+            self.entries.popitem(last=False)
+        self.last_key, self.last_call = key, call
+        return call
+
+
+def _plan_key(module, x: torch.Tensor, rows: int) -> tuple:
+    return (tuple(module.active_adapters), rows, tuple(sorted(module.scaling.items())), x.dtype, x.device)
+
+
+def _resolve(module, x: torch.Tensor, rows: int):
+    """The forward for this key: a kernel plan, or PEFT's forward when declined."""
+    declined = module._loraforge_original_forward
+    adapters = list(module.active_adapters)
+    if len(adapters) != 1 or not x.is_cuda or x.dtype not in _HALF:
         return declined
-    name = active[0]
-    sidecar = _supported(module, x, name)
-    if sidecar is None:
+    factors = _adapter_factors(module, adapters[0], dtype=x.dtype)
+    if factors is None:
         return declined
-    a, b, scale = sidecar
-    base_layer = module.base_layer
-    probe = x.reshape(-1, x.shape[-1])
-    if not probe.is_contiguous():
-        probe = probe.contiguous()
-    run = build_plan(probe, base_layer.weight, base_layer.bias, a, b, scale)
-    module._loraforge_decode_choice = "base" if (a.shape[0] == 0 or scale == 0) else (
-        "decode" if rows < MIN_GEMM_ROWS else "gemm")
-    out_features = base_layer.out_features
+    a, b, scale = factors
+    base = module.base_layer
+    if a.shape[0] == 0 or scale == 0:
+        module._loraforge_decode_choice = "base"
+    else:
+        module._loraforge_decode_choice = "decode" if rows < MIN_GEMM_ROWS else "gemm"
+    plan = build_plan(_as_rows(x), base.weight, base.bias, a, b, scale)
+    width = base.out_features
 
-    def call(x):
-        shape = x.shape
-        x2 = x.reshape(-1, shape[-1])
-        if not x2.is_contiguous():
-            x2 = x2.contiguous()
-        return run(x2).reshape(*shape[:-1], out_features)
+    def run(x):
+        return plan(_as_rows(x)).reshape(*x.shape[:-1], width)
 
-    return module._active_adapter, rows, call
+    return run
 
 
-def _loraforge_linear_forward(self, x: torch.Tensor, *args, **kwargs):
-    """Drop-in inference forward for a PEFT LoRA Linear (peft_integration.py:199-232)."""
-    if args or kwargs or self.training or getattr(self, "merged", False) or getattr(self, "disable_adapters", False):
+def _patched_forward(self, x: torch.Tensor, *args, **kwargs):
+    """Inference forward of a patched PEFT LoRA Linear (peft_integration.py:199-232)."""
+    if args or kwargs or _bypassed(self):
         return self._loraforge_original_forward(x, *args, **kwargs)
     rows = x.numel() // x.shape[-1]
-    plan = getattr(self, "_loraforge_plan", None)
-    if (plan is None or plan[0] != self._active_adapter or plan[1] != rows
-            or plan[3] != self.scaling or plan[4] != (x.dtype, x.device)):
-        cache = self._loraforge_plans
-        key = (tuple(self.active_adapters), rows, tuple(self.scaling.items()), x.dtype, x.device)
-        plan = cache.get(key)
-        if plan is None:
-            adapter, plan_rows, call = _build_plan(self, x, rows)
-            adapter = adapter.copy() if isinstance(adapter, list) else adapter
-            plan = (adapter, plan_rows, call, dict(self.scaling), (x.dtype, x.device))
-            if len(cache) >= 2:
-                cache.pop(next(iter(cache)))
-            cache[key] = plan
-        self._loraforge_plan = plan
-    call = plan[2]
-    if call is not None:
-        return call(x)
-    return self._loraforge_original_forward(x)
+    key = _plan_key(self, x, rows)
+    cache = self._loraforge_plans
+    call = cache.lookup(key)
+    if call is None:
+        call = cache.store(key, _resolve(self, x, rows))
+    self._loraforge_plan = call
+    return call(x)
 
 
-def _patch_grouped_mlp(mlp_module) -> bool:
-    """Serve gate_proj and up_proj with one packed weight (peft_integration.py:270-411).
+# --------------------------------------------------------------- grouping
+class _SiblingGroup:
+    """Projections of one parent that read the same x, served by one packed linear.
 
-    The gate call computes both projections and caches up for the following
-    up call on the same input; anything unusual falls back to the individual
-    forwards.
+    The first member called with a new x computes every member's output and
+    keeps the others' for their own calls.  The key of that hand-off is x's
+    storage address, shape and version counter, so an x written in place in
+    between (or any other x) makes the member compute on its own.  Calls with
+    extra arguments, other dtypes, several or disabled adapters or merged
+    weights take the members' individual forwards.  So do 129..256-row calls
+    whose summed rank exceeds 64: the one-launch split-K linear serving that
+    row range takes ranks up to 64, and the individual projections measured
+    faster than the packed one there.
     """
-    gate_proj = mlp_module._modules.get("gate_proj")
-    up_proj = mlp_module._modules.get("up_proj")
-    if getattr(mlp_module, "_loraforge_grouped_mlp", False):
-        return False
-    if gate_proj is None or up_proj is None or not (is_lora_linear(gate_proj) and is_lora_linear(up_proj)):
-        return False
-    name = list(gate_proj.active_adapters)[0] if gate_proj.active_adapters else "default"
-    if name not in gate_proj.lora_A or name not in up_proj.lora_A:
-        return False
-    wg, wu = gate_proj.base_layer.weight, up_proj.base_layer.weight
-    a_g, a_u = gate_proj.lora_A[name].weight, up_proj.lora_A[name].weight
-    b_g, b_u = gate_proj.lora_B[name].weight, up_proj.lora_B[name].weight
-    rg, ru = a_g.shape[0], a_u.shape[0]
-    if rg + ru > 128 or wg.shape != wu.shape:
-        return False
-    dtype = wg.dtype
-    if not (
-        _inactive_dropout(gate_proj.lora_dropout[name]) and _inactive_dropout(up_proj.lora_dropout[name])
-        and all(t.dtype == dtype for t in (wu, a_g, a_u, b_g, b_u)) and dtype in (torch.float16, torch.bfloat16)
-        and gate_proj.base_layer.bias is None and up_proj.base_layer.bias is None
-    ):
-        return False
-    n, k = wg.shape
-    # Packed once: [W_g; W_u], [A_g; A_u], block-diagonal B with scales folded.
-    w_gu = torch.cat([wg, wu], dim=0).detach().contiguous()
-    a_gu = torch.cat([a_g, a_u], dim=0).detach().contiguous()
-    b_gu = torch.zeros((2 * n, rg + ru), device=wg.device, dtype=dtype)
-    b_gu[:n, :rg].copy_(b_g.detach().float() * float(gate_proj.scaling[name]))
-    b_gu[n:, rg:].copy_(b_u.detach().float() * float(up_proj.scaling[name]))
 
-    gate_individual = gate_proj.forward
-    up_individual = up_proj.forward
-    cache = {"key": None, "up": None}
-    plans = {}
+    def __init__(self, parent, names, members, adapter: str, tag: str):
+        self.parent, self.names, self.members, self.adapter, self.tag = parent, names, members, adapter, tag
+        ws = [m.base_layer.weight for m in members]
+        self.dtype = ws[0].dtype
+        self.widths = [w.shape[0] for w in ws]
+        ranks = [m.lora_A[adapter].weight.shape[0] for m in members]
+        self.rank = sum(ranks)
+        device = ws[0].device
+        self.weight = torch.cat([w.detach() for w in ws], dim=0).contiguous()
+        self.down = torch.cat([m.lora_A[adapter].weight.detach() for m in members], dim=0).contiguous()
+        self.up = torch.zeros((sum(self.widths), self.rank), device=device, dtype=self.dtype)
+        self.bias = None
+        if any(m.base_layer.bias is not None for m in members):
+            self.bias = torch.zeros((sum(self.widths),), device=device, dtype=self.dtype)
+        row = col = 0
+        for m, width, r in zip(members, self.widths, ranks):
+            scaled = m.lora_B[adapter].weight.detach().float() * float(m.scaling[adapter])
+            self.up[row:row + width, col:col + r].copy_(scaled)
+            if m.base_layer.bias is not None:
+                self.bias[row:row + width].copy_(m.base_layer.bias.detach())
+            row, col = row + width, col + r
+        self.individual = [m.forward for m in members]
+        self.plans: dict[int, object] = {}
+        self.handoff_key = None
+        self.handoff: dict[int, torch.Tensor] = {}
 
-    def gate_forward(self, x, *args, **kwargs):
-        rows = x.numel() // x.shape[-1]
-        if (
-            args or kwargs or list(self.active_adapters) != [name] or list(up_proj.active_adapters) != [name]
-            or getattr(self, "merged", False) or getattr(up_proj, "merged", False)
-            or getattr(self, "disable_adapters", False) or getattr(up_proj, "disable_adapters", False)
-            or not x.is_cuda or x.dtype != dtype
-        ):
-            cache["key"] = cache["up"] = None
-            return gate_individual(x, *args, **kwargs)
-        shape = x.shape
-        x2 = x.reshape(-1, shape[-1])
-        if not x2.is_contiguous():
-            x2 = x2.contiguous()
-        plan = plans.get(rows)
+    @staticmethod
+    def eligible(members, adapter: str, max_rank: int = 128) -> bool:
+        factors = [_adapter_factors(m, adapter) for m in members]
+        if any(f is None for f in factors) or any(list(m.active_adapters) != [adapter] for m in members):
+            return False
+        k = members[0].base_layer.weight.shape[1]
+        dtype = members[0].base_layer.weight.dtype
+        same = all(m.base_layer.weight.shape[1] == k and m.base_layer.weight.dtype == dtype for m in members)
+        return same and sum(f[0].shape[0] for f in factors) <= max_rank
+
+    def _packable(self, x, args, kwargs) -> bool:
+        if args or kwargs or not x.is_cuda or x.dtype != self.dtype:
+            return False
+        return all(list(m.active_adapters) == [self.adapter] and not getattr(m, "merged", False)
+                   and not getattr(m, "disable_adapters", False) for m in self.members)
+
+    def call(self, index: int, x: torch.Tensor, *args, **kwargs):
+        key = (x.data_ptr(), tuple(x.shape), x._version)
+        if not args and not kwargs and key == self.handoff_key and index in self.handoff:
+            return self.handoff.pop(index)
+        self.handoff_key, self.handoff = None, {}
+        if not self._packable(x, args, kwargs):
+            return self.individual[index](x, *args, **kwargs)
+        x2 = _as_rows(x)
+        rows = x2.shape[0]
+        if 128 < rows <= 256 and self.rank > 64:
+            self.parent._loraforge_grouped_choices[rows] = "individual"
+            return self.individual[index](x, *args, **kwargs)
+        plan = self.plans.get(rows)
         if plan is None:
-            plan = build_plan(x2, w_gu, None, a_gu, b_gu, 1.0)
-            plans[rows] = plan
-            mlp_module._loraforge_grouped_choices[rows] = "grouped"
-        both = plan(x2)
-        gate = both[:, :n].reshape(*shape[:-1], n)
-        up = both[:, n:].reshape(*shape[:-1], n)
-        cache["key"] = (x.data_ptr(), tuple(shape))
-        cache["up"] = up
-        return gate
+            plan = self.plans[rows] = build_plan(x2, self.weight, self.bias, self.down, self.up, 1.0)
+            self.parent._loraforge_grouped_choices[rows] = "grouped"
+        packed = plan(x2)
+        outs, c0 = {}, 0
+        for j, width in enumerate(self.widths):
+            outs[j] = packed[:, c0:c0 + width].reshape(*x.shape[:-1], width)
+            c0 += width
+        mine = outs.pop(index)
+        self.handoff_key, self.handoff = key, outs
+        return mine
 
-    def up_forward(self, x, *args, **kwargs):
-        key = (x.data_ptr(), tuple(x.shape))
-        if not args and not kwargs and cache["key"] == key and cache["up"] is not None:
-            result = cache["up"]
-            cache["key"] = cache["up"] = None
-            return result
-        cache["key"] = cache["up"] = None
-        return up_individual(x, *args, **kwargs)
+    def install(self) -> None:
+        for i, m in enumerate(self.members):
+            m._loraforge_individual_forward = self.individual[i]
 
-    gate_proj._loraforge_individual_forward = gate_individual
-    up_proj._loraforge_individual_forward = up_individual
-    gate_proj.forward = types.MethodType(gate_forward, gate_proj)
-    up_proj.forward = types.MethodType(up_forward, up_proj)
-    mlp_module._gate_up_packed = (w_gu, a_gu, b_gu)
-    mlp_module._loraforge_grouped_choices = {}
-    mlp_module._loraforge_grouped_timings_us = {}
-    mlp_module._loraforge_grouped_mlp = True
-    return True
+            def forward(module, x, *args, _i=i, **kwargs):
+                return self.call(_i, x, *args, **kwargs)
+
+            m.forward = types.MethodType(forward, m)
+        if "_loraforge_grouped_choices" not in self.parent.__dict__:
+            self.parent._loraforge_grouped_choices = {}
+            self.parent._loraforge_grouped_timings_us = {}
 
 
+def _group_siblings(parent, names, tag: str) -> _SiblingGroup | None:
+    """Pack ``parent``'s children ``names`` into one group if they qualify."""
+    if parent.__dict__.get(f"_loraforge_grouped_{tag}", False):
+        return None
+    members = [parent._modules.get(nm) for nm in names]  # direct children only (PEFT wrappers delegate getattr)
+    if any(m is None or not is_lora_linear(m) for m in members):
+        return None
+    active = list(members[0].active_adapters)
+    if len(active) != 1 or not _SiblingGroup.eligible(members, active[0]):
+        return None
+    group = _SiblingGroup(parent, names, members, active[0], tag)
+    group.install()
+    setattr(parent, f"_loraforge_grouped_{tag}", True)
+    return group
+
+
+MLP_GROUP = ("gate_proj", "up_proj")
 ATTENTION_GROUP = ("q_proj", "k_proj", "v_proj")
 
 
-def _patch_grouped_siblings(parent, names, tag: str) -> bool:
-    """Serve sibling projections that read the same x with ONE packed linear.
-
-    An extension beyond the reference (which groups only gate/up): for an
-    attention block's q, k and v (``names``), ``[W_q; W_k; W_v]`` and
-    ``[A_q; A_k; A_v]`` are packed once with a block-diagonal
-    ``[B_q*s_q, 0, 0; 0, B_k*s_k, 0; 0, 0, B_v*s_v]`` sidecar and the biases side
-    by side, so one plan (one shrink and one GEMM, or one small-M launch) reads x
-    once for all of them.  Output widths may differ (grouped-query attention).
-    Whichever member is called first with a new x computes every member's
-    output and keeps the others' for their own calls; the cache key is x's
-    storage, shape and version counter, so an x modified in place in between
-    takes the member's individual forward.  Anything unusual (other call
-    arguments, several or disabled adapters, merged weights, other dtypes)
-    also falls back to the individual forwards, and so do 129..256-row calls
-    whose summed rank exceeds 32 (measured slower packed there).  Measured at
-    K = N = 4096, r = 16 per projection: 8192 rows 829 -> 824 us, 16 rows
-    42.1 -> 39.7 us for the three projections.
-    """
-    mods = [parent._modules.get(nm) for nm in names]
-    if any(m is None or not is_lora_linear(m) for m in mods):
+def _patch_grouped_mlp(mlp_module) -> bool:
+    """Serve gate_proj and up_proj with one packed linear (peft_integration.py:270-411)."""
+    group = _group_siblings(mlp_module, MLP_GROUP, "mlp")
+    if group is None:
         return False
-    if getattr(parent, "_loraforge_grouped_" + tag, False):
-        return False
-    name = list(mods[0].active_adapters)[0] if mods[0].active_adapters else "default"
-    ws, bs, a_s, b_s, ranks = [], [], [], [], []
-    for m in mods:
-        if name not in m.lora_A or list(m.active_adapters) != [name] or not isinstance(m.base_layer, torch.nn.Linear):
-            return False
-        if not _inactive_dropout(m.lora_dropout[name]) or (getattr(m, "use_dora", {}) or {}).get(name, False):
-            return False
-        ws.append(m.base_layer.weight)
-        bs.append(m.base_layer.bias)
-        a_s.append(m.lora_A[name].weight)
-        b_s.append(m.lora_B[name].weight)
-        ranks.append(a_s[-1].shape[0])
-    dtype = ws[0].dtype
-    k = ws[0].shape[1]
-    if dtype not in (torch.float16, torch.bfloat16) or sum(ranks) > 128:
-        return False
-    if any(w.shape[1] != k or w.dtype != dtype for w in ws) or any(t.dtype != dtype for t in a_s + b_s):
-        return False
-    widths = [w.shape[0] for w in ws]
-    n_all, r_all = sum(widths), sum(ranks)
-    w_pack = torch.cat(ws, dim=0).detach().contiguous()
-    a_pack = torch.cat(a_s, dim=0).detach().contiguous()
-    b_pack = torch.zeros((n_all, r_all), device=ws[0].device, dtype=dtype)
-    bias_pack = None
-    if any(b is not None for b in bs):
-        bias_pack = torch.zeros((n_all,), device=ws[0].device, dtype=dtype)
-    n0 = r0 = 0
-    for m, w, bias, bb, r in zip(mods, ws, bs, b_s, ranks):
-        b_pack[n0:n0 + w.shape[0], r0:r0 + r].copy_(bb.detach().float() * float(m.scaling[name]))
-        if bias is not None:
-            bias_pack[n0:n0 + w.shape[0]].copy_(bias.detach())
-        n0 += w.shape[0]
-        r0 += r
-    individual = [m.forward for m in mods]
-    cache = {"key": None, "outs": {}}
-    plans = {}
-
-    def member_forward(i):
-        def forward(self, x, *args, **kwargs):
-            key = (x.data_ptr(), tuple(x.shape), x._version)
-            if not args and not kwargs and cache["key"] == key and i in cache["outs"]:
-                return cache["outs"].pop(i)
-            cache["key"], cache["outs"] = None, {}
-            if (
-                args or kwargs or not x.is_cuda or x.dtype != dtype
-                or any(list(m.active_adapters) != [name] or getattr(m, "merged", False)
-                       or getattr(m, "disable_adapters", False) for m in mods)
-            ):
-                return individual[i](x, *args, **kwargs)
-            shape = x.shape
-            x2 = x.reshape(-1, shape[-1])
-            if not x2.is_contiguous():
-                x2 = x2.contiguous()
-            rows = x2.shape[0]
-            if 128 < rows <= 256 and r_all > 64:
-                # the one-launch split-K linear of this row range takes ranks <= 64
-                # only: the individual projections measured faster here than the
-                # pack with its summed rank
-                return individual[i](x, *args, **kwargs)
-            plan = plans.get(rows)
-            if plan is None:
-                plan = build_plan(x2, w_pack, bias_pack, a_pack, b_pack, 1.0)
-                plans[rows] = plan
-                parent._loraforge_grouped_choices[rows] = "grouped"
-            packed = plan(x2)
-            outs, c0 = {}, 0
-            for j, wd in enumerate(widths):
-                outs[j] = packed[:, c0:c0 + wd].reshape(*shape[:-1], wd)
-                c0 += wd
-            mine = outs.pop(i)
-            cache["key"], cache["outs"] = key, outs
-            return mine
-        return forward
-
-    for i, m in enumerate(mods):
-        m._loraforge_individual_forward = individual[i]
-        m.forward = types.MethodType(member_forward(i), m)
-    setattr(parent, "_" + tag + "_packed", (w_pack, a_pack, b_pack, bias_pack))
-    if not hasattr(parent, "_loraforge_grouped_choices"):
-        parent._loraforge_grouped_choices = {}
-    setattr(parent, "_loraforge_grouped_" + tag, True)
+    mlp_module._gate_up_packed = (group.weight, group.down, group.up)
     return True
+
+
+def _patch_grouped_siblings(parent, names, tag: str) -> bool:
+    """Serve sibling projections ``names`` of ``parent`` with one packed linear.
+
+    Used for an attention block's q, k and v (an extension: the reference
+    groups only gate/up).  Output widths may differ (grouped-query attention).
+    Measured at K = N = 4096, r = 16 per projection: 8192 rows 829 -> 824 us,
+    16 rows 42.1 -> 39.7 us for the three projections.
+    """
+    group = _group_siblings(parent, names, tag)
+    if group is None:
+        return False
+    setattr(parent, f"_{tag}_packed", (group.weight, group.down, group.up, group.bias))
+    return True
+
+
+# ------------------------------------------------------------ public API
+def _cast_adapters(module) -> None:
+    """Bring the active adapters' factors to the base weight's half dtype (PEFT
+    often keeps them in fp32 for training)."""
+    if not isinstance(module.base_layer, torch.nn.Linear):
+        return
+    target = module.base_layer.weight.dtype
+    if target not in _HALF:
+        return
+    for adapter in module.active_adapters:
+        for table in (module.lora_A, module.lora_B):
+            if adapter in table:
+                table[adapter].to(dtype=target)
 
 
 def enable_loraforge_peft(model, enable_grouping: bool = True, cast_adapter_dtype: bool = True,
                           group_attention: bool | None = None) -> int:
-    """Patch supported PEFT LoRA Linear modules for inference (peft_integration.py:414-448).
+    """Patch the model's PEFT LoRA Linear modules for inference; returns how many
+    were patched (peft_integration.py:414-448).
 
-    ``group_attention`` (default: the ``LORAFORGE_GROUPED_ATTN`` environment
-    variable, off) additionally packs each attention block's q, k and v
-    projections into one linear that reads x once (``_patch_grouped_siblings``);
-    the reference has no such grouping.
+    ``cast_adapter_dtype`` casts active adapter factors to the base dtype
+    (pass False to keep PEFT's fp32 sidecars, which then take PEFT's forward).
+    ``enable_grouping`` packs MLP gate/up pairs; ``group_attention`` (default:
+    ``LORAFORGE_GROUPED_ATTN``, off) packs q/k/v.
     """
-    count = 0
-    for module in model.modules():
-        if is_lora_linear(module) and not hasattr(module, "_loraforge_original_forward"):
-            if cast_adapter_dtype and isinstance(module.base_layer, torch.nn.Linear):
-                target_dtype = module.base_layer.weight.dtype
-                if target_dtype in (torch.float16, torch.bfloat16):
-                    for name in module.active_adapters:
-                        if name in module.lora_A and name in module.lora_B:
-                            module.lora_A[name].to(dtype=target_dtype)
-                            module.lora_B[name].to(dtype=target_dtype)
-            module._loraforge_original_forward = module.forward
-            module._loraforge_plan = None
-            module._loraforge_plans = {}
-            module.forward = types.MethodType(_loraforge_linear_forward, module)
-            count += 1
-    grouped = 0
+    patched = 0
+    for module in list(model.modules()):
+        if not is_lora_linear(module) or "_loraforge_original_forward" in module.__dict__:
+            continue
+        if cast_adapter_dtype:
+            _cast_adapters(module)
+        module._loraforge_original_forward = module.forward
+        module._loraforge_plan = None
+        module._loraforge_plans = _PlanCache()
+        module.forward = types.MethodType(_patched_forward, module)
+        patched += 1
+
     if enable_grouping and os.environ.get("LORAFORGE_GROUPED_MLP", "").strip().lower() != "individual":
-        for module in model.modules():
-            if _patch_grouped_mlp(module):
-                grouped += 1
-    model._loraforge_grouped_mlp_count = grouped
+        for m in list(model.modules()):
+            _patch_grouped_mlp(m)
     if group_attention is None:
         group_attention = os.environ.get("LORAFORGE_GROUPED_ATTN", "").strip().lower() in ("1", "true", "yes")
-    grouped_attn = 0
     if group_attention:
-        for module in model.modules():
-            if _patch_grouped_siblings(module, ATTENTION_GROUP, "attention"):
-                grouped_attn += 1
-    model._loraforge_grouped_attention_count = grouped_attn
-    return count
+        for m in list(model.modules()):
+            _patch_grouped_siblings(m, ATTENTION_GROUP, "attention")
+    # groups installed in the model so far (a repeated call counts earlier ones too)
+    model._loraforge_grouped_mlp_count = sum(
+        bool(m.__dict__.get("_loraforge_grouped_mlp")) for m in model.modules())
+    model._loraforge_grouped_attention_count = sum(
+        bool(m.__dict__.get("_loraforge_grouped_attention")) for m in model.modules())
+    return patched
 
 
 def peft_plan_report(model) -> dict:
-    """Summarize selected implementations (peft_integration.py:451-479)."""
-    choices = Counter()
-    timing_samples = []
-    grouped_choices = Counter()
-    grouped_timing_samples = []
+    """Which path each patched module and group took (peft_integration.py:451-479)."""
+    decode = Counter()
+    decode_samples = []
+    grouped = Counter()
+    grouped_samples = []
     for module in model.modules():
-        choice = module.__dict__.get("_loraforge_decode_choice")
+        state = module.__dict__  # not getattr: PEFT wrappers delegate attribute lookups
+        choice = state.get("_loraforge_decode_choice")
         if choice is not None:
-            choices[choice] += 1
-            timing_samples.append({"choice": choice,
-                                   "timings_us": module.__dict__.get("_loraforge_decode_timings_us", {})})
-        for rows, grouped_choice in module.__dict__.get("_loraforge_grouped_choices", {}).items():
-            grouped_choices[grouped_choice] += 1
-            grouped_timing_samples.append({"rows": rows, "choice": grouped_choice, "timings_us": {}})
+            decode[choice] += 1
+            decode_samples.append({"choice": choice, "timings_us": state.get("_loraforge_decode_timings_us", {})})
+        timings = state.get("_loraforge_grouped_timings_us", {})
+        for rows, how in state.get("_loraforge_grouped_choices", {}).items():
+            grouped[how] += 1
+            grouped_samples.append({"rows": rows, "choice": how, "timings_us": timings.get(rows, {})})
     return {
-        "decode_choices": dict(choices),
+        "decode_choices": dict(decode),
         "grouped_mlp_modules": getattr(model, "_loraforge_grouped_mlp_count", 0),
         "grouped_attention_modules": getattr(model, "_loraforge_grouped_attention_count", 0),
-        "decode_timing_samples": timing_samples,
-        "grouped_mlp_choices": dict(grouped_choices),
-        "grouped_mlp_timing_samples": grouped_timing_samples,
+        "decode_timing_samples": decode_samples,
+        "grouped_mlp_choices": dict(grouped),
+        "grouped_mlp_timing_samples": grouped_samples,
     }

@@ -1,9 +1,19 @@
-"""Attach LoRA sidecars to plain ``nn.Linear`` layers as fused modules.
+"""Runtime (unmerged) LoRA on plain ``nn.Linear`` layers, served by the fused kernels.
 
-Drop-in for ``loraforge_kernels.runtime_lora`` (runtime_lora.py:1-69).  A second
-attach on the same path stacks adapters by concatenation, which is exact:
-``a1*B1@A1 + a2*B2@A2 == [B1|B2] @ [a1*A1; a2*A2]`` with the second adapter's
-alpha folded into its shrink factor relative to the layer's scale.
+Drop-in for ``loraforge_kernels.runtime_lora`` (runtime_lora.py:1-69):
+``attach_fused_lora`` replaces the ``nn.Linear`` found at a dotted path with a
+:class:`FusedLoRALinear` that keeps the base weight untouched and runs the
+adapter inside the base GEMM.  Attaching again at the same path adds the new
+adapter to the stack.
+
+Stacking algebra.  A layer carrying adapters (A_i, B_i, alpha_i) computes
+``x W^T + sum_i alpha_i (x A_i^T) B_i^T``.  The fused layer holds one scale s
+(the first adapter's alpha) and one pair of factors, so the i-th adapter
+enters as the rank block ``A_i * (alpha_i / s)`` of the down factor and the
+column block ``B_i`` of the up factor: ``s [A_1; (a_2/s) A_2] ... `` times
+``[B_1 | B_2]`` reproduces the sum exactly, and the kernels see one adapter of
+the summed rank.  The ratio is applied in fp32 and the result rounded once to
+the layer's dtype, which is the reference's rounding (runtime_lora.py:49-53).
 """
 
 from __future__ import annotations
@@ -15,42 +25,53 @@ from .fused_linear import FusedLoRALinear
 
 
 def resolve_parent(root: nn.Module, dotted_path: str) -> tuple[nn.Module, str]:
-    """Split ``"a.b.c"`` into the module holding ``c`` and the attribute name."""
-    parts = dotted_path.split(".")
-    parent = root
-    for part in parts[:-1]:
-        parent = getattr(parent, part)
-    return parent, parts[-1]
+    """The module that owns the last component of ``dotted_path``, and that component's name."""
+    owner_path, _, leaf = dotted_path.rpartition(".")
+    owner = root
+    for step in owner_path.split(".") if owner_path else ():
+        owner = getattr(owner, step)
+    return owner, leaf
+
+
+def _with_extra_adapter(layer: FusedLoRALinear, down: torch.Tensor, up: torch.Tensor, alpha: float):
+    """``layer``'s factors with one more adapter appended as a new rank block."""
+    device, dtype = layer.weight.device, layer.weight.dtype
+    ratio = float(alpha) / layer.scale
+    down_block = (down.detach().to(device=device, dtype=torch.float32) * ratio).to(dtype)
+    up_block = up.detach().to(device=device, dtype=dtype)
+    return torch.cat((layer.lora_a, down_block), dim=0), torch.cat((layer.lora_b, up_block), dim=1)
 
 
 def attach_fused_lora(root: nn.Module, dotted_path: str, down: torch.Tensor, up: torch.Tensor,
                       alpha: float = 1.0) -> FusedLoRALinear:
-    """Give the ``nn.Linear`` at ``dotted_path`` a fused LoRA sidecar (runtime_lora.py:29-61)."""
-    parent, attr = resolve_parent(root, dotted_path)
-    target = getattr(parent, attr)
+    """Serve the ``nn.Linear`` at ``dotted_path`` with a fused LoRA sidecar (runtime_lora.py:29-61).
 
-    if isinstance(target, FusedLoRALinear):
-        device, dtype = target.weight.device, target.weight.dtype
-        # Fold the new adapter's alpha into its shrink factor so the stack can
-        # share the single scale the layer already carries.
-        folded = (alpha / target.scale) * down.detach().to(device=device, dtype=torch.float32)
-        target.set_factors(
-            torch.cat([target.lora_a, folded.to(dtype)], dim=0),
-            torch.cat([target.lora_b, up.detach().to(device=device, dtype=dtype)], dim=1),
-        )
-        return target
+    ``down`` is lora_A.weight ``[r, in]``, ``up`` is lora_B.weight ``[out, r]``
+    and ``alpha`` the adapter's scale.  A path that already holds a fused layer
+    gets the adapter stacked onto it; anything other than an ``nn.Linear`` is
+    refused with ``TypeError``.  Returns the fused layer.
+    """
+    owner, leaf = resolve_parent(root, dotted_path)
+    current = getattr(owner, leaf)
+    if isinstance(current, FusedLoRALinear):
+        current.set_factors(*_with_extra_adapter(current, down, up, alpha))
+        return current
+    if not isinstance(current, nn.Linear):
+        raise TypeError(f"LoRA target {dotted_path} is {type(current).__name__}, not nn.Linear")
+    replacement = FusedLoRALinear(current, down, up, scale=alpha)
+    setattr(owner, leaf, replacement)
+    return replacement
 
-    if not isinstance(target, nn.Linear):
-        raise TypeError(f"LoRA target {dotted_path} is {type(target).__name__}, not nn.Linear")
 
-    fused = FusedLoRALinear(target, down, up, scale=alpha)
-    setattr(parent, attr, fused)
-    return fused
+def _fused_layers(root: nn.Module):
+    return [m for m in root.modules() if isinstance(m, FusedLoRALinear)]
 
 
 def fused_lora_module_count(root: nn.Module) -> int:
-    return sum(1 for module in root.modules() if isinstance(module, FusedLoRALinear))
+    """How many fused LoRA layers ``root`` contains."""
+    return len(_fused_layers(root))
 
 
 def total_fused_rank(root: nn.Module) -> int:
-    return sum(module.rank for module in root.modules() if isinstance(module, FusedLoRALinear))
+    """Sum of the (stacked) ranks of every fused LoRA layer under ``root``."""
+    return sum(layer.rank for layer in _fused_layers(root))

@@ -65,16 +65,37 @@ def local_segments(seg_start: torch.Tensor, seg_adapter: torch.Tensor, world: in
     return t0, t1, (seg_start[s0:s1 + 1] - t0).contiguous(), seg_adapter[s0:s1].contiguous()
 
 
-def gather_rows(local: torch.Tensor, total_rows: int, group=None) -> torch.Tensor:
-    """All-gather row shards (``shard_rows`` layout) into a full ``[total_rows, ...]`` tensor."""
+def gather_rows(local: torch.Tensor, total_rows: int, group=None, out: torch.Tensor | None = None) -> torch.Tensor:
+    """All-gather row shards (``shard_rows`` layout) into a full ``[total_rows, ...]`` tensor.
+
+    One ``all_gather_into_tensor`` (NCCL over NVLink on GPUs).  When every rank
+    holds the same number of rows the ranks' shards land directly in their
+    places of the result (``out`` if given); otherwise shorter shards are padded
+    by one row for the collective and the result is compacted by one gather of
+    rows.
+    """
     world = dist.get_world_size(group)
     sizes = [shard_rows(total_rows, world, r) for r in range(world)]
     width = max(b - a for a, b in sizes)
-    padded = local.new_zeros((width,) + tuple(local.shape[1:]))
+    tail = tuple(local.shape[1:])
+    if local.shape[0] != sizes[dist.get_rank(group)][1] - sizes[dist.get_rank(group)][0]:
+        raise ValueError(f"gather_rows: this rank holds {local.shape[0]} rows, its shard of {total_rows} is "
+                         f"{sizes[dist.get_rank(group)]}")
+    if width * world == total_rows:
+        if out is None:
+            out = local.new_empty((total_rows,) + tail)
+        dist.all_gather_into_tensor(out, local.contiguous(), group=group)
+        return out
+    padded = local.new_zeros((width,) + tail)
     padded[: local.shape[0]] = local
-    parts = [torch.empty_like(padded) for _ in range(world)]
-    dist.all_gather(parts, padded, group=group)
-    return torch.cat([p[: b - a] for p, (a, b) in zip(parts, sizes)], dim=0)
+    stacked = local.new_empty((width * world,) + tail)
+    dist.all_gather_into_tensor(stacked, padded, group=group)
+    keep = torch.cat([torch.arange(r * width, r * width + (b - a)) for r, (a, b) in enumerate(sizes)])
+    rows = stacked.index_select(0, keep.to(stacked.device))
+    if out is not None:
+        out.copy_(rows)
+        return out
+    return rows
 
 
 class ShardedLoRALinear(torch.nn.Module):

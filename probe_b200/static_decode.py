@@ -1,121 +1,154 @@
-"""CUDA-graph greedy decoding for a fixed Transformers model and adapter.
+"""Greedy decoding replayed from one CUDA graph per step.
 
-Drop-in for ``loraforge_kernels.static_decode`` (static_decode.py:1-120): the
-prompt is prefilled eagerly into a Transformers ``StaticCache``; every decode
-step after it -- the model forward at one token per sequence, the argmax, the
-position and the additive attention mask -- is one captured CUDA graph that
-is replayed.  The LoRA linears of this package run inside it (their plans are
-resolved by the warm-up steps before capture; the small-M decode kernels need
-no workspace).
+Drop-in for ``loraforge_kernels.static_decode`` (static_decode.py:1-120).  The
+prompt is prefilled eagerly into a Transformers ``StaticCache``; the decode
+step -- model forward at one token per sequence, argmax, the new token's
+write into the output row, position and additive-mask update -- is captured
+once and replayed for every further token, so a step costs one graph launch
+instead of hundreds of kernel launches.  This package's LoRA linears run
+inside the graph (their plans and workspaces are set up by the warm-up steps,
+which run on the capture stream before capture).
 
-Fixed-length greedy only: no EOS stop, sampling, beams, padding or adapter
-switching.  Build a new runner after changing weights, adapters, batch size or
-length.  The model must support ``StaticCache`` and a 4-D additive mask.
+Design: every tensor the step touches lives in the runner at a fixed address.
+``history`` holds the whole output sequence; the captured step scatters its
+new token to column ``position + 1``, so a generation is a prefill, replays
+and one copy of ``history`` -- no per-step host work.
+
+Limits: fixed batch, prompt length and token count; greedy only (no EOS stop,
+sampling, beams, padding or adapter switching).  Build a new runner after
+changing weights, adapters, batch size or lengths.  The model must accept a
+``StaticCache`` and a 4-D additive attention mask.
 """
 
 from __future__ import annotations
 
 import torch
 
+_WARMUP_STEPS = 2      # eager steps on the capture stream before capture
+_SPARE_POSITIONS = 4   # cache slots beyond the generated tokens (warm-up and capture steps write there)
+
+
+def _check_prompt(ids: torch.Tensor, new_tokens: int) -> None:
+    shaped = ids.ndim == 2 and ids.is_cuda and ids.dtype == torch.long
+    if not shaped or new_tokens < 1:
+        raise ValueError("Expected CUDA [batch, prefix] IDs and new_tokens >= 1")
+    if ids.shape[1] == 0:
+        raise ValueError("A nonempty unpadded prefix is required")
+
 
 class StaticDecodeRunner:
-    """Greedy generation of exactly ``new_tokens`` tokens for a fixed batch
-    and prompt length (static_decode.py:11-120).  Returned token tensors belong
-    to the caller; the graph's buffers stay inside the runner."""
+    """Generate exactly ``new_tokens`` greedy tokens for a fixed batch and
+    prompt length (static_decode.py:11-120).
+
+    ``runner(ids)`` returns a fresh ``[batch, prefix + new_tokens]`` int64
+    tensor owned by the caller; ``runner(ids, replay=False)`` runs the same
+    steps eagerly; ``validate(ids)`` compares replayed and eager logits.
+    """
 
     @torch.inference_mode()
     def __init__(self, model, example_ids: torch.Tensor, new_tokens: int):
         from transformers import StaticCache
 
-        if example_ids.ndim != 2 or not example_ids.is_cuda or example_ids.dtype != torch.long or new_tokens < 1:
-            raise ValueError("Expected CUDA [batch, prefix] IDs and new_tokens >= 1")
+        _check_prompt(example_ids, new_tokens)
         if model.training:
             raise ValueError("Call model.eval() before capturing inference")
         self.model = model
-        self.batch, self.prefix = example_ids.shape
-        if self.prefix == 0:
-            raise ValueError("A nonempty unpadded prefix is required")
-        self.new_tokens = new_tokens
-        self.capacity = self.prefix + new_tokens + 4
-        dev = example_ids.device
+        self.batch, self.prefix = (int(v) for v in example_ids.shape)
+        self.new_tokens = int(new_tokens)
+        self.capacity = self.prefix + self.new_tokens + _SPARE_POSITIONS
+        device = example_ids.device
         self.cache = StaticCache(config=model.config, max_cache_len=self.capacity)
-        # graph inputs / outputs: fixed addresses, updated in place
-        self.token = torch.empty((self.batch, 1), device=dev, dtype=torch.long)
-        self.position = torch.full_like(self.token, self.prefix)
-        self.columns = torch.arange(self.capacity, device=dev)
-        self.mask = torch.empty((self.batch, 1, 1, self.capacity), device=dev, dtype=model.dtype)
-        self.prefix_mask = torch.ones_like(example_ids)
-        self._prefill(example_ids)
-        # Plans, lazily built tables and cache allocations must exist before
-        # capture: two eager steps on throw-away cache state.
-        for _ in range(2):
-            self._step()
-        torch.cuda.synchronize()
+        # fixed-address state read and written by the captured step
+        self.history = torch.zeros((self.batch, self.capacity), device=device, dtype=torch.long)
+        self.token = torch.zeros((self.batch, 1), device=device, dtype=torch.long)
+        self.position = torch.zeros((self.batch, 1), device=device, dtype=torch.long)
+        self._columns = torch.arange(self.capacity, device=device)
+        self.mask = torch.zeros((self.batch, 1, 1, self.capacity), device=device, dtype=model.dtype)
+        self._prompt_mask = torch.ones((self.batch, self.prefix), device=device, dtype=torch.long)
+        self._mask_fill = torch.finfo(model.dtype).min
+        self.step_logits = None
+
+        self._start(example_ids)
+        capture_stream = torch.cuda.Stream(device)
+        capture_stream.wait_stream(torch.cuda.current_stream(device))
+        with torch.cuda.stream(capture_stream):
+            for _ in range(_WARMUP_STEPS):  # plans, workspaces and cache buffers appear here, not in capture
+                self._advance()
+        torch.cuda.current_stream(device).wait_stream(capture_stream)
+        torch.cuda.synchronize(device)
         self.graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(self.graph):
-            self._step()
+        with torch.cuda.graph(self.graph, stream=capture_stream):
+            self._advance()
         self.graph_logits = self.step_logits
-        # The graph holds device addresses, not Python references: keep every
-        # parameter and buffer it read alive as long as the runner.
-        self._captured = tuple(model.parameters()) + tuple(model.buffers())
+        # The graph refers to device addresses only; hold the tensors behind them.
+        self._keepalive = (tuple(model.parameters()), tuple(model.buffers()))
 
-    def _update_mask(self):
-        visible = self.columns[None, :] <= self.position  # [batch, capacity]
-        self.mask.copy_(torch.where(visible, 0.0, torch.finfo(self.mask.dtype).min)[:, None, None, :])
+    # -------------------------------------------------------------- steps
+    def _refresh_mask(self) -> None:
+        hidden = self._columns[None, :] > self.position  # [batch, capacity]: columns not yet visible
+        self.mask.zero_()
+        self.mask.masked_fill_(hidden[:, None, None, :], self._mask_fill)
 
-    def _prefill(self, input_ids):
+    def _start(self, ids: torch.Tensor) -> None:
+        """Prefill the prompt; the first new token goes to column ``prefix``."""
         self.cache.reset()
-        out = self.model(input_ids=input_ids, attention_mask=self.prefix_mask, past_key_values=self.cache,
-                         use_cache=True, logits_to_keep=1)
-        self.token.copy_(out.logits[:, -1].argmax(-1, keepdim=True))
+        logits = self.model(input_ids=ids, attention_mask=self._prompt_mask, past_key_values=self.cache,
+                            use_cache=True, logits_to_keep=1).logits[:, -1]
+        self.token.copy_(torch.argmax(logits, dim=-1, keepdim=True))
+        self.history[:, : self.prefix].copy_(ids)
+        self.history[:, self.prefix: self.prefix + 1].copy_(self.token)
         self.position.fill_(self.prefix)
-        self._update_mask()
+        self._refresh_mask()
 
-    def _step(self):
-        out = self.model(input_ids=self.token, position_ids=self.position, attention_mask=self.mask,
-                         past_key_values=self.cache, use_cache=True, logits_to_keep=1)
-        self.step_logits = out.logits[:, -1]
-        self.token.copy_(self.step_logits.argmax(-1, keepdim=True))
+    def _advance(self) -> None:
+        """Feed ``token`` at ``position``; write the next token to column position + 1."""
+        logits = self.model(input_ids=self.token, position_ids=self.position, attention_mask=self.mask,
+                            past_key_values=self.cache, use_cache=True, logits_to_keep=1).logits[:, -1]
+        self.step_logits = logits
+        self.token.copy_(torch.argmax(logits, dim=-1, keepdim=True))
+        self.history.scatter_(1, self.position + 1, self.token)
         self.position.add_(1)
-        self._update_mask()
+        self._refresh_mask()
 
-    @torch.inference_mode()
-    def validate(self, input_ids, tolerance: float = 0.01) -> float:
-        """Largest relative L2 difference between replayed and eager logits on
-        the same teacher-forced tokens (argmax ties may flip under rounding, so
-        the trajectories are matched rather than compared).  Raises above
-        ``tolerance``."""
-        self._prefill(input_ids)
-        tokens, logits = [], []
-        for _ in range(1, self.new_tokens):
-            tokens.append(self.token.clone())
-            self._step()
-            logits.append(self.step_logits.clone())
-        self._prefill(input_ids)
-        worst = 0.0
-        for tok, ref in zip(tokens, logits):
-            self.token.copy_(tok)
-            self.graph.replay()
-            err = float(torch.linalg.vector_norm(self.graph_logits.float() - ref.float())
-                        / torch.linalg.vector_norm(ref.float()).clamp_min(1e-8))
-            worst = max(worst, err)
-        if worst > tolerance:
-            raise AssertionError(f"Captured decode logit relative L2 error {worst:.4g} > {tolerance}")
-        return worst
-
-    @torch.inference_mode()
-    def __call__(self, input_ids, *, replay: bool = True) -> torch.Tensor:
-        if (input_ids.shape != (self.batch, self.prefix) or input_ids.device != self.token.device
-                or input_ids.dtype != torch.long):
+    # ------------------------------------------------------------ public
+    def _check_request(self, ids: torch.Tensor) -> None:
+        if tuple(ids.shape) != (self.batch, self.prefix) or ids.device != self.token.device \
+                or ids.dtype != torch.long:
             raise ValueError("Input must match the captured batch, prefix, device and int64 dtype")
-        self._prefill(input_ids)
-        result = torch.empty((self.batch, self.prefix + self.new_tokens), device=input_ids.device, dtype=torch.long)
-        result[:, : self.prefix].copy_(input_ids)
-        result[:, self.prefix: self.prefix + 1].copy_(self.token)
-        for step in range(1, self.new_tokens):
+
+    @torch.inference_mode()
+    def __call__(self, input_ids: torch.Tensor, *, replay: bool = True) -> torch.Tensor:
+        self._check_request(input_ids)
+        self._start(input_ids)
+        for _ in range(self.new_tokens - 1):
             if replay:
                 self.graph.replay()
             else:
-                self._step()
-            result[:, self.prefix + step: self.prefix + step + 1].copy_(self.token)
-        return result
+                self._advance()
+        return self.history[:, : self.prefix + self.new_tokens].clone()
+
+    @torch.inference_mode()
+    def validate(self, input_ids: torch.Tensor, tolerance: float = 0.01) -> float:
+        """Worst relative L2 distance between replayed and eager step logits.
+
+        Both runs are fed the same (eager) tokens: near an argmax tie bf16
+        rounding could send free-running trajectories apart, which would say
+        nothing about the graph.  Raises ``AssertionError`` above ``tolerance``.
+        """
+        self._check_request(input_ids)
+        self._start(input_ids)
+        fed, eager = [], []
+        for _ in range(self.new_tokens - 1):
+            fed.append(self.token.clone())
+            self._advance()
+            eager.append(self.step_logits.float().clone())
+        self._start(input_ids)
+        worst = 0.0
+        for token, ref in zip(fed, eager):
+            self.token.copy_(token)
+            self.graph.replay()
+            diff = torch.linalg.vector_norm(self.graph_logits.float() - ref)
+            worst = max(worst, float(diff / torch.linalg.vector_norm(ref).clamp_min(1e-8)))
+        if worst > tolerance:
+            raise AssertionError(f"Captured decode logit relative L2 error {worst:.4g} > {tolerance}")
+        return worst

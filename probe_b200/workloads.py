@@ -33,6 +33,8 @@ class Projection:
     b: torch.Tensor          # [N, r]
     scale: float
     bias: torch.Tensor | None = None
+    # the adapters behind a stacked (a, b): (down [r_i, K], up [N, r_i], alpha_i), input dtype
+    adapters: list = field(default_factory=list)
 
     @property
     def m(self) -> int:
@@ -182,21 +184,33 @@ def c3(device="cpu", dtype=torch.float32, tokens=4096, segments=128, n_adapters=
                      scales, a_list, b_list)
 
 
+def stack_folded(adapters, dtype):
+    """Stack adapters the way ``attach_fused_lora`` does: the first alpha is the
+    layer's scale, every later down factor is multiplied by alpha_i / alpha_0 in
+    fp32 and rounded back to ``dtype``, and the factors are concatenated along
+    the rank.  Returns (a [sum r, K], b [N, sum r], scale)."""
+    scale = float(adapters[0][2])
+    a_parts = [adapters[0][0].to(dtype)]
+    for down, _, alpha in adapters[1:]:
+        a_parts.append(((float(alpha) / scale) * down.float()).to(dtype))
+    a = torch.cat(a_parts, 0).contiguous()
+    b = torch.cat([up.to(dtype) for _, up, _ in adapters], 1).contiguous()
+    return a, b, scale
+
+
 def _projection(g, name, m, k, n, ranks_scales, device, dtype, x=None):
-    """One projection; adapters stacked with attach_fused_lora semantics (first alpha = layer scale)."""
+    """One projection whose adapters (drawn per rank, stored in ``dtype`` like
+    adapter files) are stacked with attach_fused_lora semantics."""
     if x is None:
         x = _randn(g, (m, k), 1.0, device, dtype)
     w = _randn(g, (n, k), 1 / math.sqrt(k), device, dtype)
-    a_blocks, b_blocks = [], []
-    base_scale = ranks_scales[0][1]
+    adapters = []
     for r, s in ranks_scales:
-        a = _randn(g, (r, k), 1 / math.sqrt(k), device, torch.float32)
-        b = _randn(g, (n, r), 1 / math.sqrt(r), device, torch.float32)
-        a_blocks.append((s / base_scale) * a)
-        b_blocks.append(b)
-    a = torch.cat(a_blocks, 0).to(dtype)
-    b = torch.cat(b_blocks, 1).to(dtype).contiguous()
-    return Projection(name, k, n, x, w, a, b, base_scale)
+        down = _randn(g, (r, k), 1 / math.sqrt(k), device, dtype)
+        up = _randn(g, (n, r), 1 / math.sqrt(r), device, dtype)
+        adapters.append((down, up, s))
+    a, b, scale = stack_folded(adapters, dtype)
+    return Projection(name, k, n, x, w, a, b, scale, adapters=adapters)
 
 
 def c4(device="cuda", dtype=torch.bfloat16, m=8192) -> list[Projection]:
@@ -207,13 +221,32 @@ def c4(device="cuda", dtype=torch.bfloat16, m=8192) -> list[Projection]:
     return [_projection(g, nm, m, k, n, [(16, 2.0)], device, dtype) for nm, k, n in shapes]
 
 
-def c5(device="cuda", dtype=torch.bfloat16, m=32760) -> list[Projection]:
-    """C5: Wan DiT projections, M = 32760 tokens, 3-LoRA stack r = 32/64/128 with weights 1.0/0.7/0.4."""
+C5_STACK = ((32, 1.0), (64, 0.7), (128, 0.4))
+C5_SHAPES = (("q", HIDDEN_WAN, HIDDEN_WAN), ("k", HIDDEN_WAN, HIDDEN_WAN), ("v", HIDDEN_WAN, HIDDEN_WAN),
+             ("o", HIDDEN_WAN, HIDDEN_WAN), ("ffn_up", HIDDEN_WAN, FFN_WAN), ("ffn_down", FFN_WAN, HIDDEN_WAN))
+
+
+def c5(device="cuda", dtype=torch.bfloat16, m=32760, only=None, rows=None) -> list[Projection]:
+    """C5: Wan DiT projections, M = 32760 tokens, 3-LoRA stack r = 32/64/128 with weights 1.0/0.7/0.4.
+
+    ``only`` keeps a subset of the projection names; the draws of the others
+    still happen (on the device they are cheap), so every projection's values
+    do not depend on which ones are kept.  ``rows = (start, stop)`` keeps that
+    token range of each projection's x (the rank's shard of the batch); the
+    weights and adapters, drawn after the full batch's x, are the same on
+    every rank.
+    """
     g = _gen(4, device)
-    h, f = HIDDEN_WAN, FFN_WAN
-    stack = [(32, 1.0), (64, 0.7), (128, 0.4)]
-    shapes = [("q", h, h), ("k", h, h), ("v", h, h), ("o", h, h), ("ffn_up", h, f), ("ffn_down", f, h)]
-    return [_projection(g, nm, m, k, n, stack, device, dtype) for nm, k, n in shapes]
+    out = []
+    for nm, k, n in C5_SHAPES:
+        x = _randn(g, (m, k), 1.0, device, dtype)
+        if rows is not None:
+            x = x[rows[0]:rows[1]].clone()
+        p = _projection(g, nm, m, k, n, C5_STACK, device, dtype, x=x)
+        if only is None or nm in only:
+            out.append(p)
+        del p, x
+    return out
 
 
 def c5_flops(m=32760) -> float:

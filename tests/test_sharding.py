@@ -55,14 +55,19 @@ def _worker(rank, world, port, mode, q):
         from datetime import timedelta
 
         dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=10))
-        total, n = 37, 5
-        a, b = shard_rows(total, world, rank)
-        local = torch.arange(a, b, dtype=torch.float32)[:, None].repeat(1, n) * 10 + torch.arange(n)
-        if mode == "fail" and rank == 1:
-            raise RuntimeError("injected failure before the all-gather")
-        full = gather_rows(local, total)
-        want = torch.arange(total, dtype=torch.float32)[:, None].repeat(1, n) * 10 + torch.arange(n)
-        q.put((rank, "ok" if torch.equal(full, want) else "mismatch"))
+        n = 5
+        verdict = "ok"
+        for total in (37, 36):  # uneven shards (padded gather), then equal ones (straight into the output)
+            a, b = shard_rows(total, world, rank)
+            local = torch.arange(a, b, dtype=torch.float32)[:, None].repeat(1, n) * 10 + torch.arange(n)
+            if mode == "fail" and rank == 1:
+                raise RuntimeError("injected failure before the all-gather")
+            out = torch.full((total, n), -1.0) if total == 36 else None
+            full = gather_rows(local, total, out=out)
+            want = torch.arange(total, dtype=torch.float32)[:, None].repeat(1, n) * 10 + torch.arange(n)
+            if not torch.equal(full, want) or (out is not None and full.data_ptr() != out.data_ptr()):
+                verdict = "mismatch"
+        q.put((rank, verdict))
         dist.destroy_process_group()
     except Exception as exc:  # noqa: BLE001
         q.put((rank, f"error: {type(exc).__name__}: {str(exc)[:80]}"))
