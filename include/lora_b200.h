@@ -277,6 +277,20 @@ LORA_API int lora_sgmv_expand(const void* y, int64_t ldy, const void* z, int64_t
                      int64_t ldo, int64_t T, int64_t S, int64_t N, int64_t r_max, float scale,
                      int dtype, void* stream);
 
+/* lora_sgmv_expand for the rank-major flat table b_flat [b_rows, N] (leading
+ * dimension ldb) without row indirection: knowing the table's extent lets the
+ * tensor-core form (units of one tile x 256 output columns, adapter rows and
+ * y loaded by TMA, tcgen05 MMAs) bound its reads; it serves r_max <= 64 with
+ * N and the leading dimensions multiples of 8 and 16-byte aligned rows, and
+ * anything else goes to lora_sgmv_expand.  Replaces the same reference
+ * functions as lora_sgmv_expand: the expand of segmented_branch.py:31-47 and
+ * ragged_branch.py:18-27. */
+LORA_API int lora_sgmv_expand_ex(const void* y, int64_t ldy, const void* z, int64_t ldz, int z_dtype,
+                        const void* b, int64_t b_rows, int64_t ldb, const int64_t* offsets,
+                        const int64_t* ranks, int64_t n_adapters, const int32_t* tiles, void* out,
+                        int64_t ldo, int64_t T, int64_t S, int64_t N, int64_t r_max, float scale,
+                        int dtype, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -74,6 +74,8 @@ SIGNATURES = {
                                  _I64, _I64, _F, _I, _I, _P, _SZ, _P]),
     "lora_sgmv_expand": (_I, [_P, _I64, _P, _I64, _I, _P, _I64, _I64, _P, _P, _I64, _P, _P, _P, _I64, _I64, _I64,
                               _I64, _I64, _F, _I, _P]),
+    "lora_sgmv_expand_ex": (_I, [_P, _I64, _P, _I64, _I, _P, _I64, _I64, _P, _P, _I64, _P, _P, _I64, _I64, _I64,
+                                 _I64, _I64, _F, _I, _P]),
 }
 
 

@@ -408,7 +408,8 @@ extern "C" int lora_sgmv_pick_split_k(int64_t T, int64_t K, int64_t r_max) {
   if (T <= 0 || K <= 0 || r_max <= 0) return 1;
   const int dev = current_device();
   const int sms = dev >= 0 ? device_info(dev).num_sms : 148;
-  return sgmv_shrink_block_split(T, K, sms > 0 ? sms : 148);
+  (void)sms;
+  return sgmv_unit_split(K);
 }
 
 extern "C" size_t lora_sgmv_shrink_workspace_size(int64_t T, int64_t S, int64_t z_width, int split_k) {
@@ -443,10 +444,18 @@ int sgmv_shrink_impl(const void* x, int64_t ldx, const void* a_flat, int64_t lda
     if (sgmv_max_tiles(T, S) > kMaxCounters) return LORA_ERR_SHAPE;
   }
 
-  // Tensor cores first (sgmv_tc.cu: 128-token blocks, TMA-fed, needs the row
-  // count of a_flat and no row indirection), then dense 64-token blocks on
+  // Tensor cores first: the unit-scheduled kernel (sgmv_unit.cu: (tile, K
+  // slice) units over persistent CTAs, split-K through the workspace), else the
+  // 128-token block kernel (sgmv_tc.cu, cluster split-K); both need the row
+  // count of a_flat and no row indirection.  Then dense 64-token blocks on
   // mma.sync (sgmv_block.cu); the per-tile kernel below covers the layouts
-  // neither takes (unaligned rows, r_max > 128).
+  // none of them takes (unaligned rows, r_max > 128).
+  if (rows == nullptr && a_rows > 0 && r_max > 0 && K > 0 && split_k > 1) {
+    const int rc = launch_sgmv_shrink_unit(x, ldx, a_flat, lda, a_rows, offsets, ranks, tiles, sgmv_max_tiles(T, S), z,
+                                           ldz, z_dtype, z_width, T, K, r_max, scale, dtype, split_k, workspace,
+                                           workspace_bytes, info.num_sms, info.err_word, stream);
+    if (rc != LORA_ERR_UNSUPPORTED) return rc;
+  }
   if (rows == nullptr && a_rows > 0 && r_max > 0 && K > 0) {
     const int rc = launch_sgmv_shrink_tc(x, ldx, a_flat, lda, a_rows, offsets, ranks, tiles, z, ldz, z_dtype, z_width,
                                          T, K, r_max, scale, dtype, info.num_sms, info.err_word, stream);

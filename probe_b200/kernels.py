@@ -303,6 +303,13 @@ def sgmv_expand(y: torch.Tensor | None, z: torch.Tensor, b: torch.Tensor, b_sj: 
         out = torch.empty((z.shape[0], n), device=z.device, dtype=dtype)
     offsets = _i64(offsets, z.device)
     ranks = _i64(ranks, z.device)
+    if rows is None and b_sn == 1 and b.dim() == 2 and b.stride(1) == 1 and b_sj == b.stride(0):
+        # flat rank-major table: the entry point that knows its row count (TMA-bounded tensor-core form)
+        _lib.call("lora_sgmv_expand_ex", _lib.ptr(y), _lib.ld(y) if y is not None else 0, _lib.ptr(z), _lib.ld(z),
+                  _lib.dtype_code(z.dtype), _lib.ptr(b), b.shape[0], int(b_sj), _lib.ptr(offsets), _lib.ptr(ranks),
+                  offsets.numel(), _lib.ptr(tiles), _lib.ptr(out), out.stride(0), t, s, n, int(r_max), float(scale),
+                  _lib.dtype_code(dtype), _lib.stream_handle(z.device))
+        return out
     if rows is not None:
         rows = _i64(rows, z.device)
     _lib.call("lora_sgmv_expand", _lib.ptr(y), _lib.ld(y) if y is not None else 0, _lib.ptr(z), _lib.ld(z),

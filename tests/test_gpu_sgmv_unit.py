@@ -1,0 +1,87 @@
+"""Unit-scheduled segmented shrink (GPU): (tile, K slice) units over persistent
+CTAs, split-K reduced by the last slice of each tile.
+
+Cases reach its edges: one-token tiles (random per-token ids), a last tile cut
+by T, K not a multiple of 64, ranks 1..128 (stage layouts for r_max <= 64 and
+> 64), rank-0 adapters, many slices, fp32 and bf16 z; results against the
+float64 oracle and bit-identical across repeated calls (the reduction order
+is fixed).
+"""
+
+import math
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import lora_oracle as orc
+from probe_b200 import _lib, kernels
+from tests.helpers import np64, randn
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+
+
+def _tables(ranks, k, seed):
+    g = torch.Generator().manual_seed(seed)
+    rk = torch.tensor(ranks, dtype=torch.int64)
+    offs = torch.zeros_like(rk)
+    offs[1:] = torch.cumsum(rk, 0)[:-1]
+    a = (torch.randn(max(int(rk.sum()), 1), k, generator=g) / math.sqrt(k)).to(torch.bfloat16)
+    return a.to(DEV), offs.to(DEV), rk.to(DEV)
+
+
+def _run(x, a, offs, rk, ids, r_max, split_k, z_dtype=torch.float32, scale=0.7):
+    t = x.shape[0]
+    tiles, s = kernels.sgmv_schedule(t, offs.numel(), ids=torch.as_tensor(ids, device=DEV))
+    return kernels.sgmv_shrink(x, a, offs, rk, tiles, s, r_max, scale=scale, z_dtype=z_dtype, split_k=split_k)
+
+
+@pytest.mark.parametrize("t,k,ranks,mode,split_k", [
+    (1000, 4096, [4, 8, 16, 32, 64], "random", 8),       # one-token tiles everywhere
+    (777, 520, [64, 13, 0, 33], "runs", 3),              # K % 64 != 0, rank 0, last tile cut by T
+    (300, 1024, [128, 96, 1, 127], "runs", 16),          # r_max > 64: wider stages
+    (64, 2048, [16], "runs", 2),                         # one tile
+    (4096, 4096, [4, 8, 16, 32, 64] * 12 + [8] * 4, "zipf", 0),  # C3-like, default split
+])
+def test_unit_shrink_matches_oracle(t, k, ranks, mode, split_k):
+    rng = np.random.default_rng(t + k)
+    n_ad = len(ranks)
+    if mode == "random":
+        ids = rng.integers(0, n_ad, size=t)
+    elif mode == "runs":
+        ids = np.repeat(rng.integers(0, n_ad, size=t // 5 + 1), 5)[:t]
+    else:
+        lens = np.maximum(1, (t * (np.arange(1, 129) ** -1.1) / (np.arange(1, 129) ** -1.1).sum()).astype(int))
+        lens[0] += t - lens.sum()
+        ids = np.repeat(rng.integers(0, n_ad, size=128), lens)
+    a, offs, rk = _tables(ranks, k, seed=t)
+    x = randn((t, k), 1.0, seed=k)
+    r_max = max(ranks)
+    z = _run(x, a, offs, rk, ids, r_max, split_k)
+    want = 0.7 * orc.shrink_ragged(np64(x), np64(a), offs.cpu().numpy(), rk.cpu().numpy(), ids, r_max)
+    err = np.abs(np64(z) - want).max()
+    assert err < 2e-4 * max(1.0, np.abs(want).max()), err
+    again = _run(x, a, offs, rk, ids, r_max, split_k)
+    assert torch.equal(z, again)  # fixed reduction order
+    zb = _run(x, a, offs, rk, ids, r_max, split_k, z_dtype=torch.bfloat16)
+    assert np.abs(np64(zb) - want).max() <= 1e-2 * max(1.0, np.abs(want).max())
+    assert _lib.device_error() == 0
+
+
+def test_unit_shrink_out_of_range_ids_are_zero_and_reported():
+    t, k = 200, 512
+    a, offs, rk = _tables([16, 32], k, seed=5)
+    ids = np.zeros(t, dtype=np.int64)
+    ids[50:70] = 7  # no such adapter
+    ids[120:] = 1
+    x = randn((t, k), 1.0, seed=6)
+    z = _run(x, a, offs, rk, ids, 32, 4)
+    assert torch.count_nonzero(z[50:70]) == 0
+    want = 0.7 * orc.shrink_ragged(np64(x), np64(a), offs.cpu().numpy(), rk.cpu().numpy(),
+                                   np.where(ids == 7, 0, ids), 32)
+    keep = np.ones(t, dtype=bool)
+    keep[50:70] = False
+    assert np.abs(np64(z)[keep] - want[keep]).max() < 2e-4
+    assert _lib.device_error() == 110  # out-of-range adapter id recorded (and cleared by the read)
+    assert _lib.device_error() == 0
