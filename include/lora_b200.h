@@ -103,6 +103,21 @@ LORA_API int lora_b200_device_error(int device, int* code);
 LORA_API int lora_gemm(const void* x, int64_t ldx, const void* w, int64_t ldw, const void* z, int64_t ldz,
               const void* bw, int64_t ldbw, const void* bias, void* out, int64_t ldo, int64_t M,
               int64_t N, int64_t K, int64_t R, float alpha, int64_t lo_offset, int dtype, void* stream);
+/* lora_gemm with a workspace for its split tail: when the tiles do not fill a
+ * whole number of waves of resident CTA pairs, the tiles of the last, partial
+ * wave are cut along K across the otherwise idle pairs; their fp32 partials
+ * meet in the workspace and the last piece of each tile to finish sums them in
+ * a fixed order (results do not depend on timing).  Workspace:
+ * lora_gemm_workspace_size(M, N, K, R) bytes (0 = no split for this shape),
+ * with a zeroed ticket region first, as lora_shrink's (its counters are
+ * returned to zero by every call).  NULL or short workspace: no split.
+ * Replaces the same reference functions as lora_gemm; the split is a B200
+ * scheduling choice with no counterpart there. */
+LORA_API size_t lora_gemm_workspace_size(int64_t M, int64_t N, int64_t K, int64_t R);
+LORA_API int lora_gemm_ex(const void* x, int64_t ldx, const void* w, int64_t ldw, const void* z, int64_t ldz,
+                 const void* bw, int64_t ldbw, const void* bias, void* out, int64_t ldo, int64_t M,
+                 int64_t N, int64_t K, int64_t R, float alpha, int64_t lo_offset, int dtype,
+                 void* workspace, size_t workspace_bytes, void* stream);
 
 /* ---------------------------------------------------------------------------
  * Split-K rank shrink  z[M, z_width] = scale * x[M,K] . a[R,K]^T

@@ -50,6 +50,9 @@ SIGNATURES = {
     "lora_b200_device_error": (_I, [_I, ctypes.POINTER(_I)]),
     "lora_gemm": (_I, [_P, _I64, _P, _I64, _P, _I64, _P, _I64, _P, _P, _I64, _I64, _I64, _I64, _I64, _F, _I64, _I,
                        _P]),
+    "lora_gemm_workspace_size": (_SZ, [_I64, _I64, _I64, _I64]),
+    "lora_gemm_ex": (_I, [_P, _I64, _P, _I64, _P, _I64, _P, _I64, _P, _P, _I64, _I64, _I64, _I64, _I64, _F, _I64,
+                          _I, _P, _SZ, _P]),
     "lora_shrink_workspace_size": (_SZ, [_I64, _I64, _I]),
     "lora_shrink_pick_split_k": (_I, [_I64, _I64, _I64]),
     "lora_shrink": (_I, [_P, _I64, _P, _I64, _P, _I64, _I, _I64, _I, _I64, _I64, _I64, _F, _I, _I, _P, _SZ, _P]),

@@ -46,7 +46,29 @@ struct GemmArgs {
   int num_m_tiles, num_n_tiles, num_tiles, group_m;
   int l2_hints;  // bit 0: W / B_dup evict_last; bit 1: x / z evict_first; bit 2: out evict_first
   float alpha;
+  // Split tail (CTA-pair kernel): the first full_tiles tiles run whole; each
+  // later tile is cut into `split` K ranges, one per pair, whose fp32 partials
+  // meet in tail_ws and are summed by the last to finish (ticket per tile half).
+  int full_tiles, split;
+  float* tail_ws;
+  int* tail_tickets;
 };
+
+// Work item `item` of the CTA-pair kernel: its tile and K-block range.
+LORA_DEVINL void pair_item(int item, const GemmArgs& a, int num_kb, int& tile, int& kb0, int& kb1, int& unit) {
+  if (item < a.full_tiles) {
+    tile = item;
+    kb0 = 0;
+    kb1 = num_kb;
+    unit = -1;
+    return;
+  }
+  unit = item - a.full_tiles;
+  tile = a.full_tiles + unit / a.split;
+  const int slice = unit - (unit / a.split) * a.split;
+  kb0 = (num_kb * slice) / a.split;
+  kb1 = (num_kb * (slice + 1)) / a.split;
+}
 
 LORA_DEVINL void gemm_tile_coords(int tile, const GemmArgs& a, int& mt, int& nt) {
   const int group_size = a.group_m * a.num_n_tiles;
@@ -384,6 +406,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
   uint64_t* acc_empty = acc_full + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  volatile int* last_flag = reinterpret_cast<volatile int*>(tmem_slot + 2);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -421,6 +444,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
   const int num_kb = args.num_kb_main + args.num_kb_tail;
+  const int num_items = args.full_tiles + (args.num_tiles - args.full_tiles) * args.split;
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
@@ -430,12 +454,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
-      for (int tile = pair; ok && tile < args.num_tiles; tile += npairs) {
+      for (int item = pair; ok && item < num_items; item += npairs) {
+        int tile, kb0, kb1, unit;
+        pair_item(item, args, num_kb, tile, kb0, kb1, unit);
         int mt, nt;
         gemm_tile_coords(tile, args, mt, nt);
         const int row_a = mt * 256 + static_cast<int>(rank) * 128;
         const int row_b = nt * kTileN + static_cast<int>(rank) * 128;  // + 256 for the second box
-        for (int kb = 0; kb < num_kb; ++kb) {
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait_bounded(&empty[stage], phase ^ 1, abort_flag, args.err, kDevErrTimeoutEmpty)) {
             ok = false;
             break;
@@ -472,7 +498,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
       uint32_t phase = 0;
       int local = 0;
       bool ok = true;
-      for (int tile = pair; ok && tile < args.num_tiles; tile += npairs, ++local) {
+      for (int item = pair; ok && item < num_items; item += npairs, ++local) {
+        int tile, kb0, kb1, unit;
+        pair_item(item, args, num_kb, tile, kb0, kb1, unit);
         // NW = 1: accumulator local & 1, its (local >> 1)-th use; NW = 2: both halves, every tile
         const int acc = NW == 1 ? (local & 1) : 0;
         const uint32_t acc_phase = NW == 1 ? ((local >> 1) & 1) : (local & 1);
@@ -480,7 +508,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
           break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * 256);
-        for (int kb = 0; kb < num_kb; ++kb) {
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait_bounded(&full[stage], phase, abort_flag, args.err, kDevErrTimeoutFull)) {
             ok = false;
             break;
@@ -491,9 +519,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
           const int nk = (kb == num_kb - 1 && args.num_kb_tail > 0) ? args.tail_last_k16 : 4;
           for (int k = 0; k < nk; ++k)
             tc_mma_f16_pair(d_tmem, adesc + static_cast<uint64_t>(2 * k), bdesc + static_cast<uint64_t>(2 * k),
-                            kIdesc, (kb > 0 || k > 0) ? 1u : 0u);
+                            kIdesc, (kb > kb0 || k > 0) ? 1u : 0u);
           if constexpr (NW == 2) {
-            if (kb == 0) {  // the second half of the accumulator: free once the epilogue has drained it
+            if (kb == kb0) {  // the second half of the accumulator: free once the epilogue has drained it
               if (!mbar_wait_bounded(&acc_empty[1], acc_phase ^ 1, abort_flag, args.err, kDevErrTimeoutAccEmpty)) {
                 ok = false;
                 break;
@@ -503,7 +531,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
             const uint64_t bdesc1 = umma_desc_sw128(smem_u32(sm_b + stage * L::kBBytes + 128 * kGemmBK * 2));
             for (int k = 0; k < nk; ++k)
               tc_mma_f16_pair(tmem_base + 256, adesc + static_cast<uint64_t>(2 * k),
-                              bdesc1 + static_cast<uint64_t>(2 * k), kIdesc, (kb > 0 || k > 0) ? 1u : 0u);
+                              bdesc1 + static_cast<uint64_t>(2 * k), kIdesc, (kb > kb0 || k > 0) ? 1u : 0u);
           }
           tc_commit_pair(&empty[stage], kBoth);
           if (++stage == STAGES) {
@@ -523,15 +551,21 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
     const bool vec_ok = (args.ldo % 8) == 0 && (reinterpret_cast<uintptr_t>(args.out) % 16) == 0;
     const uint64_t st_policy = l2_policy_evict_first();
     int local = 0;
-    for (int tile = pair; tile < args.num_tiles; tile += npairs, ++local) {
+    for (int item = pair; item < num_items; item += npairs, ++local) {
+      int tile, kb0, kb1, unit;
+      pair_item(item, args, num_kb, tile, kb0, kb1, unit);
       const int acc = NW == 1 ? (local & 1) : 0;
       const uint32_t acc_phase = NW == 1 ? ((local >> 1) & 1) : (local & 1);
       int mt, nt;
       gemm_tile_coords(tile, args, mt, nt);
       if (!mbar_wait_bounded(&acc_full[acc], acc_phase, abort_flag, args.err, kDevErrTimeoutAccFull)) break;
       tc_fence_after();
-      const int row = mt * 256 + static_cast<int>(rank) * 128 + quad * 32 + lane;
+      const int trow = static_cast<int>(rank) * 128 + quad * 32 + lane;  // row within the tile
+      const int row = mt * 256 + trow;
       T* out_row = static_cast<T*>(args.out) + static_cast<int64_t>(row) * args.ldo;
+      // split item: this CTA's 128 rows of the partial tile, fp32, kTileN wide
+      float* part = unit < 0 ? nullptr
+                             : args.tail_ws + (static_cast<int64_t>(unit) * 256 + trow) * kTileN;
 #pragma unroll 1
       for (int h = 0; h < NW; ++h) {
         const int half = NW == 1 ? acc : h;  // TMEM accumulator drained in this round
@@ -542,11 +576,59 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
           uint32_t r[16];
           tmem_ld_32x32b_x16(t_row + c, r);
           tmem_wait_ld();
-          epilogue_store16<T>(args, out_row, bias, row, nt * kTileN + h * 256 + c, vec_ok, r, st_policy);
+          if (part == nullptr) {
+            epilogue_store16<T>(args, out_row, bias, row, nt * kTileN + h * 256 + c, vec_ok, r, st_policy);
+          } else {
+            float4* dst = reinterpret_cast<float4*>(part + h * 256 + c);
+#pragma unroll
+            for (int e = 0; e < 4; ++e)
+              dst[e] = make_float4(__uint_as_float(r[4 * e]), __uint_as_float(r[4 * e + 1]),
+                                   __uint_as_float(r[4 * e + 2]), __uint_as_float(r[4 * e + 3]));
+          }
         }
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(&acc_empty[half]), 0));
+      }
+      if (part != nullptr) {
+        // The last of the tile's split items to store its partial (per CTA
+        // half: ticket (tile, rank)) sums the partials in slice order.
+        __threadfence();
+        named_bar_sync(1, 128);
+        if (threadIdx.x == 64) {
+          int* ticket = args.tail_tickets + (tile - args.full_tiles) * 2 + static_cast<int>(rank);
+          const int last = atomicAdd(ticket, 1) == args.split - 1;
+          if (last) *ticket = 0;  // every slice has arrived: back to zero for the next call
+          *last_flag = last;
+        }
+        named_bar_sync(1, 128);
+        if (*last_flag) {
+          __threadfence();
+          const int first_unit = (tile - args.full_tiles) * args.split;
+#pragma unroll 1
+          for (int c = 0; c < kTileN; c += 16) {
+            float v[16];
+#pragma unroll
+            for (int e = 0; e < 16; ++e) v[e] = 0.f;
+            for (int sl = 0; sl < args.split; ++sl) {
+              const float4* src = reinterpret_cast<const float4*>(
+                  args.tail_ws + (static_cast<int64_t>(first_unit + sl) * 256 + trow) * kTileN + c);
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                const float4 q = __ldcg(src + e);
+                v[4 * e] += q.x;
+                v[4 * e + 1] += q.y;
+                v[4 * e + 2] += q.z;
+                v[4 * e + 3] += q.w;
+              }
+            }
+            uint32_t r[16];
+#pragma unroll
+            for (int e = 0; e < 16; ++e) r[e] = __float_as_uint(v[e]);
+            epilogue_store16<T>(args, out_row, bias, row, nt * kTileN + c, vec_ok, r, st_policy);
+          }
+        }
+        named_bar_sync(1, 128);  // last_flag is rewritten by the next split item
       }
     }
   }
@@ -618,6 +700,10 @@ int launch_gemm(const void* x, int64_t ldx, const void* w, int64_t ldw, const vo
   a.num_tiles = a.num_m_tiles * a.num_n_tiles;
   a.group_m = 8;
   a.l2_hints = 0;
+  a.full_tiles = a.num_tiles;
+  a.split = 1;
+  a.tail_ws = nullptr;
+  a.tail_tickets = nullptr;
   a.alpha = alpha;
 
   auto kernel = gemm_tc_kernel<BN, STAGES, T>;
@@ -666,10 +752,61 @@ int env_int(const char* name, int fallback) {
   return parsed > 0 || std::strcmp(v, "0") == 0 ? parsed : fallback;
 }
 
+// Split tail of the CTA-pair GEMM: with `pairs` resident pairs and `tiles`
+// tiles, the last (tiles mod pairs) tiles are cut along K into `split` pieces
+// (one per idle pair, each at least 4 k-blocks) when that leaves >= 2 pieces.
+struct PairSplit {
+  int full_tiles, split;
+  size_t ws_bytes;  // workspace: ticket region + fp32 partials
+};
+
+PairSplit pair_split_plan(int64_t tiles, int pairs, int num_kb, int tile_n) {
+  PairSplit sp{static_cast<int>(tiles), 1, 0};
+  if (pairs <= 0 || tiles <= 0) return sp;
+  const int64_t rem = tiles % pairs;
+  if (rem == 0) return sp;
+  int64_t s = pairs / rem;
+  s = std::min<int64_t>(s, std::max(num_kb / 4, 1));
+  s = std::min<int64_t>(s, 16);
+  if (s < 2 || rem * 2 > kMaxCounters) return sp;
+  sp.full_tiles = static_cast<int>(tiles - rem);
+  sp.split = static_cast<int>(s);
+  sp.ws_bytes = kCounterBytes + static_cast<size_t>(rem * s) * 256 * static_cast<size_t>(tile_n) * sizeof(float);
+  return sp;
+}
+
+// Resident CTA pairs of gemm_tc2_kernel<STAGES, NW> on this device (cached).
+template <int STAGES, int NW, typename T>
+int pair_capacity(int dev, const DeviceInfo& info, cudaError_t* attr_status) {
+  using L = PairSmem<STAGES, NW>;
+  auto kernel = gemm_tc2_kernel<STAGES, NW, T>;
+  static std::once_flag once[64];
+  static cudaError_t attr_err[64];
+  static int max_clusters[64];
+  std::call_once(once[dev & 63], [&] {
+    attr_err[dev & 63] = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kBytes);
+    int clusters = 0;
+    if (attr_err[dev & 63] == cudaSuccess) {
+      cudaLaunchConfig_t cfg = {};
+      cfg.gridDim = dim3(2 * info.num_sms);
+      cfg.blockDim = dim3(kGemmThreads);
+      cfg.dynamicSmemBytes = L::kBytes;
+      if (cudaOccupancyMaxActiveClusters(&clusters, kernel, &cfg) != cudaSuccess) {
+        cudaGetLastError();
+        clusters = info.num_sms / 2;
+      }
+    }
+    max_clusters[dev & 63] = clusters > 0 ? clusters : info.num_sms / 2;
+  });
+  *attr_status = attr_err[dev & 63];
+  return max_clusters[dev & 63];
+}
+
 template <int STAGES, int NW, typename T>
 int launch_gemm_pair(const void* x, int64_t ldx, const void* w, int64_t ldw, const void* z, int64_t ldz,
                      const void* bw, int64_t ldbw, const void* bias, void* out, int64_t ldo, int64_t M, int64_t N,
-                     int64_t K, int64_t R, float alpha, int64_t lo_offset, int dtype, cudaStream_t stream) {
+                     int64_t K, int64_t R, float alpha, int64_t lo_offset, int dtype, void* ws, size_t ws_bytes,
+                     cudaStream_t stream) {
   using L = PairSmem<STAGES, NW>;
   const int dev = current_device();
   if (dev < 0) return LORA_ERR_DEVICE;
@@ -706,26 +843,24 @@ int launch_gemm_pair(const void* x, int64_t ldx, const void* w, int64_t ldw, con
   a.alpha = alpha;
 
   auto kernel = gemm_tc2_kernel<STAGES, NW, T>;
-  static std::once_flag once[64];
-  static cudaError_t attr_err[64];
-  static int max_clusters[64];
-  std::call_once(once[dev & 63], [&] {
-    attr_err[dev & 63] = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kBytes);
-    int clusters = 0;
-    if (attr_err[dev & 63] == cudaSuccess) {
-      cudaLaunchConfig_t cfg = {};
-      cfg.gridDim = dim3(2 * info.num_sms);
-      cfg.blockDim = dim3(kGemmThreads);
-      cfg.dynamicSmemBytes = L::kBytes;
-      if (cudaOccupancyMaxActiveClusters(&clusters, kernel, &cfg) != cudaSuccess) {
-        cudaGetLastError();
-        clusters = info.num_sms / 2;
-      }
+  cudaError_t attr_status = cudaSuccess;
+  const int capacity = pair_capacity<STAGES, NW, T>(dev, info, &attr_status);
+  if (attr_status != cudaSuccess) return LORA_ERR_CUDA;
+  a.full_tiles = a.num_tiles;
+  a.split = 1;
+  a.tail_ws = nullptr;
+  a.tail_tickets = nullptr;
+  if (ws != nullptr && env_int("LORA_B200_SPLIT_TAIL", 1) != 0) {
+    const PairSplit sp = pair_split_plan(a.num_tiles, capacity, a.num_kb_main + a.num_kb_tail, 256 * NW);
+    if (sp.split > 1 && ws_bytes >= sp.ws_bytes && (reinterpret_cast<uintptr_t>(ws) & 15u) == 0) {
+      a.full_tiles = sp.full_tiles;
+      a.split = sp.split;
+      a.tail_tickets = static_cast<int*>(ws);
+      a.tail_ws = reinterpret_cast<float*>(static_cast<char*>(ws) + kCounterBytes);
     }
-    max_clusters[dev & 63] = clusters > 0 ? clusters : info.num_sms / 2;
-  });
-  if (attr_err[dev & 63] != cudaSuccess) return LORA_ERR_CUDA;
-  const int pairs = static_cast<int>(std::min<int64_t>(a.num_tiles, max_clusters[dev & 63]));
+  }
+  const int64_t items = a.full_tiles + static_cast<int64_t>(a.num_tiles - a.full_tiles) * a.split;
+  const int pairs = static_cast<int>(std::min<int64_t>(items, capacity));
   kernel<<<2 * pairs, kGemmThreads, L::kBytes, stream>>>(tm_x, tm_w, tm_z, tm_b, a);
   return cudaGetLastError() == cudaSuccess ? LORA_OK : LORA_ERR_CUDA;
 }
@@ -736,7 +871,19 @@ int launch_gemm_pair(const void* x, int64_t ldx, const void* w, int64_t ldw, con
 // tile.  Chosen when their waves of pairs, weighted by the tile's doubled work
 // and the ~10% faster products, cost less than the 256 x 256 waves.
 // LORA_B200_GEMM_WIDE=0 / 1 forces the choice (tuning sweeps).
-int pair_tile_width(int64_t M, int64_t N, int pairs) {
+// Waves of pair tiles, counting a split tail as the fraction of a wave each
+// of its pieces takes (plus a little for the partials' round trip).
+double pair_waves(int64_t tiles, int pairs, int num_kb, bool can_split) {
+  const int64_t full = tiles / pairs, rem = tiles % pairs;
+  if (rem == 0) return static_cast<double>(full);
+  if (can_split) {
+    const PairSplit sp = pair_split_plan(tiles, pairs, num_kb, 256);
+    if (sp.split > 1) return static_cast<double>(full) + 1.0 / sp.split + 0.05;
+  }
+  return static_cast<double>(full + 1);
+}
+
+int pair_tile_width(int64_t M, int64_t N, int64_t K, int64_t R, int pairs, bool can_split) {
   static const int force = [] {  // -1: choose, 0 / 1: forced (read once)
     const char* v = std::getenv("LORA_B200_GEMM_WIDE");
     return (v != nullptr && (v[0] == '0' || v[0] == '1')) ? v[0] - '0' : -1;
@@ -744,9 +891,10 @@ int pair_tile_width(int64_t M, int64_t N, int pairs) {
   if (force == 0 || N < 512) return 1;
   if (force == 1) return 2;
   const int64_t mt = (M + 255) / 256;
-  const int64_t w1 = (mt * ((N + 255) / 256) + pairs - 1) / pairs;
-  const int64_t w2 = (mt * ((N + 511) / 512) + pairs - 1) / pairs;
-  return 1.8 * static_cast<double>(w2) < static_cast<double>(w1) ? 2 : 1;
+  const int num_kb = static_cast<int>((K + kGemmBK - 1) / kGemmBK + (R + kGemmBK - 1) / kGemmBK);
+  const double w1 = pair_waves(mt * ((N + 255) / 256), pairs, num_kb, can_split);
+  const double w2 = pair_waves(mt * ((N + 511) / 512), pairs, num_kb, can_split);
+  return 1.8 * w2 < w1 ? 2 : 1;
 }
 
 // Pair tiles when the output is wide and there are enough 256x256 tiles to
@@ -774,10 +922,12 @@ int gemm_pick_bn(int64_t M, int64_t N, int num_sms) {
 
 }  // namespace lora
 
-extern "C" int lora_gemm(const void* x, int64_t ldx, const void* w, int64_t ldw, const void* z, int64_t ldz,
-                         const void* bw, int64_t ldbw, const void* bias, void* out, int64_t ldo, int64_t M,
-                         int64_t N, int64_t K, int64_t R, float alpha, int64_t lo_offset, int dtype, void* stream) {
-  using namespace lora;
+namespace lora {
+namespace {
+
+int gemm_impl(const void* x, int64_t ldx, const void* w, int64_t ldw, const void* z, int64_t ldz, const void* bw,
+              int64_t ldbw, const void* bias, void* out, int64_t ldo, int64_t M, int64_t N, int64_t K, int64_t R,
+              float alpha, int64_t lo_offset, int dtype, void* ws, size_t ws_bytes, void* stream) {
   if (x == nullptr || w == nullptr || out == nullptr) return LORA_ERR_ARG;
   if (dtype != LORA_BF16 && dtype != LORA_F16) return LORA_ERR_DTYPE;
   if (M < 0 || N < 0 || K < 0 || R < 0) return LORA_ERR_SHAPE;
@@ -801,22 +951,57 @@ extern "C" int lora_gemm(const void* x, int64_t ldx, const void* w, int64_t ldw,
   const int bn = gemm_pick_bn(M, N, info.num_sms);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (use_pair_tiles(M, N, info.num_sms)) {
-    if (pair_tile_width(M, N, info.num_sms / 2) == 2) {
+    if (pair_tile_width(M, N, K, R, info.num_sms / 2, ws != nullptr) == 2) {
       if (dtype == LORA_BF16)
         return launch_gemm_pair<4, 2, __nv_bfloat16>(x, ldx, w, ldw, z, ldz, bw, ldbw, bias, out, ldo, M, N, K, R,
-                                                     alpha, lo_offset, dtype, s);
+                                                     alpha, lo_offset, dtype, ws, ws_bytes, s);
       return launch_gemm_pair<4, 2, __half>(x, ldx, w, ldw, z, ldz, bw, ldbw, bias, out, ldo, M, N, K, R, alpha,
-                                            lo_offset, dtype, s);
+                                            lo_offset, dtype, ws, ws_bytes, s);
     }
     if (dtype == LORA_BF16)
       return launch_gemm_pair<6, 1, __nv_bfloat16>(x, ldx, w, ldw, z, ldz, bw, ldbw, bias, out, ldo, M, N, K, R,
-                                                   alpha, lo_offset, dtype, s);
+                                                   alpha, lo_offset, dtype, ws, ws_bytes, s);
     return launch_gemm_pair<6, 1, __half>(x, ldx, w, ldw, z, ldz, bw, ldbw, bias, out, ldo, M, N, K, R, alpha,
-                                          lo_offset, dtype, s);
+                                          lo_offset, dtype, ws, ws_bytes, s);
   }
   if (dtype == LORA_BF16)
     return dispatch_gemm<__nv_bfloat16>(bn, x, ldx, w, ldw, z, ldz, bw, ldbw, bias, out, ldo, M, N, K, R, alpha,
                                         lo_offset, dtype, s);
   return dispatch_gemm<__half>(bn, x, ldx, w, ldw, z, ldz, bw, ldbw, bias, out, ldo, M, N, K, R, alpha, lo_offset,
                                dtype, s);
+}
+
+}  // namespace
+}  // namespace lora
+
+extern "C" int lora_gemm(const void* x, int64_t ldx, const void* w, int64_t ldw, const void* z, int64_t ldz,
+                         const void* bw, int64_t ldbw, const void* bias, void* out, int64_t ldo, int64_t M,
+                         int64_t N, int64_t K, int64_t R, float alpha, int64_t lo_offset, int dtype, void* stream) {
+  return lora::gemm_impl(x, ldx, w, ldw, z, ldz, bw, ldbw, bias, out, ldo, M, N, K, R, alpha, lo_offset, dtype,
+                         nullptr, 0, stream);
+}
+
+extern "C" size_t lora_gemm_workspace_size(int64_t M, int64_t N, int64_t K, int64_t R) {
+  using namespace lora;
+  if (M <= 0 || N <= 0 || K <= 0 || R < 0 || M > INT32_MAX || N > INT32_MAX) return 0;
+  const int dev = current_device();
+  if (dev < 0) return 0;
+  const DeviceInfo& info = device_info(dev);
+  if (!info.is_sm100 || !use_pair_tiles(M, N, info.num_sms)) return 0;
+  const int nw = pair_tile_width(M, N, K, R, info.num_sms / 2, true);
+  cudaError_t st = cudaSuccess;
+  const int capacity = nw == 2 ? pair_capacity<4, 2, __nv_bfloat16>(dev, info, &st)
+                               : pair_capacity<6, 1, __nv_bfloat16>(dev, info, &st);
+  if (st != cudaSuccess) return 0;
+  const int64_t tiles = ((M + 255) / 256) * ((N + 256 * nw - 1) / (256 * nw));
+  const int num_kb = static_cast<int>((K + kGemmBK - 1) / kGemmBK + (R + kGemmBK - 1) / kGemmBK);
+  return pair_split_plan(tiles, capacity, num_kb, 256 * nw).ws_bytes;
+}
+
+extern "C" int lora_gemm_ex(const void* x, int64_t ldx, const void* w, int64_t ldw, const void* z, int64_t ldz,
+                            const void* bw, int64_t ldbw, const void* bias, void* out, int64_t ldo, int64_t M,
+                            int64_t N, int64_t K, int64_t R, float alpha, int64_t lo_offset, int dtype,
+                            void* workspace, size_t workspace_bytes, void* stream) {
+  return lora::gemm_impl(x, ldx, w, ldw, z, ldz, bw, ldbw, bias, out, ldo, M, N, K, R, alpha, lo_offset, dtype,
+                         workspace, workspace_bytes, stream);
 }

@@ -75,11 +75,13 @@ def gemm(x: torch.Tensor, w: torch.Tensor, z: torch.Tensor | None = None, bw: to
         bw = _lib.row_major(bw)
         if z.shape[0] != m or bw.shape[0] != n or z.shape[1] < rank or bw.shape[1] < rank:
             raise ValueError("gemm: z / bw must be [M|N, >= rank]")
-    _lib.call("lora_gemm", _lib.ptr(x), _lib.ld(x), _lib.ptr(w), _lib.ld(w),
+    ws_bytes = _lib.load().lora_gemm_workspace_size(m, n, k, int(rank))
+    ws = _lib.WORKSPACE.get(ws_bytes, x.device, "gemm") if ws_bytes else None
+    _lib.call("lora_gemm_ex", _lib.ptr(x), _lib.ld(x), _lib.ptr(w), _lib.ld(w),
               _lib.ptr(z) if rank > 0 else None, _lib.ld(z) if rank > 0 else 0,
               _lib.ptr(bw) if rank > 0 else None, _lib.ld(bw) if rank > 0 else 0,
               _lib.ptr(bias), _lib.ptr(out), out.stride(0), m, n, k, int(rank), float(alpha), int(lo_offset), _dt(x),
-              _lib.stream_handle(x.device))
+              _lib.ptr(ws), ws.numel() if ws is not None else 0, _lib.stream_handle(x.device))
     return out
 
 
