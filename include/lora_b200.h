@@ -292,19 +292,26 @@ LORA_API int lora_sgmv_expand(const void* y, int64_t ldy, const void* z, int64_t
                      int64_t ldo, int64_t T, int64_t S, int64_t N, int64_t r_max, float scale,
                      int dtype, void* stream);
 
-/* lora_sgmv_expand for the rank-major flat table b_flat [b_rows, N] (leading
- * dimension ldb) without row indirection: knowing the table's extent lets the
- * tensor-core form (units of one tile x 256 output columns, adapter rows and
- * y loaded by TMA, tcgen05 MMAs) bound its reads; it serves r_max <= 64 with
- * N and the leading dimensions multiples of 8 and 16-byte aligned rows, and
- * anything else goes to lora_sgmv_expand.  Replaces the same reference
- * functions as lora_sgmv_expand: the expand of segmented_branch.py:31-47 and
- * ragged_branch.py:18-27. */
-LORA_API int lora_sgmv_expand_ex(const void* y, int64_t ldy, const void* z, int64_t ldz, int z_dtype,
-                        const void* b, int64_t b_rows, int64_t ldb, const int64_t* offsets,
-                        const int64_t* ranks, int64_t n_adapters, const int32_t* tiles, void* out,
-                        int64_t ldo, int64_t T, int64_t S, int64_t N, int64_t r_max, float scale,
-                        int dtype, void* stream);
+/* The whole segmented branch in one call:
+ *   out[t, :] = y[t, :] + (scale * x[t] . A_a^T) . B_a     a = adapter of t's tile
+ * with a_flat [a_rows, K] (lda) and the rank-major b_flat [b_rows, N] (ldb,
+ * each adapter's scale folded in, as the reference's tables), tiles from
+ * lora_sgmv_schedule.  Three kernels on tensor cores: the shrink over (tile,
+ * K slice) units writing fp32 partials, their sum in slice order into a
+ * 16-bit hi/lo z, the expand over (tile, 256-column chunk) units with B and y
+ * read by TMA.  y may be NULL (out = the LoRA term).  Workspace:
+ * lora_sgmv_branch_workspace_size(T, S, K, r_max) bytes of scratch (no
+ * zeroing needed; one buffer per stream).  Serves r_max <= 64, K, N and the
+ * leading dimensions multiples of 8, 16-byte aligned rows; returns
+ * LORA_ERR_UNSUPPORTED otherwise (use lora_sgmv_shrink_ex + lora_sgmv_expand).
+ * Replaces the shrink / expand pair of ragged_branch.branch
+ * (ragged_branch.py:6-40) and segmented_branch (segmented_branch.py:12-60). */
+LORA_API size_t lora_sgmv_branch_workspace_size(int64_t T, int64_t S, int64_t K, int64_t r_max);
+LORA_API int lora_sgmv_branch(const void* x, int64_t ldx, const void* y, int64_t ldy, const void* a_flat,
+                     int64_t lda, int64_t a_rows, const void* b_flat, int64_t ldb, int64_t b_rows,
+                     const int64_t* offsets, const int64_t* ranks, int64_t n_adapters, const int32_t* tiles,
+                     void* out, int64_t ldo, int64_t T, int64_t S, int64_t K, int64_t N, int64_t r_max,
+                     float scale, int dtype, void* workspace, size_t workspace_bytes, void* stream);
 
 #ifdef __cplusplus
 }

@@ -77,8 +77,9 @@ SIGNATURES = {
                                  _I64, _I64, _F, _I, _I, _P, _SZ, _P]),
     "lora_sgmv_expand": (_I, [_P, _I64, _P, _I64, _I, _P, _I64, _I64, _P, _P, _I64, _P, _P, _P, _I64, _I64, _I64,
                               _I64, _I64, _F, _I, _P]),
-    "lora_sgmv_expand_ex": (_I, [_P, _I64, _P, _I64, _I, _P, _I64, _I64, _P, _P, _I64, _P, _P, _I64, _I64, _I64,
-                                 _I64, _I64, _F, _I, _P]),
+    "lora_sgmv_branch_workspace_size": (_SZ, [_I64, _I64, _I64, _I64]),
+    "lora_sgmv_branch": (_I, [_P, _I64, _P, _I64, _P, _I64, _I64, _P, _I64, _I64, _P, _P, _I64, _P, _P, _I64, _I64,
+                              _I64, _I64, _I64, _I64, _F, _I, _P, _SZ, _P]),
 }
 
 

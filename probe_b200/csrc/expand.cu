@@ -355,31 +355,3 @@ extern "C" int lora_sgmv_expand(const void* y, int64_t ldy, const void* z, int64
   dim3 grid(static_cast<unsigned>(expand_grid_x(max_tiles, nch, info.num_sms)), static_cast<unsigned>(nch));
   return launch_expand(p, dtype, z_dtype, grid, static_cast<cudaStream_t>(stream));
 }
-
-extern "C" int lora_sgmv_expand_ex(const void* y, int64_t ldy, const void* z, int64_t ldz, int z_dtype,
-                                   const void* b, int64_t b_rows, int64_t ldb, const int64_t* offsets,
-                                   const int64_t* ranks, int64_t n_adapters, const int32_t* tiles, void* out,
-                                   int64_t ldo, int64_t T, int64_t S, int64_t N, int64_t r_max, float scale, int dtype,
-                                   void* stream) {
-  if (out == nullptr || tiles == nullptr || offsets == nullptr || ranks == nullptr) return LORA_ERR_ARG;
-  if (r_max > 0 && (z == nullptr || b == nullptr)) return LORA_ERR_ARG;
-  if (dtype != LORA_BF16 && dtype != LORA_F16) return LORA_ERR_DTYPE;
-  if (z_dtype != LORA_F32 && z_dtype != dtype) return LORA_ERR_DTYPE;
-  if (T < 0 || N < 0 || S < 0 || r_max < 0 || r_max > 256 || n_adapters < 0 || b_rows < 0) return LORA_ERR_SHAPE;
-  if (T > INT32_MAX / 2 || N > INT32_MAX || ldo < N || (y != nullptr && ldy < N) || (r_max > 0 && ldz < r_max) ||
-      ldb < N)
-    return LORA_ERR_SHAPE;
-  if (y != nullptr && y == out) return LORA_ERR_ARG;
-  if (T == 0 || N == 0) return LORA_OK;
-  const int dev = current_device();
-  if (dev < 0 || !device_info(dev).is_sm100) return LORA_ERR_DEVICE;
-  const DeviceInfo& info = device_info(dev);
-  if (r_max > 0 && b_rows > 0) {
-    const int rc = launch_sgmv_expand_unit(y, ldy, z, ldz, z_dtype, b, b_rows, ldb, offsets, ranks, tiles,
-                                           sgmv_max_tiles(T, S), out, ldo, T, N, r_max, scale, dtype, info.num_sms,
-                                           info.err_word, stream);
-    if (rc != LORA_ERR_UNSUPPORTED) return rc;
-  }
-  return lora_sgmv_expand(y, ldy, z, ldz, z_dtype, b, ldb, 1, offsets, ranks, n_adapters, tiles, nullptr, out, ldo, T,
-                          S, N, r_max, scale, dtype, stream);
-}

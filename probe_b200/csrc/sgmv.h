@@ -82,26 +82,24 @@ int launch_sgmv_shrink_tc(const void* x, int64_t ldx, const void* a_flat, int64_
                           int z_dtype, int64_t z_width, int64_t T, int64_t K, int64_t r_max, float scale, int dtype,
                           int num_sms, int* err, void* stream);
 
-// Unit-scheduled tensor-core segmented shrink (sgmv_unit.cu): persistent CTAs
-// over (tile, K slice) units, deterministic split-K through the workspace
-// (split >= 2; tickets in its counter region, partials [split][T][r_max] fp32
-// after it).  Needs the row count of a_flat, no row indirection, aligned rows.
-int sgmv_unit_split(int64_t K);
-size_t sgmv_unit_workspace_bytes(int64_t T, int64_t r_max, int split);
+// Unit-scheduled tensor-core segmented branch (sgmv_unit.cu): a shrink over
+// (tile, K slice) units writing fp32 partials, a reduce kernel summing them in
+// slice order, and an expand over (tile, 256-column chunk) units.  Needs the
+// row counts of the tables (TMA bounds), no row indirection, aligned rows.
+// The shrink's workspace: sgmv_unit_shrink_workspace() bytes of partials.
+size_t sgmv_unit_shrink_workspace(int64_t T, int64_t K, int64_t r_max, int64_t max_tiles, int num_sms);
 int launch_sgmv_shrink_unit(const void* x, int64_t ldx, const void* a_flat, int64_t lda, int64_t a_rows,
                             const int64_t* offsets, const int64_t* ranks, const int32_t* tiles, int64_t max_tiles,
                             void* z, int64_t ldz, int z_dtype, int64_t z_width, int64_t T, int64_t K, int64_t r_max,
-                            float scale, int dtype, int split, void* workspace, size_t workspace_bytes, int num_sms,
-                            int* err, void* stream);
-
-// Unit-scheduled tensor-core segmented expand (sgmv_unit.cu): persistent CTAs
-// over (tile, 256-column chunk) units; rank-major b_flat [b_rows, N] read by
-// TMA as an MN-major operand, y by TMA, z rebuilt as a hi/lo 16-bit operand.
-// r_max <= 64, N and the leading dimensions multiples of 8, 16-byte aligned
-// rows, no row indirection; LORA_ERR_UNSUPPORTED otherwise.
-int launch_sgmv_expand_unit(const void* y, int64_t ldy, const void* z, int64_t ldz, int z_dtype, const void* b,
-                            int64_t b_rows, int64_t ldb, const int64_t* offsets, const int64_t* ranks,
-                            const int32_t* tiles, int64_t max_tiles, void* out, int64_t ldo, int64_t T, int64_t N,
-                            int64_t r_max, float scale, int dtype, int num_sms, int* err, void* stream);
+                            float scale, int dtype, void* workspace, size_t workspace_bytes, int num_sms, int* err,
+                            void* stream);
+// The whole branch out = y + (x . A_a^T) . B_a in three launches (r_max <= 64,
+// N and leading dimensions multiples of 8); LORA_ERR_UNSUPPORTED otherwise.
+size_t sgmv_unit_branch_workspace(int64_t T, int64_t K, int64_t r_max, int64_t max_tiles, int num_sms);
+int launch_sgmv_branch_unit(const void* x, int64_t ldx, const void* y, int64_t ldy, const void* a_flat, int64_t lda,
+                            int64_t a_rows, const void* b_flat, int64_t ldb, int64_t b_rows, const int64_t* offsets,
+                            const int64_t* ranks, const int32_t* tiles, int64_t max_tiles, void* out, int64_t ldo,
+                            int64_t T, int64_t K, int64_t N, int64_t r_max, float scale, int dtype, void* workspace,
+                            size_t workspace_bytes, int num_sms, int* err, void* stream);
 
 }  // namespace lora

@@ -408,14 +408,23 @@ extern "C" int lora_sgmv_pick_split_k(int64_t T, int64_t K, int64_t r_max) {
   if (T <= 0 || K <= 0 || r_max <= 0) return 1;
   const int dev = current_device();
   const int sms = dev >= 0 ? device_info(dev).num_sms : 148;
-  (void)sms;
-  return sgmv_unit_split(K);
+  return sgmv_shrink_block_split(T, K, sms > 0 ? sms : 148);
 }
 
 extern "C" size_t lora_sgmv_shrink_workspace_size(int64_t T, int64_t S, int64_t z_width, int split_k) {
-  if (T <= 0 || z_width <= 0 || split_k <= 1) return 256;
+  if (T <= 0 || z_width <= 0) return 256;
+  // the unit-scheduled tensor-core shrink keeps its partials after the
+  // counter region; its K split (<= 16, about four units per SM over the
+  // tile capacity) is bounded here without K
+  const int dev = current_device();
+  const int sms = dev >= 0 ? device_info(dev).num_sms : 148;
+  const int64_t max_tiles = std::max<int64_t>(sgmv_max_tiles(T, S), 1);
+  const int64_t unit_split = std::min<int64_t>(16, (4 * static_cast<int64_t>(sms > 0 ? sms : 148) + max_tiles - 1) /
+                                                       max_tiles);
+  const size_t unit = kCounterBytes + round256(static_cast<size_t>(unit_split) * T * ((z_width + 15) / 16 * 16) * 4);
+  if (split_k <= 1) return unit;
   const size_t partial = static_cast<size_t>(split_k) * T * z_width * sizeof(float);
-  return kCounterBytes + round256(partial);
+  return std::max(unit, kCounterBytes + round256(partial));
 }
 
 namespace {
@@ -450,10 +459,12 @@ int sgmv_shrink_impl(const void* x, int64_t ldx, const void* a_flat, int64_t lda
   // count of a_flat and no row indirection.  Then dense 64-token blocks on
   // mma.sync (sgmv_block.cu); the per-tile kernel below covers the layouts
   // none of them takes (unaligned rows, r_max > 128).
-  if (rows == nullptr && a_rows > 0 && r_max > 0 && K > 0 && split_k > 1) {
+  if (rows == nullptr && a_rows > 0 && r_max > 0 && K > 0 && workspace != nullptr &&
+      workspace_bytes > kCounterBytes) {
     const int rc = launch_sgmv_shrink_unit(x, ldx, a_flat, lda, a_rows, offsets, ranks, tiles, sgmv_max_tiles(T, S), z,
-                                           ldz, z_dtype, z_width, T, K, r_max, scale, dtype, split_k, workspace,
-                                           workspace_bytes, info.num_sms, info.err_word, stream);
+                                           ldz, z_dtype, z_width, T, K, r_max, scale, dtype,
+                                           static_cast<char*>(workspace) + kCounterBytes,
+                                           workspace_bytes - kCounterBytes, info.num_sms, info.err_word, stream);
     if (rc != LORA_ERR_UNSUPPORTED) return rc;
   }
   if (rows == nullptr && a_rows > 0 && r_max > 0 && K > 0) {
@@ -657,4 +668,35 @@ extern "C" int lora_shrink_static_scratch(const void* x, int64_t ldx, const void
       std::min<int64_t>(tiles, std::max<int64_t>(1, (4 * static_cast<int64_t>(sms) + split_k - 1) / split_k));
   dim3 grid(static_cast<unsigned>(gx), static_cast<unsigned>(split_k));
   return launch_shrink(p, dtype, z_dtype, aligned, grid, s);
+}
+
+extern "C" size_t lora_sgmv_branch_workspace_size(int64_t T, int64_t S, int64_t K, int64_t r_max) {
+  if (T <= 0 || K <= 0 || r_max <= 0) return 256;
+  const int dev = current_device();
+  const int sms = dev >= 0 ? device_info(dev).num_sms : 148;
+  return sgmv_unit_branch_workspace(T, K, r_max, sgmv_max_tiles(T, S), sms > 0 ? sms : 148);
+}
+
+extern "C" int lora_sgmv_branch(const void* x, int64_t ldx, const void* y, int64_t ldy, const void* a_flat,
+                                int64_t lda, int64_t a_rows, const void* b_flat, int64_t ldb, int64_t b_rows,
+                                const int64_t* offsets, const int64_t* ranks, int64_t n_adapters,
+                                const int32_t* tiles, void* out, int64_t ldo, int64_t T, int64_t S, int64_t K,
+                                int64_t N, int64_t r_max, float scale, int dtype, void* workspace,
+                                size_t workspace_bytes, void* stream) {
+  if (x == nullptr || a_flat == nullptr || b_flat == nullptr || offsets == nullptr || ranks == nullptr ||
+      tiles == nullptr || out == nullptr)
+    return LORA_ERR_ARG;
+  if (dtype != LORA_BF16 && dtype != LORA_F16) return LORA_ERR_DTYPE;
+  if (T < 0 || S < 0 || K < 0 || N < 0 || r_max < 0 || n_adapters < 0 || a_rows < 0 || b_rows < 0)
+    return LORA_ERR_SHAPE;
+  if (ldx < K || lda < K || ldb < N || ldo < N || (y != nullptr && ldy < N)) return LORA_ERR_SHAPE;
+  if (y != nullptr && y == out) return LORA_ERR_ARG;
+  if (T == 0 || N == 0) return LORA_OK;
+  if (r_max == 0 || K == 0) return LORA_ERR_UNSUPPORTED;
+  const int dev = current_device();
+  if (dev < 0 || !device_info(dev).is_sm100) return LORA_ERR_DEVICE;
+  const DeviceInfo& info = device_info(dev);
+  return launch_sgmv_branch_unit(x, ldx, y, ldy, a_flat, lda, a_rows, b_flat, ldb, b_rows, offsets, ranks, tiles,
+                                 sgmv_max_tiles(T, S), out, ldo, T, K, N, r_max, scale, dtype, workspace,
+                                 workspace_bytes, info.num_sms, info.err_word, stream);
 }

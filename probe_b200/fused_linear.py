@@ -386,29 +386,36 @@ def build_plan(probe, weight, bias, a, b, scale, base_layer=None):
     if weight.dtype != dtype or a.dtype != dtype or b.dtype != dtype:
         raise TypeError("build_plan: x, weight, a and b must share one dtype")
 
-    runners = {}
+    # Factories, not runners: a variant's plan-time state (kconcat's [B | B],
+    # concat's [W; A; 0]) is built only for the variant that will run (or for
+    # every candidate of a timing race), never on a call that picks another.
+    makers = {}
     if eligible("decode", rows, k, n, r, dtype, False):
-        runners["decode"] = lambda x: _decode(x, weight, bias, a, b, scale)
+        makers["decode"] = lambda: (lambda x: _decode(x, weight, bias, a, b, scale))
     if eligible("kconcat", rows, k, n, r, dtype, False):
-        runners["kconcat"] = _KConcat(weight, bias, a, b, scale)
+        makers["kconcat"] = lambda: _KConcat(weight, bias, a, b, scale)
     tune = os.environ.get("LORAFORGE_TUNE", "0") == "1"
     forced = _forced_variant()
     if tune or forced in ("hybrid", "concat"):
         if eligible("hybrid", rows, k, n, r, dtype, False):
-            runners["hybrid"] = lambda x: _hybrid(x, weight, bias, a, b, scale)
+            makers["hybrid"] = lambda: (lambda x: _hybrid(x, weight, bias, a, b, scale))
         pack = os.environ.get("LORAFORGE_PACK", "view").strip().lower()
         if pack not in ("0", "off", "none") and eligible("concat", rows, k, n, r, dtype, True):
-            weight_aug = augment_weight(weight, a)
-            bias_aug = augment_bias(bias, r)
-            runners["concat"] = lambda x: _concat(x, weight_aug, bias_aug, b, scale, n)
-    if not runners:
+            def make_concat():
+                weight_aug = augment_weight(weight, a)
+                bias_aug = augment_bias(bias, r)
+                return lambda x: _concat(x, weight_aug, bias_aug, b, scale, n)
+            makers["concat"] = make_concat
+    if not makers:
         # Odd K with many rows: the decode kernel over 64-row chunks.
         return lambda x: _rowwise(lambda xs: _decode(xs, weight, bias, a, b, scale), x)
 
-    if forced in runners:
-        return runners[forced]
+    if forced in makers:
+        return makers[forced]()
     if not tune:
-        return runners.get(_default_variant(rows, k, r)) or next(iter(runners.values()))
+        choice = _default_variant(rows, k, r)
+        return makers[choice]() if choice in makers else next(iter(makers.values()))()
+    runners = {nm: make() for nm, make in makers.items()}
     key = (rows, k, n, r, dtype, torch.cuda.current_device())
     variant = select_variant({nm: (lambda f=fn: f(probe)) for nm, fn in runners.items()}, key)
     return runners[variant]

@@ -305,17 +305,43 @@ def sgmv_expand(y: torch.Tensor | None, z: torch.Tensor, b: torch.Tensor, b_sj: 
         out = torch.empty((z.shape[0], n), device=z.device, dtype=dtype)
     offsets = _i64(offsets, z.device)
     ranks = _i64(ranks, z.device)
-    if rows is None and b_sn == 1 and b.dim() == 2 and b.stride(1) == 1 and b_sj == b.stride(0):
-        # flat rank-major table: the entry point that knows its row count (TMA-bounded tensor-core form)
-        _lib.call("lora_sgmv_expand_ex", _lib.ptr(y), _lib.ld(y) if y is not None else 0, _lib.ptr(z), _lib.ld(z),
-                  _lib.dtype_code(z.dtype), _lib.ptr(b), b.shape[0], int(b_sj), _lib.ptr(offsets), _lib.ptr(ranks),
-                  offsets.numel(), _lib.ptr(tiles), _lib.ptr(out), out.stride(0), t, s, n, int(r_max), float(scale),
-                  _lib.dtype_code(dtype), _lib.stream_handle(z.device))
-        return out
     if rows is not None:
         rows = _i64(rows, z.device)
     _lib.call("lora_sgmv_expand", _lib.ptr(y), _lib.ld(y) if y is not None else 0, _lib.ptr(z), _lib.ld(z),
               _lib.dtype_code(z.dtype), _lib.ptr(b.contiguous()), int(b_sj), int(b_sn), _lib.ptr(offsets),
               _lib.ptr(ranks), offsets.numel(), _lib.ptr(tiles), _lib.ptr(rows), _lib.ptr(out), out.stride(0), t, s, n,
               int(r_max), float(scale), _lib.dtype_code(dtype), _lib.stream_handle(z.device))
+    return out
+
+
+def sgmv_branch(x: torch.Tensor, y: torch.Tensor | None, a_flat: torch.Tensor, b_flat: torch.Tensor,
+                offsets: torch.Tensor, ranks: torch.Tensor, tiles: torch.Tensor, s: int, r_max: int,
+                scale: float = 1.0, out: torch.Tensor | None = None) -> torch.Tensor | None:
+    """``out = y + (scale * x @ A_a.T) @ B_a`` per tile in one ABI call (tensor-core shrink,
+    ordered reduction, tensor-core expand).  Returns None when the shape is outside
+    that path (r_max > 64, unaligned rows): then use sgmv_shrink + sgmv_expand."""
+    _lib.require_cuda(x, a_flat, b_flat, y, where="sgmv_branch")
+    _check_half(x, "sgmv_branch")
+    x = _lib.row_major(x)
+    a_flat = _lib.row_major(a_flat)
+    b_flat = _lib.row_major(b_flat)
+    t, k = x.shape
+    n = b_flat.shape[1]
+    if y is not None:
+        y = _lib.row_major(y)
+    if out is None:
+        out = torch.empty((t, n), device=x.device, dtype=x.dtype)
+    lib = _lib.load()
+    ws_bytes = lib.lora_sgmv_branch_workspace_size(t, s, k, int(r_max))
+    ws = _lib.WORKSPACE.get(ws_bytes, x.device, "branch")
+    offsets = _i64(offsets, x.device)
+    ranks = _i64(ranks, x.device)
+    rc = lib.lora_sgmv_branch(_lib.ptr(x), _lib.ld(x), _lib.ptr(y), _lib.ld(y) if y is not None else 0,
+                              _lib.ptr(a_flat), _lib.ld(a_flat), a_flat.shape[0], _lib.ptr(b_flat), _lib.ld(b_flat),
+                              b_flat.shape[0], _lib.ptr(offsets), _lib.ptr(ranks), offsets.numel(), _lib.ptr(tiles),
+                              _lib.ptr(out), out.stride(0), t, s, k, n, int(r_max), float(scale), _dt(x),
+                              _lib.ptr(ws), ws.numel(), _lib.stream_handle(x.device))
+    if rc == _lib.LORA_ERR_UNSUPPORTED:
+        return None
+    _lib.check(rc, "lora_sgmv_branch")
     return out

@@ -23,5 +23,9 @@ def branch(x, y, a, b, offsets, ranks, indices, rmax, skip_zero=True, split_k=8)
     t, k = x.shape
     n = y.shape[1]
     tiles, s = kernels.sgmv_schedule(t, offsets.numel(), ids=indices)
+    out = kernels.sgmv_branch(x, y, a, b, offsets, ranks, tiles, s, rmax)
+    if out is not None:
+        return out
+    # ranks above 64 or unaligned rows: shrink then expand
     z = kernels.sgmv_shrink(x, a, offsets, ranks, tiles, s, rmax, z_dtype=torch.float32, split_k=split_k)
     return kernels.sgmv_expand(y, z, b, n, 1, offsets, ranks, tiles, s, n, rmax)

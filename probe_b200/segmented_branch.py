@@ -45,6 +45,10 @@ def segmented_branch_varlen(x, y, a, b, offsets, ranks, seg_start, seg_adapter, 
     total, k = x.shape
     n = y.shape[1]
     tiles, s = kernels.sgmv_schedule(total, offsets.numel(), seg_start=seg_start, seg_adapter=seg_adapter)
+    out = kernels.sgmv_branch(x, y, a, b, offsets, ranks, tiles, s, rmax)
+    if out is not None:
+        return out
+    # ranks above 64 or unaligned rows: shrink then expand
     z = kernels.sgmv_shrink(x, a, offsets, ranks, tiles, s, rmax, z_dtype=torch.float32,
                             split_k=split_k if split_k and split_k > 0 else 0)
     return kernels.sgmv_expand(y, z, b, n, 1, offsets, ranks, tiles, s, n, rmax)

@@ -85,3 +85,64 @@ def test_unit_shrink_out_of_range_ids_are_zero_and_reported():
     assert np.abs(np64(z)[keep] - want[keep]).max() < 2e-4
     assert _lib.device_error() == 110  # out-of-range adapter id recorded (and cleared by the read)
     assert _lib.device_error() == 0
+
+
+def _branch_case(t, k, n, ranks, ids, seed, with_y=True):
+    g = torch.Generator().manual_seed(seed)
+    rk = torch.tensor(ranks, dtype=torch.int64)
+    offs = torch.zeros_like(rk)
+    offs[1:] = torch.cumsum(rk, 0)[:-1]
+    tot = max(int(rk.sum()), 1)
+    a = (torch.randn(tot, k, generator=g) / math.sqrt(k)).to(torch.bfloat16).to(DEV)
+    b = (torch.randn(tot, n, generator=g) * 0.3).to(torch.bfloat16).to(DEV)
+    x = randn((t, k), 1.0, seed=seed + 1)
+    y = randn((t, n), 1.0, seed=seed + 2) if with_y else None
+    return x, y, a, b, offs.to(DEV), rk.to(DEV)
+
+
+@pytest.mark.parametrize("t,k,n,ranks,mode,with_y", [
+    (4096, 4096, 4096, [4, 8, 16, 32, 64] * 12 + [8] * 4, "zipf", True),  # C3-like
+    (1000, 1024, 320, [4, 8, 16, 32, 64], "random", True),                # one-token tiles, N % 256 != 0
+    (777, 576, 512, [64, 13, 0, 33], "runs", True),                      # rank 0, last tile cut by T
+    (300, 256, 1024, [16, 48], "runs", False),                           # y = None
+])
+def test_unit_branch_matches_oracle(t, k, n, ranks, mode, with_y):
+    from oracle import checks
+
+    rng = np.random.default_rng(t + n)
+    n_ad = len(ranks)
+    if mode == "random":
+        ids = rng.integers(0, n_ad, size=t)
+    elif mode == "runs":
+        ids = np.repeat(rng.integers(0, n_ad, size=t // 5 + 1), 5)[:t]
+    else:
+        lens = np.maximum(1, (t * (np.arange(1, 129) ** -1.1) / (np.arange(1, 129) ** -1.1).sum()).astype(int))
+        lens[0] += t - lens.sum()
+        ids = np.repeat(rng.integers(0, n_ad, size=128), lens)
+    x, y, a, b, offs, rk = _branch_case(t, k, n, ranks, ids, seed=t)
+    tiles, s = kernels.sgmv_schedule(t, offs.numel(), ids=torch.as_tensor(ids, device=DEV))
+    out = kernels.sgmv_branch(x, y, a, b, offs, rk, tiles, s, max(ranks))
+    assert out is not None
+    yy = y if y is not None else torch.zeros((t, n), device=DEV, dtype=torch.bfloat16)
+    rep = checks.branch_report(out, x, yy, a, b, offs, rk, ids, n_random=64)
+    assert rep["ok"], rep
+    again = kernels.sgmv_branch(x, y, a, b, offs, rk, tiles, s, max(ranks))
+    assert torch.equal(out, again)
+    assert _lib.device_error() == 0
+
+
+def test_unit_branch_declines_outside_its_domain():
+    """Ranks above 64, N or K not a multiple of 64: the one-call branch declines and
+    the public branch surfaces take shrink + expand instead (same results)."""
+    from probe_b200 import ragged_branch
+
+    for k, n, ranks in ((256, 256, [96, 16]), (256, 264, [16, 32]), (520, 256, [16, 32])):
+        ids = np.repeat([0, 1], 64)
+        x, y, a, b, offs, rk = _branch_case(128, k, n, ranks, ids, seed=9)
+        idt = torch.as_tensor(ids, device=DEV)
+        tiles, s = kernels.sgmv_schedule(128, 2, ids=idt)
+        assert kernels.sgmv_branch(x, y, a, b, offs, rk, tiles, s, max(ranks)) is None
+        out = ragged_branch.branch(x, y, a, b, offs, rk, idt, max(ranks))
+        want = orc.ragged_branch(np64(x), np64(y), np64(a), np64(b), offs.cpu().numpy(), rk.cpu().numpy(), ids)
+        from tests.helpers import assert_parity
+        assert_parity(out, want)
