@@ -760,9 +760,15 @@ struct PairSplit {
   size_t ws_bytes;  // workspace: ticket region + fp32 partials
 };
 
+// Splits pay only for long K: each piece's partial (256 x tile_n fp32) makes
+// a round trip through L2 and the last piece to finish sums them, a cost that
+// measured on B200 matched the time saved at K = 5120 and was clearly below it
+// at K = 13824 (C5 shard shapes).
+constexpr int kSplitMinKb = 128;
+
 PairSplit pair_split_plan(int64_t tiles, int pairs, int num_kb, int tile_n) {
   PairSplit sp{static_cast<int>(tiles), 1, 0};
-  if (pairs <= 0 || tiles <= 0) return sp;
+  if (pairs <= 0 || tiles <= 0 || num_kb < kSplitMinKb) return sp;
   const int64_t rem = tiles % pairs;
   if (rem == 0) return sp;
   int64_t s = pairs / rem;
@@ -892,21 +898,37 @@ int pair_tile_width(int64_t M, int64_t N, int64_t K, int64_t R, int pairs, bool 
   if (force == 1) return 2;
   const int64_t mt = (M + 255) / 256;
   const int num_kb = static_cast<int>((K + kGemmBK - 1) / kGemmBK + (R + kGemmBK - 1) / kGemmBK);
+  const int64_t tiles2 = mt * ((N + 511) / 512);
+  // With few 256 x 512 tiles per pair their unhidden epilogue and pipeline
+  // fill cost more than the wider tile saves (measured at 4095 and 8190 rows,
+  // K = 5120): keep them for at least five waves, or four with long K.
+  if (tiles2 < 5 * static_cast<int64_t>(pairs) && !(tiles2 >= 4 * static_cast<int64_t>(pairs) && num_kb >= 128))
+    return 1;
   const double w1 = pair_waves(mt * ((N + 255) / 256), pairs, num_kb, can_split);
-  const double w2 = pair_waves(mt * ((N + 511) / 512), pairs, num_kb, can_split);
+  const double w2 = pair_waves(tiles2, pairs, num_kb, can_split);
   return 1.8 * w2 < w1 ? 2 : 1;
 }
 
 // Pair tiles when the output is wide and there are enough 256x256 tiles to
-// keep every SM pair busy; LORA_B200_GEMM=1sm / 2sm forces one or the other.
-bool use_pair_tiles(int64_t M, int64_t N, int num_sms) {
+// keep every SM pair busy -- or, with a workspace for the split tail, when
+// cutting the few tiles there are along K puts at least half the pairs to
+// work (a rank-224 shrink of a few thousand tokens: 16 tiles become 64
+// pieces instead of 64 single-CTA tiles on 64 SMs).  LORA_B200_GEMM=1sm /
+// 2sm forces one or the other.
+bool use_pair_tiles(int64_t M, int64_t N, int64_t K, int64_t R, int num_sms, bool can_split) {
   const char* force = std::getenv("LORA_B200_GEMM");
   if (force != nullptr && std::strcmp(force, "1sm") == 0) return false;
   const int64_t tiles = ((M + 255) / 256) * ((N + 255) / 256);
   if (force != nullptr && std::strcmp(force, "2sm") == 0) return N > 128;
+  if (N <= 128) return false;
   // Outputs wider than 128 columns (the rank-224 shrink included: one 256-wide
   // pair tile reads x once instead of twice) once the grid fills a wave of pairs.
-  return N > 128 && tiles >= num_sms / 2;
+  const int pairs = num_sms / 2;
+  if (tiles >= pairs) return true;
+  if (!can_split || env_int("LORA_B200_SPLIT_TAIL", 1) == 0) return false;
+  const int num_kb = static_cast<int>((K + kGemmBK - 1) / kGemmBK + (R + kGemmBK - 1) / kGemmBK);
+  const PairSplit sp = pair_split_plan(tiles, pairs, num_kb, 256);
+  return sp.split > 1 && tiles * sp.split * 2 >= pairs;
 }
 
 }  // namespace
@@ -950,7 +972,7 @@ int gemm_impl(const void* x, int64_t ldx, const void* w, int64_t ldw, const void
   if (!info.is_sm100) return LORA_ERR_DEVICE;
   const int bn = gemm_pick_bn(M, N, info.num_sms);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  if (use_pair_tiles(M, N, info.num_sms)) {
+  if (use_pair_tiles(M, N, K, R, info.num_sms, ws != nullptr)) {
     if (pair_tile_width(M, N, K, R, info.num_sms / 2, ws != nullptr) == 2) {
       if (dtype == LORA_BF16)
         return launch_gemm_pair<4, 2, __nv_bfloat16>(x, ldx, w, ldw, z, ldz, bw, ldbw, bias, out, ldo, M, N, K, R,
@@ -987,7 +1009,7 @@ extern "C" size_t lora_gemm_workspace_size(int64_t M, int64_t N, int64_t K, int6
   const int dev = current_device();
   if (dev < 0) return 0;
   const DeviceInfo& info = device_info(dev);
-  if (!info.is_sm100 || !use_pair_tiles(M, N, info.num_sms)) return 0;
+  if (!info.is_sm100 || !use_pair_tiles(M, N, K, R, info.num_sms, true)) return 0;
   const int nw = pair_tile_width(M, N, K, R, info.num_sms / 2, true);
   cudaError_t st = cudaSuccess;
   const int capacity = nw == 2 ? pair_capacity<4, 2, __nv_bfloat16>(dev, info, &st)

@@ -721,13 +721,17 @@ __global__ void __launch_bounds__(kExThreads, 1) sgmv_expand_unit_kernel(const _
 // ===================================================================== host
 namespace {
 
-// K slices of the shrink: about four units per SM over the schedule's tile
-// capacity, at least 4 k-blocks per slice, at most 16 slices.
-int unit_slices(int64_t max_tiles, int64_t K, int num_sms) {
+// K slices of the shrink: about four units per SM counting one tile per 64
+// tokens (the fewest any schedule of T tokens has), at least 4 k-blocks per
+// slice, at most 16 slices.  It depends on T and K only, so per-token ids
+// and segment tables describing the same batch sum their partials alike and
+// give bit-identical results.
+int unit_slices(int64_t T, int64_t K, int num_sms) {
   const int64_t kb = std::max<int64_t>((K + kUnitBK - 1) / kUnitBK, 1);
-  int64_t s = (4 * static_cast<int64_t>(num_sms) + max_tiles - 1) / std::max<int64_t>(max_tiles, 1);
+  const int64_t blocks = std::max<int64_t>((T + 63) / 64, 1);
+  int64_t s = (4 * static_cast<int64_t>(num_sms) + blocks - 1) / blocks;
   s = std::max<int64_t>(1, std::min<int64_t>({s, 16, std::max<int64_t>(kb / 4, 1)}));
-  const int64_t per = (kb + s - 1) / s;
+  const int64_t per = ((kb + s - 1) / s + kShKC - 1) / kShKC * kShKC;
   return static_cast<int>((kb + per - 1) / per);
 }
 
@@ -859,7 +863,7 @@ bool shrink_units_ok(const void* x, int64_t ldx, const void* a_flat, int64_t lda
 }  // namespace
 
 size_t sgmv_unit_shrink_workspace(int64_t T, int64_t K, int64_t r_max, int64_t max_tiles, int num_sms) {
-  return static_cast<size_t>(unit_slices(max_tiles, K, num_sms)) * static_cast<size_t>(T) *
+  return static_cast<size_t>(unit_slices(T, K, num_sms)) * static_cast<size_t>(T) *
          static_cast<size_t>(rpad(r_max)) * sizeof(float);
 }
 
@@ -870,7 +874,7 @@ int launch_sgmv_shrink_unit(const void* x, int64_t ldx, const void* a_flat, int6
                             void* stream) {
   if (!shrink_units_ok(x, ldx, a_flat, lda, a_rows, T, K, r_max, max_tiles)) return LORA_ERR_UNSUPPORTED;
   if (z_dtype != LORA_F32 && z_dtype != dtype) return LORA_ERR_DTYPE;
-  const int S = unit_slices(max_tiles, K, num_sms);
+  const int S = unit_slices(T, K, num_sms);
   if (workspace == nullptr || !unit_al16(workspace) ||
       workspace_bytes < sgmv_unit_shrink_workspace(T, K, r_max, max_tiles, num_sms))
     return LORA_ERR_UNSUPPORTED;
@@ -902,7 +906,7 @@ int launch_sgmv_branch_unit(const void* x, int64_t ldx, const void* y, int64_t l
   if (workspace == nullptr || !unit_al16(workspace) ||
       workspace_bytes < sgmv_unit_branch_workspace(T, K, r_max, max_tiles, num_sms))
     return LORA_ERR_UNSUPPORTED;
-  const int S = unit_slices(max_tiles, K, num_sms);
+  const int S = unit_slices(T, K, num_sms);
   float* partial = static_cast<float*>(workspace);
   const size_t part = (sgmv_unit_shrink_workspace(T, K, r_max, max_tiles, num_sms) + 255) / 256 * 256;
   void* z_hl = static_cast<char*>(workspace) + part;

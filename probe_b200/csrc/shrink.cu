@@ -418,9 +418,9 @@ extern "C" size_t lora_sgmv_shrink_workspace_size(int64_t T, int64_t S, int64_t 
   // tile capacity) is bounded here without K
   const int dev = current_device();
   const int sms = dev >= 0 ? device_info(dev).num_sms : 148;
-  const int64_t max_tiles = std::max<int64_t>(sgmv_max_tiles(T, S), 1);
-  const int64_t unit_split = std::min<int64_t>(16, (4 * static_cast<int64_t>(sms > 0 ? sms : 148) + max_tiles - 1) /
-                                                       max_tiles);
+  const int64_t blocks = std::max<int64_t>((T + 63) / 64, 1);
+  const int64_t unit_split = std::min<int64_t>(16, (4 * static_cast<int64_t>(sms > 0 ? sms : 148) + blocks - 1) /
+                                                       blocks);
   const size_t unit = kCounterBytes + round256(static_cast<size_t>(unit_split) * T * ((z_width + 15) / 16 * 16) * 4);
   if (split_k <= 1) return unit;
   const size_t partial = static_cast<size_t>(split_k) * T * z_width * sizeof(float);

@@ -1,11 +1,11 @@
 """CTA-pair GEMM with a split tail (GPU): the tiles of the last partial wave
 cut along K across the idle pairs, partials summed in a fixed order.
 
-Shapes are picked so the tail is split (lora_gemm_workspace_size > 0): the
-8-way shard of the C5 q projection (4095 x 5120 x 5120 with the rank-224
-hi/lo K-slice), a single partial wave (all tiles split), both tile widths
-(256 and 512 columns), bias and alpha, and the hi/lo output form of the
-large-rank shrink.  Each is checked against the float64 oracle, against the
+Shapes are picked so the tail is split (lora_gemm_workspace_size > 0, which
+needs K >= 8192): the 8- and 4-way shards of the C5 FFN-down projection
+(with the rank-224 hi/lo K-slice), a narrow output whose few tiles are all
+split, both tile widths (256 and 512 columns), bias and alpha, and the hi/lo
+output form of the large-rank shrink.  Each is checked against the float64 oracle, against the
 same call without a workspace (no split), and for bit-identical repeats.
 """
 
@@ -32,18 +32,20 @@ def _gemm_no_split(x, w, z=None, bw=None, rank=0, bias=None, alpha=1.0, lo_offse
     return out
 
 
-SHAPES = [  # (M, K, N, R): tile width and split chosen by the library for 74 resident pairs
-    (4095, 5120, 5120, 448),   # C5 q shard at 8 GPUs (hi/lo tail of rank 224): 256x512 tiles, 6 pieces
-    (4095, 13824, 5120, 448),  # C5 FFN-down shard
-    (8190, 5120, 5120, 448),   # C5 q shard at 4 GPUs: 3 pieces
-    (2000, 2048, 8192, 0),     # 256x256 tiles, 2 pieces
-    (1300, 1024, 16384, 0),    # 4 pieces
-    (5000, 1024, 4096, 32),
+SHAPES = [  # (M, K, N, R): long K (the tail splits only from K = 8192), for 74 resident pairs
+    (4095, 13824, 5120, 448),  # C5 FFN-down shard at 8 GPUs (hi/lo tail of rank 224): 3 pieces
+    (8190, 13824, 5120, 448),  # the same at 4 GPUs: 256x512 tiles, 3 pieces
+    (2000, 8192, 8192, 0),     # 256x256 tiles, 2 pieces
+    (1300, 16384, 4096, 0),    # 3 pieces
+    (5000, 8192, 4096, 32),
+    (4095, 13824, 224, 0),     # a narrow output on few tiles: every tile split (the rank-224 shrink)
 ]
 
 
 def test_c5_shard_splits_its_tail():
-    assert _lib.load().lora_gemm_workspace_size(4095, 5120, 5120, 448) > 0
+    lib = _lib.load()
+    assert lib.lora_gemm_workspace_size(4095, 5120, 13824, 448) > 0  # FFN down: long K
+    assert lib.lora_gemm_workspace_size(4095, 5120, 5120, 448) == 0   # q: K too short to pay
 
 
 @pytest.mark.parametrize("m,k,n,r", SHAPES)
@@ -71,9 +73,10 @@ def test_split_tail_gemm(m, k, n, r):
     assert _lib.device_error() == 0
 
 
-def test_split_tail_hilo_output():
-    """The hi/lo output form ([round(v) | v - round(v)]) through the split tail's reduction."""
-    m, k, n = 2000, 2048, 8192
+@pytest.mark.parametrize("m,k,n", [(2000, 8192, 8192), (4095, 13824, 224)])
+def test_split_tail_hilo_output(m, k, n):
+    """The hi/lo output form ([round(v) | v - round(v)], the rank-224 shrink's)
+    through the split tail's reduction."""
     if _lib.load().lora_gemm_workspace_size(m, n, k, 0) == 0:
         pytest.skip("no split tail for this shape on this device")
     x = randn((m, k), 1.0, seed=7)
