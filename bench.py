@@ -55,8 +55,8 @@ M_TOKENS = 32760
 CPU_SAMPLE_TOKENS = 4096
 # DRAM read + write of one fused-GEMM launch (C5 q projection), from the full
 # ncu capture at M = 16384 committed under profiles/, scaled linearly to M:
-# 820.2 MB read + 152.6 MB write per launch at M = 16384 (CTA-pair kernel, 256x512 tiles).
-NCU_TRAFFIC_Q_16384 = 972.8e6
+# 822.1 MB read + 151.3 MB write per launch at M = 16384 (CTA-pair kernel, 256x512 tiles).
+NCU_TRAFFIC_Q_16384 = 973.4e6
 L2_BYTES = 126e6
 
 
@@ -443,6 +443,8 @@ def run_gpu(args):
     flops_local = sum(p.flops() for p in projs)
     gemm_flops = sum(2.0 * p.m * p.k * p.n + 2.0 * p.m * p.r * p.n for p in projs)  # algorithmic (rank r)
     launches_per_step = 2 * len(projs)  # shrink GEMM + fused GEMM per projection
+    x_min_mb = min(p.m * p.k * 2 for p in projs) / 1e6
+    stream_gb = sum(p.m * (p.k + p.n) * 2 for p in projs) / 1e9  # activations read + written per step
 
     clocks = ClockSampler(local)
     ms_step, gemm_ms_step, clock_info = _time_c5(projs, runners, outs, args.steps, args.warmup, world, dist, clocks)
@@ -513,8 +515,8 @@ def run_gpu(args):
                    "parallelism": (f"token-sharded x{world} (contiguous shards of the {total}-token batch)"
                                    if args.scaling == "strong" else f"x{world} replicas of the {total}-token batch")
                    + ", weights+adapters replicated, no data-path collective",
-                   "l2": "every input > 126 MB L2 at N=1 (x >= 335 MB per projection) and 5.2 GB of activations "
-                         "streamed per step; no flush"},
+                   "l2": (f"x >= {x_min_mb:.0f} MB per projection, {stream_gb:.2f} GB of activations streamed "
+                          f"per step (> 126 MB L2 between reuses of any input); no flush")},
         "roofline": {"bound": "tensor",
                      "kernel": "gemm_tc2_kernel (CTA pair, tcgen05 cta_group::2) fused base + LoRA K-slice",
                      "achieved": round(gemm_achieved, 2), "peak": peak, "unit": "TFLOP/s",
