@@ -72,8 +72,8 @@ def parse():
     p.add_argument("--no-cpu", action="store_true")
     p.add_argument("--no-parity", action="store_true")
     p.add_argument("--no-configs", action="store_true", help="skip the C1-C4 entries of the N=1 line")
-    p.add_argument("--workload", default="c5", choices=["c1", "c2", "c3", "c4", "c5"],
-                   help="c5 is the headline; c1-c4 alone print one line each against their own rooflines")
+    p.add_argument("--workload", default="c5", choices=["c1", "c2", "c3", "c4", "c5", "gate"],
+                   help="c5 is the headline; c1-c4 (and gate: plain GEMM vs cuBLAS) alone print one line each")
     return p.parse_args()
 
 
@@ -771,6 +771,55 @@ def _config_c4(steps):
                       "projection, 7 projections per step"}
 
 
+GATE_SHAPES = (  # (name, M, K, N): the layer shapes the reference's CUTLASS-vs-cuBLAS gate runs
+    ("wan/attn-1536", 32760, 1536, 1536),
+    ("wan/ffn-up-8960", 32760, 1536, 8960),
+    ("wan/ffn-down-1536", 32760, 8960, 1536),
+    ("llm/prefill-4096", 4096, 4096, 4096),
+)
+
+
+def _config_gate(steps):
+    """Plain GEMM (no LoRA) of this library against cuBLAS (torch's linear) on
+    the gate shapes of loraforge_kernels/bench_cutlass_gate.py:21-26: fusing
+    the LoRA expand into the GEMM only pays if the GEMM itself is cuBLAS-class."""
+    import torch
+
+    from probe_b200 import kernels
+
+    dev = torch.device("cuda", 0)
+    sus = _peaks().get("bf16_tflops_sustained", 1400.0)
+    bf = torch.bfloat16
+    g = torch.Generator(device=dev).manual_seed(7)
+    rows = []
+    for name, m, k, n in GATE_SHAPES:
+        flops = 2.0 * m * k * n
+        nbytes = 2 * (m * k + k * n + m * n)
+        copies = [(torch.randn((m, k), generator=g, device=dev, dtype=bf),
+                   torch.randn((n, k), generator=g, device=dev, dtype=bf) / math.sqrt(k),
+                   torch.empty((m, n), device=dev, dtype=bf)) for _ in range(_copies_for(nbytes))]
+        ours = [lambda c=c: kernels.gemm(c[0], c[1], out=c[2]) for c in copies]
+        ref = [lambda c=c: torch.matmul(c[0], c[1].t(), out=c[2]) for c in copies]
+        ms_ours, ms_ref = _time_chain(ours, max(steps, 10), dev), _time_chain(ref, max(steps, 10), dev)
+        x, w, o = copies[0]
+        got = kernels.gemm(x, w)
+        want = torch.matmul(x, w.t())
+        rel = float((got.float() - want.float()).norm() / want.float().norm())
+        rows.append({"shape": name, "m": m, "k": k, "n": n, "ms": round(ms_ours, 5), "ms_cublas": round(ms_ref, 5),
+                     "tflops": round(flops / ms_ours / 1e9, 1), "tflops_cublas": round(flops / ms_ref / 1e9, 1),
+                     "ratio_vs_cublas": round(ms_ref / ms_ours, 3), "rel_fro_vs_cublas": rel,
+                     "copies": len(copies)})
+        del copies, ours, ref, got, want
+        torch.cuda.empty_cache()
+    geo = math.exp(sum(math.log(r["ratio_vs_cublas"]) for r in rows) / len(rows))
+    return {"workload": "GEMM gate: plain bf16 GEMM vs cuBLAS on the reference's gate shapes (no LoRA)",
+            "path": "kernels.gemm (lora_gemm_ex, rank 0) vs torch.matmul (cuBLAS)", "bound": "tensor",
+            "unit": "TFLOP/s", "value": round(sum(r["tflops"] for r in rows) / len(rows), 1),
+            "ms": round(sum(r["ms"] for r in rows), 5), "peak": sus,
+            "frac": round(sum(r["tflops"] for r in rows) / len(rows) / sus, 4),
+            "geomean_speedup_vs_cublas": round(geo, 3), "cases": rows, "timing": CHAIN_NOTE.split(";")[0]}
+
+
 def measure_configs(steps=10):
     """C1-C4 against their own rooflines (each entry carries its parity)."""
     out = {}
@@ -797,17 +846,18 @@ def run_config(args):
     _lib.load()
     torch.cuda.set_device(0)
     res = {"c1": lambda: _config_c1_c2("c1", args.steps), "c2": lambda: _config_c1_c2("c2", args.steps),
-           "c3": lambda: _config_c3(args.steps), "c4": lambda: _config_c4(args.steps)}[args.workload]()
-    if "cases" in res:
+           "c3": lambda: _config_c3(args.steps), "c4": lambda: _config_c4(args.steps),
+           "gate": lambda: _config_gate(args.steps)}[args.workload]()
+    if "cases" in res and args.workload != "gate":
         main = res["cases"][-1]
         value, ms, frac = main["gbs"], main["ms"], main["hbm_frac"]
         tokens = main["m"]
     else:
         value, ms = res["value"], res["ms"]
         frac = res.get("hbm_frac", res.get("frac"))
-        tokens = 4096 if args.workload == "c3" else 8192
+        tokens = {"c3": 4096, "c4": 8192}.get(args.workload, 0)
     line = {"metric": METRIC, "value": value, "unit": res["unit"], "n_gpus": 1, "steps": args.steps, "warmup": 3,
-            "ms_per_step": ms, "tokens_per_s": round(tokens / ms * 1e3, 1), "higher_is_better": True,
+            "ms_per_step": ms, "tokens_per_s": round(tokens / ms * 1e3, 1) if tokens else None, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic (seeded Gaussian; no public dataset)",
             "config": {k: v for k, v in res.items() if k not in ("value", "unit")},
