@@ -713,7 +713,19 @@ def _config_c3(steps):
     out = fns[0]()
     rep = checks.branch_report(out, x, y, tabs[0], tabs[1], c.offsets, c.ranks, c.token_ids())
     gbs = nbytes / ms / 1e6
-    del fns, copies
+    # The same batch with its base linear: base GEMM then the branch, against the
+    # fused kernel (base and adapters in one GEMM).
+    unfused = [lambda x=x, tabs=tabs: segmented_branch.segmented_branch_varlen(x, kernels.gemm(x, w), *tabs, c.r_max)
+               for x, _, tabs in copies]
+    fused = [lambda x=x, tabs=tabs: segmented_branch.segmented_linear_varlen(x, w, None, *tabs, c.r_max)
+             for x, _, tabs in copies]
+    ms_unfused = _time_chain(unfused, max(steps, 10), dev)
+    ms_fused = _time_chain(fused, max(steps, 10), dev)
+    got = fused[0]()
+    rep_f = checks.seg_linear_report(got, x, w, None, tabs[0], tabs[1], c.offsets, c.ranks, c.token_ids())
+    flops_f = flops + 2.0 * c.x.shape[0] * c.x.shape[1] * c.w.shape[0]
+    sus = peaks.get("bf16_tflops_sustained", 1400.0)
+    del fns, copies, unfused, fused
     torch.cuda.empty_cache()
     return {"workload": "C3 segmented multi-LoRA branch: 4096 tokens, 128 Zipf(1.1) segments, 64 adapters "
                         "r in {4..64}, K=N=4096",
@@ -721,6 +733,13 @@ def _config_c3(steps):
             "value": round(gbs, 1), "ms": round(ms, 5), "ms_single": round(ms1, 5), "bytes": nbytes,
             "tflops": round(flops / ms / 1e9, 3), "peak": hbm, "hbm_frac": round(gbs / hbm, 4),
             "parity": {k: rep[k] for k in ("rows_checked", "max_abs_excess", "rel_fro", "ok")},
+            "with_base": {"what": "C3 batch with its base linear y = x W^T (W 4096x4096): base GEMM + branch "
+                                  "vs segmented_linear_varlen (one GEMM, adapters as per-tile K tail)",
+                          "ms_unfused": round(ms_unfused, 5), "ms_fused": round(ms_fused, 5),
+                          "speedup": round(ms_unfused / ms_fused, 3),
+                          "tflops_fused": round(flops_f / ms_fused / 1e9, 1),
+                          "frac_of_sustained": round(flops_f / ms_fused / 1e9 / sus, 4),
+                          "parity": {k: rep_f[k] for k in ("rows_checked", "max_abs_excess", "rel_fro", "ok")}},
             "timing": CHAIN_NOTE}
 
 

@@ -301,9 +301,10 @@ LORA_API int lora_sgmv_expand(const void* y, int64_t ldy, const void* z, int64_t
  * 16-bit hi/lo z, the expand over (tile, 256-column chunk) units with B and y
  * read by TMA.  y may be NULL (out = the LoRA term).  Workspace:
  * lora_sgmv_branch_workspace_size(T, S, K, r_max) bytes of scratch (no
- * zeroing needed; one buffer per stream).  Serves r_max <= 64, K, N and the
- * leading dimensions multiples of 8, 16-byte aligned rows; returns
- * LORA_ERR_UNSUPPORTED otherwise (use lora_sgmv_shrink_ex + lora_sgmv_expand).
+ * zeroing needed; one buffer per stream).  Serves r_max <= 64, K and N
+ * multiples of 64, leading dimensions multiples of 8, 16-byte aligned rows;
+ * returns LORA_ERR_UNSUPPORTED otherwise (use lora_sgmv_shrink_ex +
+ * lora_sgmv_expand).
  * Replaces the shrink / expand pair of ragged_branch.branch
  * (ragged_branch.py:6-40) and segmented_branch (segmented_branch.py:12-60). */
 LORA_API size_t lora_sgmv_branch_workspace_size(int64_t T, int64_t S, int64_t K, int64_t r_max);
@@ -312,6 +313,32 @@ LORA_API int lora_sgmv_branch(const void* x, int64_t ldx, const void* y, int64_t
                      const int64_t* offsets, const int64_t* ranks, int64_t n_adapters, const int32_t* tiles,
                      void* out, int64_t ldo, int64_t T, int64_t S, int64_t K, int64_t N, int64_t r_max,
                      float scale, int dtype, void* workspace, size_t workspace_bytes, void* stream);
+
+/* Base linear and segmented branch in one GEMM:
+ *   out[t, :] = x[t] . W^T + bias + (scale * x[t] . A_a^T) . B_a
+ * W [N, K] (ldw), bias [N] or NULL, tables and tiles as lora_sgmv_branch.
+ * The CTA-pair GEMM of lora_gemm takes, after each 256-token output tile's
+ * base K blocks, one more k-block per adapter piece of the tile (the tokens
+ * of one segment inside it): a block-diagonal slot of the tile's z (hi/lo
+ * bf16 pair) against the adapter's B rows, read by TMA from b_flat.  The base
+ * output is written once, with the adapters in it; no y is read or written.
+ * Launches: the tile's pieces (one CTA), the unit shrink, the slot fill, the
+ * GEMM.  Workspace: lora_sgmv_linear_workspace_size(T, S, K, r_max) bytes
+ * (256-byte aligned, no zeroing; one buffer per stream).  S: the segment
+ * count the tiles were scheduled from (0 for per-token ids).  Serves
+ * r_max <= 64, K and N multiples of 64, leading dimensions multiples of 8,
+ * 16-byte aligned rows; LORA_ERR_UNSUPPORTED otherwise (use lora_gemm +
+ * lora_sgmv_branch).  No reference counterpart: it fuses the base
+ * F.linear with ragged_branch.branch (ragged_branch.py:6-40) /
+ * segmented_branch (segmented_branch.py:12-60), the fused base + multi-adapter
+ * kernel the reference's serving notes ask for. */
+LORA_API size_t lora_sgmv_linear_workspace_size(int64_t T, int64_t S, int64_t K, int64_t r_max);
+LORA_API int lora_sgmv_linear(const void* x, int64_t ldx, const void* w, int64_t ldw, const void* bias,
+                     const void* a_flat, int64_t lda, int64_t a_rows, const void* b_flat, int64_t ldb,
+                     int64_t b_rows, const int64_t* offsets, const int64_t* ranks, int64_t n_adapters,
+                     const int32_t* tiles, void* out, int64_t ldo, int64_t T, int64_t S, int64_t K, int64_t N,
+                     int64_t r_max, float scale, int dtype, void* workspace, size_t workspace_bytes,
+                     void* stream);
 
 #ifdef __cplusplus
 }

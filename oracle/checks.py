@@ -138,3 +138,33 @@ def branch_report(out: torch.Tensor, x: torch.Tensor, y: torch.Tensor, a_flat, b
     raw, fro = orc.parity(got, want)
     return {"rows_checked": len(rows), "max_abs_excess": excess, "max_abs_raw": raw, "rel_fro": fro,
             "ok": bool(excess <= 2e-2 and fro <= 5e-3 and np.isfinite(got).all())}
+
+
+def seg_linear_report(out: torch.Tensor, x: torch.Tensor, w: torch.Tensor, bias, a_flat, b_flat, offsets, ranks,
+                      ids, dtype: str = "bf16", n_random: int = 48, seed: int = 0) -> dict:
+    """Parity of a fused base + multi-adapter linear against ``ragged_branch``
+    applied to the exact base ``x W^T + bias`` (float64), on the tokens
+    ``branch_report`` samples (segment edges and random ones)."""
+    t = out.shape[0]
+    ids_np = ids.detach().cpu().numpy().astype(np.int64) if isinstance(ids, torch.Tensor) else np.asarray(ids)
+    edges = np.flatnonzero(np.diff(ids_np)) if t > 1 else np.zeros(0, dtype=np.int64)
+    rng = np.random.default_rng(seed)
+    picks = set(int(v) for v in rng.choice(edges, size=min(len(edges), n_random), replace=False)) if len(edges) else set()
+    rows = {0, t - 1}
+    for e in picks:
+        rows.update((e, e + 1))
+    for edge in (255, 256, t - 256, t - 257):
+        rows.add(edge)
+    rows.update(int(r) for r in rng.integers(0, t, size=min(n_random, t)))
+    rows = sorted(r for r in rows if 0 <= r < t)
+    idx = torch.as_tensor(rows, device=out.device)
+    xs = np64(x.index_select(0, idx))
+    base = xs @ np64(w).T + (0.0 if bias is None else np64(bias))
+    offs = offsets.detach().cpu().numpy() if isinstance(offsets, torch.Tensor) else np.asarray(offsets)
+    rks = ranks.detach().cpu().numpy() if isinstance(ranks, torch.Tensor) else np.asarray(ranks)
+    want = orc.ragged_branch(xs, base, np64(a_flat), np64(b_flat), offs, rks, ids_np[rows])
+    got = np64(out.index_select(0, idx))
+    excess = orc.excess_abs_error(got, want, dtype)
+    raw, fro = orc.parity(got, want)
+    return {"rows_checked": len(rows), "max_abs_excess": excess, "max_abs_raw": raw, "rel_fro": fro,
+            "ok": bool(excess <= 2e-2 and fro <= 5e-3 and np.isfinite(got).all())}

@@ -21,7 +21,7 @@ INCLUDE = REPO_DIR / "include"
 BUILD_DIR = PKG_DIR / "_build"
 LIB_PATH = PKG_DIR / "liblora_b200.so"
 
-SOURCES = ("runtime.cu", "gemm_tc.cu", "shrink.cu", "expand.cu", "decode.cu", "sgmv.cu", "sgmv_block.cu", "sgmv_tc.cu", "sgmv_unit.cu", "skinny_tc.cu", "gemm_split.cu")
+SOURCES = ("runtime.cu", "gemm_tc.cu", "shrink.cu", "expand.cu", "decode.cu", "sgmv.cu", "sgmv_block.cu", "sgmv_tc.cu", "sgmv_unit.cu", "sgmv_linear.cu", "skinny_tc.cu", "gemm_split.cu")
 ARCH_FLAGS = ("-gencode", "arch=compute_100a,code=sm_100a")
 NVCC_FLAGS = ("-std=c++17", "-O3", "-lineinfo", "-Xcompiler", "-fPIC", "-Xcompiler", "-fvisibility=hidden")
 

@@ -80,6 +80,9 @@ SIGNATURES = {
     "lora_sgmv_branch_workspace_size": (_SZ, [_I64, _I64, _I64, _I64]),
     "lora_sgmv_branch": (_I, [_P, _I64, _P, _I64, _P, _I64, _I64, _P, _I64, _I64, _P, _P, _I64, _P, _P, _I64, _I64,
                               _I64, _I64, _I64, _I64, _F, _I, _P, _SZ, _P]),
+    "lora_sgmv_linear_workspace_size": (_SZ, [_I64, _I64, _I64, _I64]),
+    "lora_sgmv_linear": (_I, [_P, _I64, _P, _I64, _P, _P, _I64, _I64, _P, _I64, _I64, _P, _P, _I64, _P, _P, _I64, _I64,
+                              _I64, _I64, _I64, _I64, _F, _I, _P, _SZ, _P]),
 }
 
 

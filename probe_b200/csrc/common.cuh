@@ -388,6 +388,15 @@ LORA_DEVINL void tma_load_2d_pair(const CUtensorMap* map, void* smem_dst, uint32
       "l"(reinterpret_cast<uint64_t>(map)), "r"(bar_cluster_addr), "r"(c0), "r"(c1)
       : "memory");
 }
+// 3-D form of tma_load_2d_pair (transaction bytes counted on the leader's barrier).
+LORA_DEVINL void tma_load_3d_pair(const CUtensorMap* map, void* smem_dst, uint32_t bar_cluster_addr, int32_t c0,
+                                  int32_t c1, int32_t c2) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes "
+      "[%0], [%1, {%3, %4, %5}], [%2];" ::"r"(smem_u32(smem_dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar_cluster_addr), "r"(c0), "r"(c1), "r"(c2)
+      : "memory");
+}
 // L2 eviction-priority policies (createpolicy) for cache-hinted loads/stores.
 LORA_DEVINL uint64_t l2_policy_evict_last() {
   uint64_t p;

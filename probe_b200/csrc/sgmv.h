@@ -102,4 +102,25 @@ int launch_sgmv_branch_unit(const void* x, int64_t ldx, const void* y, int64_t l
                             int64_t T, int64_t K, int64_t N, int64_t r_max, float scale, int dtype, void* workspace,
                             size_t workspace_bytes, int num_sms, int* err, void* stream);
 
+// The shrink alone: fp32 partials [S][T][rpad16(r_max)] over S K slices
+// (sgmv_unit_slices), zeros beyond each token's rank; for callers that reduce
+// them themselves.
+int sgmv_unit_slices(int64_t T, int64_t K, int num_sms);
+int launch_sgmv_shrink_partials(const void* x, int64_t ldx, const void* a_flat, int64_t lda, int64_t a_rows,
+                                const int64_t* offsets, const int64_t* ranks, const int32_t* tiles, int64_t max_tiles,
+                                float* partial, int64_t T, int64_t K, int64_t r_max, int S, int dtype, int num_sms,
+                                int* err, void* stream);
+
+// Segmented LoRA linear in one CTA-pair GEMM (sgmv_linear.cu):
+// out = x . W^T + bias + (branch), the adapters as a per-tile K tail.
+// r_max <= 64, K and N multiples of 64, 16-byte aligned rows;
+// LORA_ERR_UNSUPPORTED otherwise.  S = segment count the schedule was built
+// from (0 for per-token ids): it bounds the schedule's tiles.
+size_t sgmv_linear_workspace(int64_t T, int64_t S, int64_t K, int64_t r_max, int num_sms);
+int launch_sgmv_linear(const void* x, int64_t ldx, const void* w, int64_t ldw, const void* bias, const void* a_flat,
+                       int64_t lda, int64_t a_rows, const void* b_flat, int64_t ldb, int64_t b_rows,
+                       const int64_t* offsets, const int64_t* ranks, const int32_t* tiles, int64_t S, void* out,
+                       int64_t ldo, int64_t T, int64_t K, int64_t N, int64_t r_max, float scale, int dtype,
+                       void* workspace, size_t workspace_bytes, int num_sms, int* err, void* stream);
+
 }  // namespace lora

@@ -919,4 +919,15 @@ int launch_sgmv_branch_unit(const void* x, int64_t ldx, const void* y, int64_t l
                              r_max, dtype, num_sms, err, stream);
 }
 
+int sgmv_unit_slices(int64_t T, int64_t K, int num_sms) { return unit_slices(T, K, num_sms); }
+
+int launch_sgmv_shrink_partials(const void* x, int64_t ldx, const void* a_flat, int64_t lda, int64_t a_rows,
+                                const int64_t* offsets, const int64_t* ranks, const int32_t* tiles, int64_t max_tiles,
+                                float* partial, int64_t T, int64_t K, int64_t r_max, int S, int dtype, int num_sms,
+                                int* err, void* stream) {
+  if (!shrink_units_ok(x, ldx, a_flat, lda, a_rows, T, K, r_max, max_tiles)) return LORA_ERR_UNSUPPORTED;
+  return launch_shrink_units(x, ldx, a_flat, lda, a_rows, offsets, ranks, tiles, max_tiles, partial, T, K, r_max, S,
+                             dtype, num_sms, err, stream);
+}
+
 }  // namespace lora

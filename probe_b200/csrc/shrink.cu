@@ -700,3 +700,34 @@ extern "C" int lora_sgmv_branch(const void* x, int64_t ldx, const void* y, int64
                                  sgmv_max_tiles(T, S), out, ldo, T, K, N, r_max, scale, dtype, workspace,
                                  workspace_bytes, info.num_sms, info.err_word, stream);
 }
+
+extern "C" size_t lora_sgmv_linear_workspace_size(int64_t T, int64_t S, int64_t K, int64_t r_max) {
+  if (T <= 0 || K <= 0 || r_max <= 0) return 256;
+  const int dev = current_device();
+  const int sms = dev >= 0 ? device_info(dev).num_sms : 148;
+  return sgmv_linear_workspace(T, S, K, r_max, sms > 0 ? sms : 148);
+}
+
+extern "C" int lora_sgmv_linear(const void* x, int64_t ldx, const void* w, int64_t ldw, const void* bias,
+                                const void* a_flat, int64_t lda, int64_t a_rows, const void* b_flat, int64_t ldb,
+                                int64_t b_rows, const int64_t* offsets, const int64_t* ranks, int64_t n_adapters,
+                                const int32_t* tiles, void* out, int64_t ldo, int64_t T, int64_t S, int64_t K,
+                                int64_t N, int64_t r_max, float scale, int dtype, void* workspace,
+                                size_t workspace_bytes, void* stream) {
+  if (x == nullptr || w == nullptr || a_flat == nullptr || b_flat == nullptr || offsets == nullptr ||
+      ranks == nullptr || tiles == nullptr || out == nullptr)
+    return LORA_ERR_ARG;
+  if (dtype != LORA_BF16 && dtype != LORA_F16) return LORA_ERR_DTYPE;
+  if (T < 0 || S < 0 || K < 0 || N < 0 || r_max < 0 || n_adapters < 0 || a_rows < 0 || b_rows < 0)
+    return LORA_ERR_SHAPE;
+  if (ldx < K || ldw < K || lda < K || ldb < N || ldo < N) return LORA_ERR_SHAPE;
+  if (out == x || out == w) return LORA_ERR_ARG;
+  if (T == 0 || N == 0) return LORA_OK;
+  if (r_max == 0 || K == 0) return LORA_ERR_UNSUPPORTED;
+  const int dev = current_device();
+  if (dev < 0 || !device_info(dev).is_sm100) return LORA_ERR_DEVICE;
+  const DeviceInfo& info = device_info(dev);
+  return launch_sgmv_linear(x, ldx, w, ldw, bias, a_flat, lda, a_rows, b_flat, ldb, b_rows, offsets, ranks, tiles, S,
+                            out, ldo, T, K, N, r_max, scale, dtype, workspace, workspace_bytes, info.num_sms,
+                            info.err_word, stream);
+}

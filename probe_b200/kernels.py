@@ -345,3 +345,45 @@ def sgmv_branch(x: torch.Tensor, y: torch.Tensor | None, a_flat: torch.Tensor, b
         return None
     _lib.check(rc, "lora_sgmv_branch")
     return out
+
+
+def sgmv_linear(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None, a_flat: torch.Tensor,
+                b_flat: torch.Tensor, offsets: torch.Tensor, ranks: torch.Tensor, tiles: torch.Tensor, s: int,
+                r_max: int, scale: float = 1.0, out: torch.Tensor | None = None) -> torch.Tensor | None:
+    """``out = x @ weight.T + bias + (scale * x @ A_a.T) @ B_a`` per tile in ONE GEMM: the
+    adapters ride as a per-256-token-tile K tail of the base GEMM (lora_sgmv_linear).
+    Returns None when the shape is outside that path (r_max > 64, K or N not a
+    multiple of 64, unaligned rows): then use gemm + sgmv_branch."""
+    _lib.require_cuda(x, weight, a_flat, b_flat, bias, where="sgmv_linear")
+    _check_half(x, "sgmv_linear")
+    if weight.dtype != x.dtype or a_flat.dtype != x.dtype or b_flat.dtype != x.dtype or (
+            bias is not None and bias.dtype != x.dtype):
+        raise TypeError("sgmv_linear: x, weight, bias and the adapter tables must share one dtype")
+    x = _lib.row_major(x)
+    weight = _lib.row_major(weight)
+    a_flat = _lib.row_major(a_flat)
+    b_flat = _lib.row_major(b_flat)
+    t, k = x.shape
+    n = weight.shape[0]
+    if weight.shape[1] != k or a_flat.shape[1] != k or b_flat.shape[1] != n:
+        raise ValueError("sgmv_linear: x, weight, a_flat and b_flat disagree on K / N")
+    if bias is not None:
+        bias = bias.contiguous()
+        if bias.shape != (n,):
+            raise ValueError("sgmv_linear: bias must have out_features elements")
+    if out is None:
+        out = torch.empty((t, n), device=x.device, dtype=x.dtype)
+    lib = _lib.load()
+    ws_bytes = lib.lora_sgmv_linear_workspace_size(t, s, k, int(r_max))
+    ws = _lib.WORKSPACE.get(ws_bytes, x.device, "sgmv_linear")
+    offsets = _i64(offsets, x.device)
+    ranks = _i64(ranks, x.device)
+    rc = lib.lora_sgmv_linear(_lib.ptr(x), _lib.ld(x), _lib.ptr(weight), _lib.ld(weight), _lib.ptr(bias),
+                              _lib.ptr(a_flat), _lib.ld(a_flat), a_flat.shape[0], _lib.ptr(b_flat), _lib.ld(b_flat),
+                              b_flat.shape[0], _lib.ptr(offsets), _lib.ptr(ranks), offsets.numel(), _lib.ptr(tiles),
+                              _lib.ptr(out), out.stride(0), t, s, k, n, int(r_max), float(scale), _dt(x),
+                              _lib.ptr(ws), ws.numel(), _lib.stream_handle(x.device))
+    if rc == _lib.LORA_ERR_UNSUPPORTED:
+        return None
+    _lib.check(rc, "lora_sgmv_linear")
+    return out
