@@ -158,9 +158,8 @@ LORA_API int lora_shrink(const void* x, int64_t ldx, const void* a, int64_t lda,
  * split_k == 0 picks the widest split that fits (down to 1, which needs no
  * scratch); an explicit split_k that does not fit returns LORA_ERR_WORKSPACE.
  * The first call on a device that splits K looks up the array's device
- * address (cudaGetSymbolAddress) and caches it; make that first call before
- * any stream capture.  A failed lookup returns LORA_ERR_CUDA and is retried
- * by the next call.  Device ordinals above 63 return LORA_ERR_DEVICE.
+ * address (cudaGetSymbolAddress) and caches it.  A failed lookup returns
+ * LORA_ERR_CUDA and is retried by the next call.  Device ordinals above 63 return LORA_ERR_DEVICE.
  * All calls share the one array: calls that overlap on the GPU (several
  * streams or threads) race and must be serialised on one stream.
  * No counterpart in the reference (its wrappers allocate per call). */

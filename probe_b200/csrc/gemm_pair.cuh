@@ -12,6 +12,11 @@ namespace lora {
 constexpr int kGemmBM = 128;
 constexpr int kGemmBK = 64;
 constexpr int kGemmThreads = 192;
+// CTA-pair GEMM: producer warp, MMA warp, then the epilogue warps (a multiple
+// of 4: each TMEM lane quadrant drained by kPairEpiWarps / 4 warps splitting the
+// columns).  Eight measured no faster than four on B200 (the epilogue is
+// already hidden behind the next tile's mainloop), so four it is.
+constexpr int kPairEpiWarps = 4;
 
 struct GemmArgs {
   void* out;

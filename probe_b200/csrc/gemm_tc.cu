@@ -276,8 +276,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 // ingest per SM, not the tensor pipe, bounds the NW = 1 form on B200).  Both
 // accumulator halves belong to the one tile; the epilogue frees them one at a
 // time and the next tile's first MMAs into each half wait only for that half.
-template <int STAGES, int NW, typename T>
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
+template <int STAGES, int NW, int EW, typename T>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(64 + 32 * EW, 1)
     gemm_tc2_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_w,
                     const __grid_constant__ CUtensorMap tm_z, const __grid_constant__ CUtensorMap tm_b,
                     const GemmArgs args) {
@@ -314,7 +314,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&acc_full[a], 1);
-      mbar_init(&acc_empty[a], 8);  // 4 epilogue warps in each CTA of the pair
+      mbar_init(&acc_empty[a], 2 * EW);  // every epilogue warp of both CTAs of the pair
     }
     *abort_flag = 0;
     fence_mbar_init();
@@ -437,8 +437,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
   } else {
     // ------------------------------------------------ epilogue (both CTAs)
     // NW = 2: acc_full[0] per tile; the halves are released through
-    // acc_empty[0] and acc_empty[1] as they are drained.
+    // acc_empty[0] and acc_empty[1] as they are drained.  Warps 2 .. EW + 1:
+    // lane quadrant warp % 4, columns [kCW * cpart, +kCW) of every 256-column half.
+    constexpr int kCW = 256 / (EW / 4);
     const int quad = warp & 3;
+    const int cpart = (warp - 2) >> 2;
     const T* bias = static_cast<const T*>(args.bias);
     const bool vec_ok = (args.ldo % 8) == 0 && (reinterpret_cast<uintptr_t>(args.out) % 16) == 0;
     const uint64_t st_policy = l2_policy_evict_first();
@@ -464,7 +467,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
         const uint32_t t_row =
             tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + static_cast<uint32_t>(half * 256);
 #pragma unroll 1
-        for (int c = 0; c < 256; c += 16) {
+        for (int c = kCW * cpart; c < kCW * cpart + kCW; c += 16) {
           uint32_t r[16];
           tmem_ld_32x32b_x16(t_row + c, r);
           tmem_wait_ld();
@@ -486,19 +489,20 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
         // The last of the tile's split items to store its partial (per CTA
         // half: ticket (tile, rank)) sums the partials in slice order.
         __threadfence();
-        named_bar_sync(1, 128);
+        named_bar_sync(1, 32 * EW);
         if (threadIdx.x == 64) {
           int* ticket = args.tail_tickets + (tile - args.full_tiles) * 2 + static_cast<int>(rank);
           const int last = atomicAdd(ticket, 1) == args.split - 1;
           if (last) *ticket = 0;  // every slice has arrived: back to zero for the next call
           *last_flag = last;
         }
-        named_bar_sync(1, 128);
+        named_bar_sync(1, 32 * EW);
         if (*last_flag) {
           __threadfence();
           const int first_unit = (tile - args.full_tiles) * args.split;
 #pragma unroll 1
-          for (int c = 0; c < kTileN; c += 16) {
+          for (int cc = 0; cc < NW * kCW; cc += 16) {
+            const int c = (cc / kCW) * 256 + kCW * cpart + cc % kCW;  // this warp's columns of each half
             float v[16];
 #pragma unroll
             for (int e = 0; e < 16; ++e) v[e] = 0.f;
@@ -520,7 +524,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
             epilogue_store16<T>(args, out_row, bias, row, nt * kTileN + c, vec_ok, r, st_policy);
           }
         }
-        named_bar_sync(1, 128);  // last_flag is rewritten by the next split item
+        named_bar_sync(1, 32 * EW);  // last_flag is rewritten by the next split item
       }
     }
   }
@@ -659,11 +663,11 @@ PairSplit pair_split_plan(int64_t tiles, int pairs, int num_kb, int tile_n) {
   return sp;
 }
 
-// Resident CTA pairs of gemm_tc2_kernel<STAGES, NW> on this device (cached).
-template <int STAGES, int NW, typename T>
+// Resident CTA pairs of gemm_tc2_kernel<STAGES, NW, EW> on this device (cached).
+template <int STAGES, int NW, int EW, typename T>
 int pair_capacity(int dev, const DeviceInfo& info, cudaError_t* attr_status) {
   using L = PairSmem<STAGES, NW>;
-  auto kernel = gemm_tc2_kernel<STAGES, NW, T>;
+  auto kernel = gemm_tc2_kernel<STAGES, NW, EW, T>;
   static std::once_flag once[64];
   static cudaError_t attr_err[64];
   static int max_clusters[64];
@@ -673,7 +677,7 @@ int pair_capacity(int dev, const DeviceInfo& info, cudaError_t* attr_status) {
     if (attr_err[dev & 63] == cudaSuccess) {
       cudaLaunchConfig_t cfg = {};
       cfg.gridDim = dim3(2 * info.num_sms);
-      cfg.blockDim = dim3(kGemmThreads);
+      cfg.blockDim = dim3(64 + 32 * EW);
       cfg.dynamicSmemBytes = L::kBytes;
       if (cudaOccupancyMaxActiveClusters(&clusters, kernel, &cfg) != cudaSuccess) {
         cudaGetLastError();
@@ -686,7 +690,7 @@ int pair_capacity(int dev, const DeviceInfo& info, cudaError_t* attr_status) {
   return max_clusters[dev & 63];
 }
 
-template <int STAGES, int NW, typename T>
+template <int STAGES, int NW, int EW, typename T>
 int launch_gemm_pair(const void* x, int64_t ldx, const void* w, int64_t ldw, const void* z, int64_t ldz,
                      const void* bw, int64_t ldbw, const void* bias, void* out, int64_t ldo, int64_t M, int64_t N,
                      int64_t K, int64_t R, float alpha, int64_t lo_offset, int dtype, void* ws, size_t ws_bytes,
@@ -726,9 +730,9 @@ int launch_gemm_pair(const void* x, int64_t ldx, const void* w, int64_t ldw, con
   a.l2_hints = env_int("LORA_B200_L2_HINTS", 0);
   a.alpha = alpha;
 
-  auto kernel = gemm_tc2_kernel<STAGES, NW, T>;
+  auto kernel = gemm_tc2_kernel<STAGES, NW, EW, T>;
   cudaError_t attr_status = cudaSuccess;
-  const int capacity = pair_capacity<STAGES, NW, T>(dev, info, &attr_status);
+  const int capacity = pair_capacity<STAGES, NW, EW, T>(dev, info, &attr_status);
   if (attr_status != cudaSuccess) return LORA_ERR_CUDA;
   a.full_tiles = a.num_tiles;
   a.split = 1;
@@ -745,15 +749,16 @@ int launch_gemm_pair(const void* x, int64_t ldx, const void* w, int64_t ldw, con
   }
   const int64_t items = a.full_tiles + static_cast<int64_t>(a.num_tiles - a.full_tiles) * a.split;
   const int pairs = static_cast<int>(std::min<int64_t>(items, capacity));
-  kernel<<<2 * pairs, kGemmThreads, L::kBytes, stream>>>(tm_x, tm_w, tm_z, tm_b, a);
+  kernel<<<2 * pairs, 64 + 32 * EW, L::kBytes, stream>>>(tm_x, tm_w, tm_z, tm_b, a);
   return cudaGetLastError() == cudaSuccess ? LORA_OK : LORA_ERR_CUDA;
 }
 
-// 256 x 512 pair tiles (NW = 2) when they still give every SM pair enough
-// tiles: they need a third less operand ingest per product, the bound of the
-// 256 x 256 form, at the price of an epilogue that only half overlaps the next
+// 256 x 512 pair tiles (NW = 2): a third less operand ingest per product
+// than 256 x 256, at the price of an epilogue that only half overlaps the next
 // tile.  Chosen when their waves of pairs, weighted by the tile's doubled work
-// and the ~10% faster products, cost less than the 256 x 256 waves.
+// and the ~10% faster products, cost less than the 256 x 256 waves (4096^3:
+// 2 waves of wide tiles against 4 of narrow ones, 20 % faster; 4095 x 5120^2:
+// 3 against 5, narrow 45 % faster).
 // LORA_B200_GEMM_WIDE=0 / 1 forces the choice (tuning sweeps).
 // Waves of pair tiles, counting a split tail as the fraction of a wave each
 // of its pieces takes (plus a little for the partials' round trip).
@@ -777,11 +782,9 @@ int pair_tile_width(int64_t M, int64_t N, int64_t K, int64_t R, int pairs, bool 
   const int64_t mt = (M + 255) / 256;
   const int num_kb = static_cast<int>((K + kGemmBK - 1) / kGemmBK + (R + kGemmBK - 1) / kGemmBK);
   const int64_t tiles2 = mt * ((N + 511) / 512);
-  // With few 256 x 512 tiles per pair their unhidden epilogue and pipeline
-  // fill cost more than the wider tile saves (measured at 4095 and 8190 rows,
-  // K = 5120): keep them for at least five waves, or four with long K.
-  if (tiles2 < 5 * static_cast<int64_t>(pairs) && !(tiles2 >= 4 * static_cast<int64_t>(pairs) && num_kb >= 128))
-    return 1;
+  // Short K: a 256 x 512 tile's epilogue is no longer hidden behind the next
+  // tile's mainloop (measured at K = 1536: 256 x 256 tiles 25 % faster).
+  if (num_kb < 48) return 1;
   const double w1 = pair_waves(mt * ((N + 255) / 256), pairs, num_kb, can_split);
   const double w2 = pair_waves(tiles2, pairs, num_kb, can_split);
   return 1.8 * w2 < w1 ? 2 : 1;
@@ -851,18 +854,15 @@ int gemm_impl(const void* x, int64_t ldx, const void* w, int64_t ldw, const void
   const int bn = gemm_pick_bn(M, N, info.num_sms);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   if (use_pair_tiles(M, N, K, R, info.num_sms, ws != nullptr)) {
-    if (pair_tile_width(M, N, K, R, info.num_sms / 2, ws != nullptr) == 2) {
-      if (dtype == LORA_BF16)
-        return launch_gemm_pair<4, 2, __nv_bfloat16>(x, ldx, w, ldw, z, ldz, bw, ldbw, bias, out, ldo, M, N, K, R,
-                                                     alpha, lo_offset, dtype, ws, ws_bytes, s);
-      return launch_gemm_pair<4, 2, __half>(x, ldx, w, ldw, z, ldz, bw, ldbw, bias, out, ldo, M, N, K, R, alpha,
-                                            lo_offset, dtype, ws, ws_bytes, s);
-    }
-    if (dtype == LORA_BF16)
-      return launch_gemm_pair<6, 1, __nv_bfloat16>(x, ldx, w, ldw, z, ldz, bw, ldbw, bias, out, ldo, M, N, K, R,
-                                                   alpha, lo_offset, dtype, ws, ws_bytes, s);
-    return launch_gemm_pair<6, 1, __half>(x, ldx, w, ldw, z, ldz, bw, ldbw, bias, out, ldo, M, N, K, R, alpha,
-                                          lo_offset, dtype, ws, ws_bytes, s);
+    const int nw = pair_tile_width(M, N, K, R, info.num_sms / 2, ws != nullptr);
+#define LORA_PAIR(ST, NWV)                                                                                        \
+  (dtype == LORA_BF16                                                                                              \
+       ? launch_gemm_pair<ST, NWV, kPairEpiWarps, __nv_bfloat16>(x, ldx, w, ldw, z, ldz, bw, ldbw, bias, out, ldo, M, \
+                                                                 N, K, R, alpha, lo_offset, dtype, ws, ws_bytes, s)   \
+       : launch_gemm_pair<ST, NWV, kPairEpiWarps, __half>(x, ldx, w, ldw, z, ldz, bw, ldbw, bias, out, ldo, M, N, K, \
+                                                          R, alpha, lo_offset, dtype, ws, ws_bytes, s))
+    return nw == 2 ? LORA_PAIR(4, 2) : LORA_PAIR(6, 1);
+#undef LORA_PAIR
   }
   if (dtype == LORA_BF16)
     return dispatch_gemm<__nv_bfloat16>(bn, x, ldx, w, ldw, z, ldz, bw, ldbw, bias, out, ldo, M, N, K, R, alpha,
@@ -890,8 +890,8 @@ extern "C" size_t lora_gemm_workspace_size(int64_t M, int64_t N, int64_t K, int6
   if (!info.is_sm100 || !use_pair_tiles(M, N, K, R, info.num_sms, true)) return 0;
   const int nw = pair_tile_width(M, N, K, R, info.num_sms / 2, true);
   cudaError_t st = cudaSuccess;
-  const int capacity = nw == 2 ? pair_capacity<4, 2, __nv_bfloat16>(dev, info, &st)
-                               : pair_capacity<6, 1, __nv_bfloat16>(dev, info, &st);
+  const int capacity = nw == 2 ? pair_capacity<4, 2, kPairEpiWarps, __nv_bfloat16>(dev, info, &st)
+                               : pair_capacity<6, 1, kPairEpiWarps, __nv_bfloat16>(dev, info, &st);
   if (st != cudaSuccess) return 0;
   const int64_t tiles = ((M + 255) / 256) * ((N + 256 * nw - 1) / (256 * nw));
   const int num_kb = static_cast<int>((K + kGemmBK - 1) / kGemmBK + (R + kGemmBK - 1) / kGemmBK);
