@@ -126,6 +126,10 @@ LORA_DEVINL void epilogue_store16(const GemmArgs& args, T* out_row, const T* bia
   }
 }
 
+// Tile width (1: 256 x 256, 2: 256 x 512) the CTA-pair GEMM picks for an
+// M x N x K product without a split tail (gemm_tc.cu).
+int gemm_pair_width(int64_t M, int64_t N, int64_t K, int num_sms);
+
 // 2-D tiled TMA map (128-byte swizzle) over a row-major [outer, inner] matrix.
 inline bool encode_tile_map(CUtensorMap* map, const void* ptr, int dtype, uint64_t inner, uint64_t outer,
                      uint64_t ld_elems, uint32_t box_inner, uint32_t box_outer) {

@@ -814,6 +814,10 @@ bool use_pair_tiles(int64_t M, int64_t N, int64_t K, int64_t R, int num_sms, boo
 
 }  // namespace
 
+int gemm_pair_width(int64_t M, int64_t N, int64_t K, int num_sms) {
+  return pair_tile_width(M, N, K, 0, num_sms / 2, false);
+}
+
 int gemm_pick_bn(int64_t M, int64_t N, int num_sms) {
   if (N <= 64) return 64;
   if (N <= 128) return 128;

@@ -20,13 +20,16 @@
 // z travels as a bf16 hi/lo pair (hi = round(v), lo = round(v - hi)): a piece
 // of rank <= 32 packs both into one 64-column slot (hi in columns 0..31, lo in
 // 32..63; two MMA chains over the same B stage), a piece of rank 33..64 takes
-// two slots.  Rank-0 pieces and tokens without a valid adapter add nothing.
+// two slots.  (Rounding z to bf16 alone, as the reference's ragged expand does
+// with z.to(b.dtype), ragged_branch.py:24-25, measured up to 0.13 max-abs
+// error at rank 64 -- beyond the 2e-2 bar.)  Rank-0 pieces and tokens without
+// a valid adapter add nothing.
 //
 // Launches (programmatic dependent launch between them):
 //   1. pieces  (one CTA): per 256-token tile, its pieces -> slot table
 //   2. shrink  (sgmv_unit.cu): fp32 partials of z over (tile, K slice) units
 //   3. z fill: sums the partials in slice order into the hi/lo slots (zeros
-//      outside each piece's rows)
+//      outside each piece's rows and beyond its rank)
 //   4. the pair GEMM below.
 #include <algorithm>
 #include <type_traits>
@@ -42,8 +45,7 @@ namespace {
 
 constexpr int kSlTile = 256;          // tokens per output tile (a CTA pair's M)
 constexpr int kSlSlotCols = 64;       // z columns per slot (one 128-byte swizzle row)
-constexpr int kSlStages = 6;
-constexpr int kSlThreads = 1024;      // pieces kernel
+constexpr int kSlStages = 6;       // 256 x 256 tiles (256 x 512: 4 stages)
 constexpr int kSlMaxRank = 64;
 
 // Slot record: {first token, end token, first B row, meta};
@@ -54,104 +56,161 @@ struct SlArgs {
 };
 
 // ------------------------------------------------------------------ pieces
-// Walks the schedule tiles of output tile mt (those of its four 64-token
-// blocks) and calls emit(t0, t1, b_row, k16, part) for every slot of its
-// pieces, in token order.  Returns the number of slots.
-template <typename Emit>
-__device__ int tile_slots(const int32_t* tiles, const int64_t* offsets, const int64_t* ranks, int mt, int T, int R,
-                          Emit&& emit) {
-  const int32_t* first = sgmv_block_first(tiles);
-  const int blocks = (T + kSgmvTileTokens - 1) / kSgmvTileTokens;
-  const int b0 = mt * (kSlTile / kSgmvTileTokens);
-  const int b1 = min(blocks, b0 + kSlTile / kSgmvTileTokens);
-  const int i0 = first[b0], i1 = first[b1];
-  int count = 0;
-  int cur = -1, cur_r = 0, t0 = 0, t1 = 0;
-  int64_t cur_row = 0;
-  auto flush = [&]() {
-    if (cur < 0 || cur_r <= 0) return;
-    const int k16 = (cur_r + 15) >> 4;
+// One warp per 256-token output tile (warps stride over the tiles).  Lanes
+// read 32 schedule tiles at a time in parallel; a piece starts at every
+// schedule tile whose adapter differs from the one before it inside the output
+// tile, and ends where the next piece starts (pieces cover the output tile,
+// those without an adapter or of rank 0 included; those emit no slot).  A
+// piece of rank <= 32 takes one slot, a larger one two.  Pass 1 counts each
+// output tile's slots into mt_first, a block-wide scan turns the counts into
+// first-slot offsets, pass 2 writes the slot records.  Every load of a pass is
+// independent of the others, so a pass costs a few memory latencies.
+constexpr int kSlPieceThreads = 256;
+constexpr int kSlPieceWarps = kSlPieceThreads / 32;
+
+struct PieceWalk {
+  const int32_t* tiles;
+  const int64_t* offsets;
+  const int64_t* ranks;
+  int T, R;
+
+  // Calls emit(k, t0, t1, b_row, k16, part) for the slots of output tile mt
+  // (k = slot index within the tile, in token order) from every lane that owns
+  // a slot; returns the tile's slot count (warp-uniform).
+  template <typename Emit>
+  __device__ int run(int mt, int lane, Emit&& emit) const {
+    const int32_t* first = sgmv_block_first(tiles);
+    const int blocks = (T + kSgmvTileTokens - 1) / kSgmvTileTokens;
+    const int b0 = mt * (kSlTile / kSgmvTileTokens);
+    const int b1 = min(blocks, b0 + kSlTile / kSgmvTileTokens);
+    const int i0 = first[b0], i1 = first[b1];
+    const int tile_end = min(T, (mt + 1) * kSlTile);
+    int carry_ad = -2;  // adapter of the last schedule tile of the previous chunk
+    int done = 0;       // slots emitted so far
+    // a piece that starts in this chunk may end in a later one: its start is
+    // kept until the next start (or the tile's end) is seen
+    int open_t0 = -1, open_ad = -1;
+    for (int c0 = i0; c0 < i1; c0 += 32) {
+      const int i = c0 + lane;
+      const bool valid = i < i1;
+      const int ad = valid ? sgmv_tile_adapter(tiles, i) : -3;
+      const int ts = valid ? sgmv_tile_start(tiles, i) : tile_end;
+      int prev = __shfl_up_sync(0xffffffffu, ad, 1);
+      if (lane == 0) prev = carry_ad;
+      const bool starts = valid && (i == i0 || ad != prev);
+      const uint32_t mask = __ballot_sync(0xffffffffu, starts);
+      // the open piece (from an earlier chunk) ends at this chunk's first start
+      if (open_t0 >= 0 && mask != 0u) {
+        const int t1 = __shfl_sync(0xffffffffu, ts, __ffs(mask) - 1);
+        done += emit_piece(done, open_t0, t1, open_ad, lane, emit);
+        open_t0 = -1;
+      }
+      // pieces starting in this chunk: each ends at the next start in the chunk,
+      // the last one stays open
+      const uint32_t later = starts ? (mask & ~((2u << lane) - 1u)) : 0u;  // starts after this lane
+      const int nxt = later ? __ffs(later) - 1 : -1;
+      const int t1_local = __shfl_sync(0xffffffffu, ts, nxt >= 0 ? nxt : 0);
+      // closed pieces of this chunk, in lane order
+      const bool closes = starts && nxt >= 0;
+      const int rr = (closes && ad >= 0) ? piece_rank(ad) : 0;
+      const int nslot = rr <= 0 ? 0 : (rr <= 32 ? 1 : 2);
+      int excl = nslot;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int v = __shfl_up_sync(0xffffffffu, excl, o);
+        if (lane >= o) excl += v;
+      }
+      const int total_c = __shfl_sync(0xffffffffu, excl, 31);
+      excl -= nslot;
+      if (nslot > 0) emit_slots(done + excl, ts, t1_local, static_cast<int>(offsets[ad]), rr, emit);
+      done += total_c;
+      if (mask != 0u) {
+        const int last = 31 - __clz(mask);
+        open_t0 = __shfl_sync(0xffffffffu, ts, last);
+        open_ad = __shfl_sync(0xffffffffu, ad, last);
+      }
+      carry_ad = __shfl_sync(0xffffffffu, ad, min(31, i1 - 1 - c0));
+    }
+    if (open_t0 >= 0) done += emit_piece(done, open_t0, tile_end, open_ad, lane, emit);
+    return done;
+  }
+
+  __device__ int piece_rank(int ad) const {
+    const int64_t rr = ranks[ad];
+    return rr <= 0 ? 0 : static_cast<int>(rr < R ? rr : R);
+  }
+
+  // The slots of one piece of rank rr > 0, from slot index k on.
+  template <typename Emit>
+  __device__ static void emit_slots(int k, int t0, int t1, int brow, int rr, Emit&& emit) {
+    const int k16 = (rr + 15) >> 4;
     if (k16 <= 2) {
-      emit(count, t0, t1, cur_row, k16, 0);
-      ++count;
+      emit(k, t0, t1, brow, k16, 0);
     } else {
-      emit(count, t0, t1, cur_row, k16, 1);
-      emit(count + 1, t0, t1, cur_row, k16, 2);
-      count += 2;
-    }
-  };
-  for (int i = i0; i < i1; ++i) {
-    const int ad = sgmv_tile_adapter(tiles, i);
-    const int ts = sgmv_tile_start(tiles, i);
-    const int te = min(sgmv_tile_start(tiles, i + 1), T);
-    if (ad == cur && ad >= 0 && ts == t1) {
-      t1 = te;
-      continue;
-    }
-    flush();
-    cur = ad;
-    t0 = ts;
-    t1 = te;
-    cur_r = 0;
-    cur_row = 0;
-    if (ad >= 0) {
-      const int64_t rr = ranks[ad];
-      cur_r = rr <= 0 ? 0 : static_cast<int>(rr < R ? rr : R);
-      cur_row = offsets[ad];
+      emit(k, t0, t1, brow, k16, 1);
+      emit(k + 1, t0, t1, brow, k16, 2);
     }
   }
-  flush();
-  return count;
-}
 
-__global__ void __launch_bounds__(kSlThreads) sgmv_linear_pieces_kernel(const int32_t* tiles, const int64_t* offsets,
-                                                                        const int64_t* ranks, int T, int R,
-                                                                        int m_tiles, int cap, int32_t* mt_first,
-                                                                        int4* slots, int* err) {
-  __shared__ int warp_sums[kSlThreads / 32];
+  // One piece known to the whole warp: lane 0 emits its slots; returns their count.
+  template <typename Emit>
+  __device__ int emit_piece(int k, int t0, int t1, int ad, int lane, Emit&& emit) const {
+    const int rr = ad >= 0 ? piece_rank(ad) : 0;
+    if (rr <= 0) return 0;
+    if (lane == 0) emit_slots(k, t0, t1, static_cast<int>(offsets[ad]), rr, emit);
+    return rr <= 32 ? 1 : 2;
+  }
+};
+
+__global__ void __launch_bounds__(kSlPieceThreads) sgmv_linear_pieces_kernel(const int32_t* tiles,
+                                                                             const int64_t* offsets,
+                                                                             const int64_t* ranks, int T, int R,
+                                                                             int m_tiles, int cap, int32_t* mt_first,
+                                                                             int4* slots, int* err) {
+  __shared__ int warp_sums[kSlPieceWarps];
+  __shared__ int carry;
   pdl_wait();  // the schedule launched before writes the tile table
   if (threadIdx.x == 0) pdl_launch_dependents();
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  const int per = (m_tiles + kSlThreads - 1) / kSlThreads;  // contiguous tiles per thread
-  const int mt0 = min(m_tiles, tid * per), mt1 = min(m_tiles, mt0 + per);
-  auto none = [](int, int, int, int64_t, int, int) {};
-  int mine = 0;
-  for (int mt = mt0; mt < mt1; ++mt) mine += tile_slots(tiles, offsets, ranks, mt, T, R, none);
-  // block-wide exclusive scan of the per-thread counts
-  int incl = mine;
-#pragma unroll
-  for (int o = 1; o < 32; o <<= 1) {
-    const int v = __shfl_up_sync(0xffffffffu, incl, o);
-    if (lane >= o) incl += v;
+  const PieceWalk walk{tiles, offsets, ranks, T, R};
+  // pass 1: slots per output tile
+  for (int mt = warp; mt < m_tiles; mt += kSlPieceWarps) {
+    const int n = walk.run(mt, lane, [](int, int, int, int, int, int) {});
+    if (lane == 0) mt_first[mt] = n;
   }
-  if (lane == 31) warp_sums[warp] = incl;
   __syncthreads();
-  if (warp == 0) {
-    int w = warp_sums[lane];
+  // exclusive scan of mt_first[0 .. m_tiles) in chunks of the block
+  if (tid == 0) carry = 0;
+  __syncthreads();
+  for (int c0 = 0; c0 < m_tiles; c0 += kSlPieceThreads) {
+    const int mt = c0 + tid;
+    const int v = mt < m_tiles ? mt_first[mt] : 0;
+    int incl = v;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
-      const int v = __shfl_up_sync(0xffffffffu, w, o);
-      if (lane >= o) w += v;
+      const int u = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += u;
     }
-    warp_sums[lane] = w;  // inclusive over warps
+    if (lane == 31) warp_sums[warp] = incl;
+    __syncthreads();
+    int before = carry;
+    for (int w2 = 0; w2 < warp; ++w2) before += warp_sums[w2];
+    if (mt < m_tiles) mt_first[mt] = min(before + incl - v, cap);
+    __syncthreads();
+    if (tid == kSlPieceThreads - 1) carry = before + incl;
+    __syncthreads();
   }
-  __syncthreads();
-  int base = incl - mine + (warp > 0 ? warp_sums[warp - 1] : 0);
-  const int total = warp_sums[kSlThreads / 32 - 1];
-  if (total > cap) {  // cannot happen (a piece holds >= 1 schedule tile, <= 2 slots each); keep every write in bounds
-    if (tid == 0) record_error(err, kDevErrBadIndex);
-  }
-  for (int mt = mt0; mt < mt1; ++mt) {
-    mt_first[mt] = min(base, cap);
-    const int b = base;
-    const int n = tile_slots(tiles, offsets, ranks, mt, T, R,
-                             [&](int k, int t0, int t1, int64_t row, int k16, int part) {
-                               if (b + k < cap)
-                                 slots[b + k] = make_int4(t0, t1, static_cast<int>(row), k16 | (part << 4));
-                             });
-    base += n;
-  }
+  const int total = carry;
+  if (total > cap && tid == 0) record_error(err, kDevErrBadIndex);  // cannot happen; keeps writes in bounds
   if (tid == 0) mt_first[m_tiles] = min(total, cap);
+  __syncthreads();
+  // pass 2: slot records
+  for (int mt = warp; mt < m_tiles; mt += kSlPieceWarps) {
+    const int base = mt_first[mt];
+    walk.run(mt, lane, [&](int k, int t0, int t1, int row, int k16, int part) {
+      if (base + k < cap) slots[base + k] = make_int4(t0, t1, row, k16 | (part << 4));
+    });
+  }
 }
 
 // ------------------------------------------------------------------ z fill
@@ -242,14 +301,40 @@ struct SlMaps {
 // stays inside the allocation.
 constexpr int kSlGuardBytes = 16 * 1024;
 
+// Order of an item's k-blocks: its n slot stages spread evenly among the kbm
+// base blocks (slot j after pos(j) base blocks).  A slot stage carries a few
+// MMAs against a full stage's loads, so a run of them would leave the tensor
+// pipe waiting on TMA latency; spread out, each hides behind the base blocks
+// around it.  Producer and MMA issuer walk the same order.
+struct KOrder {
+  int kbm, n, j = 0, b = 0, next;
+  __device__ KOrder(int kbm_, int n_) : kbm(kbm_), n(n_) { next = n > 0 ? pos(0) : kbm + 1; }
+  __device__ int pos(int jj) const {
+    return static_cast<int>((static_cast<int64_t>(jj + 1) * kbm) / (n + 1));
+  }
+  // true: slot stage j (in idx); false: base block (in idx)
+  __device__ bool step(int& idx) {
+    if (j < n && b >= next) {
+      idx = j++;
+      next = j < n ? pos(j) : kbm + 1;
+      return true;
+    }
+    idx = b++;
+    return false;
+  }
+};
+
 }  // namespace
 
-// The pair GEMM: 256 x 256 tiles (NW = 1 of gemm_tc2_kernel), base k-blocks
-// then the tile's slots.  Roles and barriers as in gemm_tc2_kernel.
-template <int STAGES, typename T>
+// The pair GEMM: 256 x 256 (NW = 1) or 256 x 512 (NW = 2) tiles as in
+// gemm_tc2_kernel, base k-blocks then the tile's slots.  Roles and barriers as
+// in gemm_tc2_kernel; NW = 2 keeps both TMEM halves for one tile and loads the
+// slot's B rows as one box per 256-column half.
+template <int STAGES, int NW, typename T>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
     sgmv_linear_pair_kernel(const __grid_constant__ SlMaps maps, const GemmArgs args, const SlArgs sl) {
-  using L = PairSmem<STAGES, 1>;
+  using L = PairSmem<STAGES, NW>;
+  constexpr int kTileN = 256 * NW;
   constexpr uint32_t kTmemCols = 512;
   constexpr uint32_t kIdesc = umma_idesc_f16(256, 256, std::is_same<T, __nv_bfloat16>::value ? 1 : 0);
   constexpr uint32_t kIdescMN = kIdesc | (1u << 16);  // B (adapter rows) MN-major
@@ -314,8 +399,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
         const int e0 = sl.mt_first[mt], e1 = sl.mt_first[mt + 1];
         const int num_kb = args.num_kb_main + (e1 - e0);
         const int row_a = mt * 256 + static_cast<int>(rank) * 128;
-        const int row_b = nt * 256 + static_cast<int>(rank) * 128;
-        for (int kb = 0; kb < num_kb; ++kb) {
+        const int row_b = nt * kTileN + static_cast<int>(rank) * 128;  // + 256 for the second half
+        KOrder order(args.num_kb_main, e1 - e0);
+        for (int q = 0; q < num_kb; ++q) {
           if (!mbar_wait_bounded(&empty[stage], phase ^ 1, abort_flag, args.err, kDevErrTimeoutEmpty)) {
             ok = false;
             break;
@@ -323,17 +409,22 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
           const uint32_t bar = mapa_shared(smem_u32(&full[stage]), 0);
           uint8_t* da = sm_a + stage * L::kABytes;
           uint8_t* db = sm_b + stage * L::kBBytes;
-          if (kb < args.num_kb_main) {
+          int kb;
+          if (!order.step(kb)) {
             if (leader) mbar_arrive_expect_tx(&full[stage], 2 * L::kStageBytes);
             tma_load_2d_pair(&maps.x, da, bar, kb * kGemmBK, row_a);
-            tma_load_2d_pair(&maps.w, db, bar, kb * kGemmBK, row_b);
+#pragma unroll
+            for (int h = 0; h < NW; ++h)
+              tma_load_2d_pair(&maps.w, db + h * (128 * kGemmBK * 2), bar, kb * kGemmBK, row_b + 256 * h);
           } else {
-            const int e = e0 + kb - args.num_kb_main;
+            const int e = e0 + kb;
             const int4 s = sl.slots[e];
             const int k16 = s.w & 15;
-            if (leader) mbar_arrive_expect_tx(&full[stage], 2 * (L::kABytes + k16 * 16 * 128 * 2));
+            if (leader) mbar_arrive_expect_tx(&full[stage], 2 * (L::kABytes + NW * k16 * 16 * 128 * 2));
             tma_load_2d_pair(&maps.z, da, bar, 0, e * 256 + static_cast<int>(rank) * 128);
-            tma_load_3d_pair(&maps.b[k16 - 1], db, bar, 0, s.z, row_b / 64);
+#pragma unroll
+            for (int h = 0; h < NW; ++h)
+              tma_load_3d_pair(&maps.b[k16 - 1], db + h * (128 * kGemmBK * 2), bar, 0, s.z, (row_b + 256 * h) / 64);
           }
           if (++stage == STAGES) {
             stage = 0;
@@ -354,35 +445,52 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
         gemm_tile_coords(item, args, mt, nt);
         const int e0 = sl.mt_first[mt], e1 = sl.mt_first[mt + 1];
         const int num_kb = args.num_kb_main + (e1 - e0);
-        const int acc = local & 1;
-        const uint32_t acc_phase = (local >> 1) & 1;
+        // NW = 1: accumulator local & 1, its (local >> 1)-th use; NW = 2: both halves, every tile
+        const int acc = NW == 1 ? (local & 1) : 0;
+        const uint32_t acc_phase = NW == 1 ? ((local >> 1) & 1) : (local & 1);
         if (!mbar_wait_bounded(&acc_empty[acc], acc_phase ^ 1, abort_flag, args.err, kDevErrTimeoutAccEmpty))
           break;
         tc_fence_after();
-        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * 256);
-        for (int kb = 0; kb < num_kb; ++kb) {
+        KOrder order(args.num_kb_main, e1 - e0);
+        uint32_t accum = 0u;  // the item's first MMA into each half starts the sum
+        for (int q = 0; q < num_kb; ++q) {
           if (!mbar_wait_bounded(&full[stage], phase, abort_flag, args.err, kDevErrTimeoutFull)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint64_t adesc = umma_desc_sw128(smem_u32(sm_a + stage * L::kABytes));
-          const uint32_t bs = smem_u32(sm_b + stage * L::kBBytes);
-          if (kb < args.num_kb_main) {
-            const uint64_t bdesc = umma_desc_sw128(bs);
-            for (int k = 0; k < 4; ++k)
-              tc_mma_f16_pair(d_tmem, adesc + static_cast<uint64_t>(2 * k), bdesc + static_cast<uint64_t>(2 * k),
-                              kIdesc, (kb > 0 || k > 0) ? 1u : 0u);
-          } else {
-            const int4 s = sl.slots[e0 + kb - args.num_kb_main];
-            const int k16 = s.w & 15, part = (s.w >> 4) & 3;
-            const uint32_t lbo = static_cast<uint32_t>(k16 * 16 * 128);  // chunk stride of the B box
-            // hi columns at k-step 0.., lo (packed slot) at k-step 2..: same B rows
-            for (int h = 0; h < (part == 0 ? 2 : 1); ++h)
-              for (int ks = 0; ks < k16; ++ks)
-                tc_mma_f16_pair(d_tmem, adesc + static_cast<uint64_t>(2 * (2 * h + ks)),
-                                sl_desc_mn(bs + static_cast<uint32_t>(ks * 2048), lbo), kIdescMN, 1u);
+          if (NW == 2 && q == 0) {  // the second half: free once the epilogue has drained it
+            if (!mbar_wait_bounded(&acc_empty[1], acc_phase ^ 1, abort_flag, args.err, kDevErrTimeoutAccEmpty)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
           }
+          const uint64_t adesc = umma_desc_sw128(smem_u32(sm_a + stage * L::kABytes));
+          int kb;
+          const bool slot = order.step(kb);
+#pragma unroll
+          for (int hn = 0; hn < NW; ++hn) {
+            const uint32_t d_tmem = tmem_base + static_cast<uint32_t>((NW == 1 ? acc : hn) * 256);
+            const uint32_t bs = smem_u32(sm_b + stage * L::kBBytes + hn * (128 * kGemmBK * 2));
+            if (!slot) {
+              const uint64_t bdesc = umma_desc_sw128(bs);
+              for (int k = 0; k < 4; ++k)
+                tc_mma_f16_pair(d_tmem, adesc + static_cast<uint64_t>(2 * k), bdesc + static_cast<uint64_t>(2 * k),
+                                kIdesc, (accum || k > 0) ? 1u : 0u);
+            } else {
+              const int4 s = sl.slots[e0 + kb];
+              const int k16 = s.w & 15, part = (s.w >> 4) & 3;
+              const uint32_t lbo = static_cast<uint32_t>(k16 * 16 * 128);  // chunk stride of the B box
+              // hi columns at k-step 0.., lo (packed slot) at k-step 2..: same B rows
+              for (int h = 0; h < (part == 0 ? 2 : 1); ++h)
+                for (int ks = 0; ks < k16; ++ks)
+                  tc_mma_f16_pair(d_tmem, adesc + static_cast<uint64_t>(2 * (2 * h + ks)),
+                                  sl_desc_mn(bs + static_cast<uint32_t>(ks * 2048), lbo), kIdescMN,
+                                  (accum || h > 0 || ks > 0) ? 1u : 0u);
+            }
+          }
+          accum = 1u;
           tc_commit_pair(&empty[stage], kBoth);
           if (++stage == STAGES) {
             stage = 0;
@@ -400,25 +508,30 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
     const uint64_t st_policy = l2_policy_evict_first();
     int local = 0;
     for (int item = pair; item < num_items; item += npairs, ++local) {
-      const int acc = local & 1;
-      const uint32_t acc_phase = (local >> 1) & 1;
+      const int acc = NW == 1 ? (local & 1) : 0;
+      const uint32_t acc_phase = NW == 1 ? ((local >> 1) & 1) : (local & 1);
       int mt, nt;
       gemm_tile_coords(item, args, mt, nt);
       if (!mbar_wait_bounded(&acc_full[acc], acc_phase, abort_flag, args.err, kDevErrTimeoutAccFull)) break;
       tc_fence_after();
       const int row = mt * 256 + static_cast<int>(rank) * 128 + quad * 32 + lane;
       T* out_row = static_cast<T*>(args.out) + static_cast<int64_t>(row) * args.ldo;
-      const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + static_cast<uint32_t>(acc * 256);
 #pragma unroll 1
-      for (int c = 0; c < 256; c += 16) {
-        uint32_t r[16];
-        tmem_ld_32x32b_x16(t_row + c, r);
-        tmem_wait_ld();
-        epilogue_store16<T>(args, out_row, bias, row, nt * 256 + c, vec_ok, r, st_policy);
+      for (int h = 0; h < NW; ++h) {
+        const int half = NW == 1 ? acc : h;  // TMEM accumulator drained in this round
+        const uint32_t t_row =
+            tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + static_cast<uint32_t>(half * 256);
+#pragma unroll 1
+        for (int c = 0; c < 256; c += 16) {
+          uint32_t r[16];
+          tmem_ld_32x32b_x16(t_row + c, r);
+          tmem_wait_ld();
+          epilogue_store16<T>(args, out_row, bias, row, nt * kTileN + h * 256 + c, vec_ok, r, st_policy);
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(&acc_empty[half]), 0));
       }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(&acc_empty[acc]), 0));
     }
   }
 
@@ -468,11 +581,11 @@ bool sl_chunk_map(CUtensorMap* map, const void* ptr, int dtype, uint64_t rows, u
 
 inline bool sl_al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
-template <typename T>
+template <int STAGES, int NW, typename T>
 int launch_sl_pair(const SlMaps& maps, const GemmArgs& a, const SlArgs& sl, int pairs_cap, cudaStream_t stream) {
-  using L = PairSmem<kSlStages, 1>;
+  using L = PairSmem<STAGES, NW>;
   const size_t smem = L::kBytes + kSlGuardBytes;
-  auto kernel = sgmv_linear_pair_kernel<kSlStages, T>;
+  auto kernel = sgmv_linear_pair_kernel<STAGES, NW, T>;
   if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem)) !=
       cudaSuccess)
     return LORA_ERR_CUDA;
@@ -519,7 +632,7 @@ int launch_sgmv_linear(const void* x, int64_t ldx, const void* w, int64_t ldw, c
     cudaLaunchConfig_t cfg = {};
     cudaLaunchAttribute attr[1];
     cfg.gridDim = dim3(1);
-    cfg.blockDim = dim3(kSlThreads);
+    cfg.blockDim = dim3(kSlPieceThreads);
     cfg.stream = s;
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
@@ -586,7 +699,10 @@ int launch_sgmv_linear(const void* x, int64_t ldx, const void* w, int64_t ldw, c
   a.num_kb_tail = 0;
   a.tail_last_k16 = 4;
   a.num_m_tiles = static_cast<int>(l.m_tiles);
-  a.num_n_tiles = static_cast<int>((N + 255) / 256);
+  // tile width as the plain GEMM picks it for this shape (the tail adds a
+  // few k-blocks per tile, not enough to change the choice)
+  const int nw = gemm_pair_width(T, N, K, num_sms);
+  a.num_n_tiles = static_cast<int>((N + 256 * nw - 1) / (256 * nw));
   a.num_tiles = a.num_m_tiles * a.num_n_tiles;
   a.group_m = 8;
   a.l2_hints = 0;
@@ -597,8 +713,11 @@ int launch_sgmv_linear(const void* x, int64_t ldx, const void* w, int64_t ldw, c
   a.tail_tickets = nullptr;
   SlArgs sl{mt_first, slots};
   const int pairs_cap = std::max(1, num_sms / 2);
-  return dtype == LORA_BF16 ? launch_sl_pair<__nv_bfloat16>(maps, a, sl, pairs_cap, s)
-                            : launch_sl_pair<__half>(maps, a, sl, pairs_cap, s);
+  if (nw == 2)
+    return dtype == LORA_BF16 ? launch_sl_pair<4, 2, __nv_bfloat16>(maps, a, sl, pairs_cap, s)
+                              : launch_sl_pair<4, 2, __half>(maps, a, sl, pairs_cap, s);
+  return dtype == LORA_BF16 ? launch_sl_pair<kSlStages, 1, __nv_bfloat16>(maps, a, sl, pairs_cap, s)
+                            : launch_sl_pair<kSlStages, 1, __half>(maps, a, sl, pairs_cap, s);
 }
 
 }  // namespace lora
