@@ -317,7 +317,7 @@ def _time_allgather(outs, total, world, dist):
                     "outside the headline timing"}
 
 
-def _copy_bound(host_x, host_out, dev_x, dev_out, dev):
+def _copy_bound(host_x, host_out, dev_x, dev_out, dev, world=1, dist=None):
     """Device time of copying the step's inputs in and outputs out at the same
     time (two streams, pinned host memory): the e2e step's lower bound."""
     import torch
@@ -326,6 +326,9 @@ def _copy_bound(host_x, host_out, dev_x, dev_out, dev):
     main = torch.cuda.current_stream(dev)
     times = []
     for _ in range(3):
+        if world > 1:  # every rank copies at once, as in the e2e steps
+            torch.cuda.synchronize()
+            dist.barrier()
         a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         a.record(main)
         h2d_s.wait_stream(main)
@@ -395,7 +398,8 @@ def _e2e(projs, steps, world, dist, dev):
             e2e_step(s)
         torch.cuda.synchronize()
         bound_ms = _copy_bound(host_x, host_out, dev_x[0], [torch.empty((p.m, p.n), device=dev,
-                                                                       dtype=torch.bfloat16) for p in projs], dev)
+                                                                       dtype=torch.bfloat16) for p in projs], dev,
+                               world, dist)
         if world > 1:
             dist.barrier()
         e_steps = max(1, min(steps, 5))
