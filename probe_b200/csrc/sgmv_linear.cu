@@ -301,6 +301,12 @@ struct SlMaps {
 // stays inside the allocation.
 constexpr int kSlGuardBytes = 16 * 1024;
 
+// Output tiles are taken heaviest row band first (most slots), and the pairs
+// take them in a snake order (forward in even rounds, backward in odd ones),
+// so a pair that drew a heavy band in one round draws a light one in the next.
+// Bands beyond this many keep the plain raster.
+constexpr int kSlSortMax = 256;
+
 // Order of an item's k-blocks: its n slot stages spread evenly among the kbm
 // base blocks (slot j after pos(j) base blocks).  A slot stage carries a few
 // MMAs against a full stage's loads, so a run of them would leave the tensor
@@ -381,11 +387,38 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
     tmem_alloc_pair(tmem_slot, kTmemCols);
     tmem_relinquish_pair();
   }
+  __shared__ int s_cost[kSlSortMax];
+  __shared__ int s_order[kSlSortMax];
+  const int m_tiles = args.num_m_tiles;
+  const bool by_cost = m_tiles <= kSlSortMax;
+  if (by_cost) {
+    for (int m = threadIdx.x; m < m_tiles; m += blockDim.x) s_cost[m] = sl.mt_first[m + 1] - sl.mt_first[m];
+    __syncthreads();
+    for (int m = threadIdx.x; m < m_tiles; m += blockDim.x) {
+      const int c = s_cost[m];
+      int rank = 0;
+      for (int j = 0; j < m_tiles; ++j) rank += (s_cost[j] > c) || (s_cost[j] == c && j < m);
+      s_order[rank] = m;
+    }
+  }
+  __syncthreads();
   tc_fence_before();
   cluster_sync_all();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
   const int num_items = args.num_tiles;
+  // This pair's j-th output tile (false: none left); every role walks the same sequence.
+  auto pair_tile = [&](int j, int& mt, int& nt) {
+    const int item = j * npairs + ((j & 1) ? (npairs - 1 - pair) : pair);
+    if (item >= num_items) return false;
+    if (by_cost) {
+      mt = s_order[item / args.num_n_tiles];
+      nt = item - (item / args.num_n_tiles) * args.num_n_tiles;
+    } else {
+      gemm_tile_coords(item, args, mt, nt);
+    }
+    return true;
+  };
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
@@ -393,9 +426,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
-      for (int item = pair; ok && item < num_items; item += npairs) {
-        int mt, nt;
-        gemm_tile_coords(item, args, mt, nt);
+      int mt, nt;
+      for (int j = 0; ok && pair_tile(j, mt, nt); ++j) {
         const int e0 = sl.mt_first[mt], e1 = sl.mt_first[mt + 1];
         const int num_kb = args.num_kb_main + (e1 - e0);
         const int row_a = mt * 256 + static_cast<int>(rank) * 128;
@@ -440,9 +472,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
       uint32_t phase = 0;
       int local = 0;
       bool ok = true;
-      for (int item = pair; ok && item < num_items; item += npairs, ++local) {
-        int mt, nt;
-        gemm_tile_coords(item, args, mt, nt);
+      int mt, nt;
+      for (int j = 0; ok && pair_tile(j, mt, nt); ++j, ++local) {
         const int e0 = sl.mt_first[mt], e1 = sl.mt_first[mt + 1];
         const int num_kb = args.num_kb_main + (e1 - e0);
         // NW = 1: accumulator local & 1, its (local >> 1)-th use; NW = 2: both halves, every tile
@@ -507,11 +538,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kGemmThreads, 1)
     const bool vec_ok = (args.ldo % 8) == 0 && (reinterpret_cast<uintptr_t>(args.out) % 16) == 0;
     const uint64_t st_policy = l2_policy_evict_first();
     int local = 0;
-    for (int item = pair; item < num_items; item += npairs, ++local) {
+    int mt, nt;
+    for (int j = 0; pair_tile(j, mt, nt); ++j, ++local) {
       const int acc = NW == 1 ? (local & 1) : 0;
       const uint32_t acc_phase = NW == 1 ? ((local >> 1) & 1) : (local & 1);
-      int mt, nt;
-      gemm_tile_coords(item, args, mt, nt);
       if (!mbar_wait_bounded(&acc_full[acc], acc_phase, abort_flag, args.err, kDevErrTimeoutAccFull)) break;
       tc_fence_after();
       const int row = mt * 256 + static_cast<int>(rank) * 128 + quad * 32 + lane;

@@ -8,8 +8,7 @@ per-token random ids (many pieces per tile), rank-0 adapters, ranks above 32
 below one tile, N not a multiple of 256, unknown adapter ids (base only,
 error recorded).  Results against the float64 oracle (the exact base plus
 ``ragged_branch``) on sampled tokens, against a plain PyTorch fp32 computation
-of the same op (z rounded to bf16, as the kernel rounds it) over the whole
-output, and bit-identical on repeat.
+of the same op over the whole output, and bit-identical on repeat.
 """
 
 import math
@@ -76,6 +75,8 @@ def _fp32_close(got, x, w, bias, a, b, offs, rk, ids):
     (2048, 2048, 2048, [4, 8, 16, 32, 64] * 4, "zipf", True),
     (1500, 3072, 4608, [4, 8, 16, 32, 64] * 4, "runs", True),  # 256 x 512 tiles, last tile cut by T
     (600, 3072, 4096, [64, 8, 0, 40], "random", False),          # 256 x 512 tiles, many pieces
+    (50, 64, 64, [16, 8], "runs", True),                          # one k-block, one 64-column chunk
+    (3000, 128, 192, [32, 64, 4], "zipf", False),                 # short K, N = 3 chunks
 ])
 def test_sgmv_linear_matches_oracle(t, k, n, ranks, mode, with_bias):
     rng = np.random.default_rng(t + n)
@@ -152,3 +153,19 @@ def test_sgmv_linear_declines_outside_its_domain():
         got = ragged_branch.linear(x, w, None, a, b, offs, rk, idt, max(ranks))
         rep = checks.seg_linear_report(got, x, w, None, a, b, offs, rk, ids)
         assert rep["ok"], rep
+
+
+def test_sgmv_linear_fp16():
+    t, k, n = 700, 512, 768
+    ids = np.repeat(np.random.default_rng(3).integers(0, 3, size=t // 50 + 1), 50)[:t]
+    a, b, offs, rk = _tables([16, 64, 8], k, n, seed=12)
+    a, b = a.half(), b.half()
+    x = randn((t, k), 1.0, dtype=torch.float16, seed=13)
+    w = randn((n, k), 1 / math.sqrt(k), dtype=torch.float16, seed=14)
+    bias = randn((n,), 1.0, dtype=torch.float16, seed=15)
+    got = ragged_branch.linear(x, w, bias, a, b, offs, rk, torch.as_tensor(ids, device=DEV), 64)
+    assert got.dtype == torch.float16
+    rep = checks.seg_linear_report(got, x, w, bias, a, b, offs, rk, ids, dtype="f16")
+    assert rep["ok"], rep
+    ok, worst = _fp32_close(got, x, w, bias, a, b, offs, rk, ids)
+    assert ok, worst
