@@ -777,10 +777,14 @@ int pair_tile_width(int64_t M, int64_t N, int64_t K, int64_t R, int pairs, bool 
     const char* v = std::getenv("LORA_B200_GEMM_WIDE");
     return (v != nullptr && (v[0] == '0' || v[0] == '1')) ? v[0] - '0' : -1;
   }();
-  if (force == 0 || N < 512) return 1;
+  if (force == 0 || N <= 256) return 1;
   if (force == 1) return 2;
   const int64_t mt = (M + 255) / 256;
   const int num_kb = static_cast<int>((K + kGemmBK - 1) / kGemmBK + (R + kGemmBK - 1) / kGemmBK);
+  // 256 < N <= 512 (the hi/lo output of a rank-224 shrink): one wide tile
+  // covers every column, so x is read once instead of once per 256 columns
+  // -- the whole cost of such a narrow, memory-bound product.
+  if (N <= 512) return num_kb >= 48 ? 2 : 1;
   const int64_t tiles2 = mt * ((N + 511) / 512);
   // Short K: a 256 x 512 tile's epilogue is no longer hidden behind the next
   // tile's mainloop (measured at K = 1536: 256 x 256 tiles 25 % faster).
