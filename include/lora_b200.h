@@ -216,12 +216,10 @@ LORA_API int lora_decode_linear(const void* x, int64_t ldx, const void* w, int64
  * Up to 128 tokens (and ranks above 64) run the W-streaming skinny kernel,
  * where scale * z enters the expand as a hi/lo pair of the input dtype.  Above
  * 128 tokens with R <= 64 a split-K CTA-pair kernel runs instead (256-token
- * tiles, K split over CTA pairs, z kept in fp32); it exchanges partial tiles
+ * tiles, K split over a cluster, z kept in fp32); it exchanges partial tiles
  * through `workspace`, which must hold lora_linear_small_workspace_size(M, N, R)
- * bytes (16-byte aligned), must be zeroed once before its first use (its
- * first 8 KiB hold arrival counters, which every launch leaves valid for the
- * next) and must not be used by a concurrent launch.  With a smaller or NULL
- * workspace the skinny kernel runs.
+ * bytes (16-byte aligned) and must not be used by a concurrent launch.  With a
+ * smaller or NULL workspace the skinny kernel runs.
  * Replaces: decode_lora_linear (decode_linear.py:81-100) and the small-M
  * fused_lora_linear (fused_linear.py:527-551) -- shrink, expand and base in
  * one launch, where the reference re-derives x . A^T in every output tile.

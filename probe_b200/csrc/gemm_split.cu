@@ -29,21 +29,7 @@
 // split order to its own columns, adds the bias and writes bf16/f16 rows.
 // The exchange goes through L2 rather than distributed shared memory: the
 // SM-to-SM network moved these ~90 KB per CTA several times slower on B200.
-// No TMA multicast; results are deterministic (split order).
-//
-// Two forms of the barrier between the partials' stores and the owners'
-// reads.  Cluster form: the 2 x S CTAs of a tile are one cluster and meet at a
-// cluster barrier; B200 keeps only 15 clusters of 8 resident, so a 16-tile
-// output gets S = 3.  Grid form (GB): clusters are single CTA pairs and the
-// S pairs of a tile meet at a counter in the workspace (one arrival per CTA,
-// a bounded spin until all 2 x S have arrived), which lets S grow until the
-// pairs fill the machine (C1's 16 tiles: S = 4, 128 SMs instead of 96).  The
-// grid form is used only when every CTA of the launch is resident at once,
-// and a CTA signals its dependents only after it has passed the barrier, so
-// no later launch can take the SMs a waiting CTA's partners need.  Each
-// (S, tile) has its own counter, which every launch advances by exactly 2 x S
-// (the wait target is derived from the value an arrival returns), so the
-// counters never need resetting.
+// No TMA multicast and no atomics: results are deterministic.
 //
 // Launched with programmatic stream serialization: every CTA signals its
 // dependents at once, and the producer loads the weight tiles (W, lora_A) of
@@ -84,7 +70,6 @@ struct SplitArgs {
   const void* bias;
   const void* b;  // lora_B [N, R] (fused form)
   float* ws;      // partial exchange (SplitWs layout)
-  unsigned* counters;  // grid form: per (S, tile) arrival counters (zeroed once)
   int* err;
   int64_t ldo, ldb;
   int M, N, R;
@@ -146,21 +131,8 @@ LORA_DEVINL void store_row16(T* out_row, int col0, int N, bool vec_ok, const flo
   }
 }
 
-// Grid-form counters: one row of kGbMaxTiles per S at the workspace's start.
-constexpr int kGbMaxS = 8;
-constexpr int kGbMaxTiles = 128;
-constexpr size_t kGbCounterBytes = 8192;
-static_assert((kGbMaxS + 1) * kGbMaxTiles * 4 <= static_cast<int>(kGbCounterBytes), "counter region");
-
-LORA_DEVINL unsigned ld_acquire_gpu(const unsigned* p) {
-  unsigned v;
-  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
-
 // RZ = 0: plain linear; RZ = 16 / 32 / 64: fused shrink of rank <= RZ.
-// GB: grid form (clusters of one CTA pair, slices meet at a workspace counter).
-template <int S, int RZ, bool GB, typename T>
+template <int S, int RZ, typename T>
 __global__ void __launch_bounds__(kSpThreads, 1)
     gemm_split_pair_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_w,
                            const __grid_constant__ CUtensorMap tm_a, const SplitArgs args) {
@@ -190,10 +162,9 @@ __global__ void __launch_bounds__(kSpThreads, 1)
   const int lane = threadIdx.x & 31;
   const uint32_t rank = cluster_ctarank();
   const uint32_t half = rank & 1u;  // 0: the pair's MMA issuer
-  const int split = GB ? static_cast<int>(blockIdx.y) : static_cast<int>(rank >> 1);
+  const int split = static_cast<int>(rank >> 1);
   const uint32_t leader_rank = rank & ~1u;
-  const uint16_t pair_mask = GB ? static_cast<uint16_t>(0x3u) : static_cast<uint16_t>(0x3u << (2 * split));
-  __shared__ int gb_passed;
+  const uint16_t pair_mask = static_cast<uint16_t>(0x3u << (2 * split));
   const int tile = blockIdx.z;
   const int mt = tile / args.num_n_tiles;
   const int nt = tile - mt * args.num_n_tiles;
@@ -217,7 +188,7 @@ __global__ void __launch_bounds__(kSpThreads, 1)
     tma_prefetch_desc(&tm_w);
     if (RZ > 0) tma_prefetch_desc(&tm_a);
   }
-  if (!GB && threadIdx.x == 0) pdl_launch_dependents();
+  if (threadIdx.x == 0) pdl_launch_dependents();
   if (warp == 2) {
     tmem_alloc_pair(tmem_slot, kTmemCols);
     tmem_relinquish_pair();
@@ -408,38 +379,11 @@ __global__ void __launch_bounds__(kSpThreads, 1)
       fence_proxy_async_global();  // the owners read these with bulk copies
     }
   }
-  // Release / acquire: every split's partials are in the workspace before any
-  // owner reads them (over the cluster, or over the grid through the counter).
+  // Release / acquire over the cluster: every split's partials are in the
+  // workspace before any owner reads them.
   tc_fence_before();
   __syncwarp();
-  if constexpr (GB) {
-    __threadfence();  // this thread's partial stores, before the CTA's arrival
-    __syncthreads();
-    if (threadIdx.x == 0) {
-      unsigned* cnt = args.counters + S * kGbMaxTiles + tile;
-      __threadfence();
-      const unsigned old = atomicAdd(cnt, 1u);
-      const unsigned target = old - old % (2u * S) + 2u * S;
-      int passed = 1;
-      if (static_cast<int>(ld_acquire_gpu(cnt) - target) < 0) {
-        const uint64_t t0 = globaltimer_ns();
-        while (static_cast<int>(ld_acquire_gpu(cnt) - target) < 0) {
-          if (globaltimer_ns() - t0 > kWaitLimitNs) {
-            record_error(args.err, kDevErrTimeoutSplitK);
-            passed = 0;
-            break;
-          }
-        }
-      }
-      __threadfence();
-      gb_passed = passed;
-      pdl_launch_dependents();  // only now: every CTA of this tile is resident
-    }
-    __syncthreads();
-    have = have && gb_passed != 0;
-  } else {
-    cluster_sync_all();
-  }
+  cluster_sync_all();
   tc_fence_after();
 
   if (warp >= 2 && have) {
@@ -526,7 +470,7 @@ int env_slices() {
   return std::atoi(v);
 }
 
-template <int S, int RZ, bool GB, typename T>
+template <int S, int RZ, typename T>
 cudaLaunchConfig_t make_config(int tiles, cudaStream_t stream, cudaLaunchAttribute* attr) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = dim3(2, S, static_cast<unsigned>(tiles));
@@ -535,7 +479,7 @@ cudaLaunchConfig_t make_config(int tiles, cudaStream_t stream, cudaLaunchAttribu
   cfg.stream = stream;
   attr[0].id = cudaLaunchAttributeClusterDimension;
   attr[0].val.clusterDim.x = 2;
-  attr[0].val.clusterDim.y = GB ? 1 : S;
+  attr[0].val.clusterDim.y = S;
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
@@ -544,17 +488,17 @@ cudaLaunchConfig_t make_config(int tiles, cudaStream_t stream, cudaLaunchAttribu
 
 // Clusters of this instance that can be resident at once (0 if it cannot
 // launch), queried once per device.
-template <int S, int RZ, bool GB, typename T>
+template <int S, int RZ, typename T>
 int resident_clusters(int dev) {
   static std::once_flag once[64];
   static int value[64];
   std::call_once(once[dev & 63], [&] {
-    auto kernel = gemm_split_pair_kernel<S, RZ, GB, T>;
+    auto kernel = gemm_split_pair_kernel<S, RZ, T>;
     int clusters = 0;
     if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SplitSmem<S, RZ>::kBytes) ==
         cudaSuccess) {
       cudaLaunchAttribute attr[1];
-      cudaLaunchConfig_t cfg = make_config<S, RZ, GB, T>(64, nullptr, attr);
+      cudaLaunchConfig_t cfg = make_config<S, RZ, T>(64, nullptr, attr);
       if (cudaOccupancyMaxActiveClusters(&clusters, kernel, &cfg) != cudaSuccess) clusters = 0;
     }
     cudaGetLastError();
@@ -563,93 +507,60 @@ int resident_clusters(int dev) {
   return value[dev & 63];
 }
 
-template <int RZ, typename T>
-int resident_t(int S, bool gb, int dev) {
-  if (gb) {
-    if (S == 8) return resident_clusters<8, RZ, true, T>(dev);
-    if (S == 6) return resident_clusters<6, RZ, true, T>(dev);
-    if (S == 5) return resident_clusters<5, RZ, true, T>(dev);
-    if (S == 4) return resident_clusters<4, RZ, true, T>(dev);
-    return 0;
-  }
-  if (S == 4) return resident_clusters<4, RZ, false, T>(dev);
-  if (S == 3) return resident_clusters<3, RZ, false, T>(dev);
-  if (S == 2) return resident_clusters<2, RZ, false, T>(dev);
-  return resident_clusters<1, RZ, false, T>(dev);
-}
-
 template <int RZ>
-int resident_for(int S, bool gb, int dtype, int dev) {
-  return dtype == LORA_BF16 ? resident_t<RZ, __nv_bfloat16>(S, gb, dev) : resident_t<RZ, __half>(S, gb, dev);
-}
-
-int resident(int S, bool gb, int rz, int dtype, int dev) {
-  if (rz == 0) return resident_for<0>(S, gb, dtype, dev);
-  if (rz == 16) return resident_for<16>(S, gb, dtype, dev);
-  if (rz == 32) return resident_for<32>(S, gb, dtype, dev);
-  return resident_for<64>(S, gb, dtype, dev);
-}
-
-struct SplitPlan {
-  int S;
-  bool gb;
-};
-
-// K slices for a launch, or S = 0 (use another kernel).  Cluster form: the
-// most slices (4, 3, 2) whose 2 x S-CTA clusters are all resident in one wave
-// (a second wave costs a whole extra mainloop), each slice keeping at least 8
-// k-blocks.  Grid form, when it allows more slices than that: S in 8, 6, 5, 4
-// with every pair of the launch resident at once (its barrier waits for all
-// of them).  Wider outputs take one slice (no exchange), in as many waves of
-// resident pairs as their tiles need: each wave costs about one 256 x 256
-// tile's mainloop, still well under the W-streaming kernel's time at these
-// token counts.  LORA_B200_SPLIT_PAIR=0/1/2/3/4 forces the cluster form's
-// choice, =g4/g5/g6/g8 the grid form (for tuning sweeps).
-SplitPlan plan_slices(int64_t M, int64_t N, int64_t num_kb, int rz, int dtype, int dev, int num_sms) {
-  const SplitPlan none{0, false};
-  if (M <= 0 || N <= 128 || num_kb <= 0) return none;
-  const int64_t tiles = ((M + 255) / 256) * ((N + 255) / 256);
-  if (tiles > 65535) return none;
-  const char* env = std::getenv("LORA_B200_SPLIT_PAIR");
-  if (env != nullptr && env[0] == 'g') {
-    const int S = std::atoi(env + 1);
-    if ((S == 4 || S == 5 || S == 6 || S == 8) && num_kb >= S * S && tiles <= kGbMaxTiles &&
-        tiles * S <= resident(S, true, rz, dtype, dev))
-      return SplitPlan{S, true};
-    return none;
+int resident_for(int S, int dtype, int dev) {
+  if (dtype == LORA_BF16) {
+    if (S == 4) return resident_clusters<4, RZ, __nv_bfloat16>(dev);
+    if (S == 3) return resident_clusters<3, RZ, __nv_bfloat16>(dev);
+    if (S == 2) return resident_clusters<2, RZ, __nv_bfloat16>(dev);
+    return resident_clusters<1, RZ, __nv_bfloat16>(dev);
   }
+  if (S == 4) return resident_clusters<4, RZ, __half>(dev);
+  if (S == 3) return resident_clusters<3, RZ, __half>(dev);
+  if (S == 2) return resident_clusters<2, RZ, __half>(dev);
+  return resident_clusters<1, RZ, __half>(dev);
+}
+
+int resident(int S, int rz, int dtype, int dev) {
+  if (rz == 0) return resident_for<0>(S, dtype, dev);
+  if (rz == 16) return resident_for<16>(S, dtype, dev);
+  if (rz == 32) return resident_for<32>(S, dtype, dev);
+  return resident_for<64>(S, dtype, dev);
+}
+
+// K slices for a launch, or 0 (use another kernel): the most slices (4, 3, 2)
+// whose 2 x S CTAs per tile fit the machine with every cluster resident in one
+// wave (a second wave costs a whole extra mainloop), each slice keeping at
+// least 8 k-blocks.  Wider outputs take one slice (no exchange), in as many
+// waves of resident pairs as their tiles need: each wave costs about one
+// 256 x 256 tile's mainloop, still well under the W-streaming kernel's time
+// at these token counts.  LORA_B200_SPLIT_PAIR=0/1/2/3/4 forces the choice
+// (for tuning sweeps).
+int plan_slices(int64_t M, int64_t N, int64_t num_kb, int rz, int dtype, int dev, int num_sms) {
+  if (M <= 0 || N <= 128 || num_kb <= 0) return 0;
+  const int64_t tiles = ((M + 255) / 256) * ((N + 255) / 256);
+  if (tiles > 65535) return 0;
   const int forced = env_slices();
-  if (forced == 0) return none;
+  if (forced == 0) return 0;
   if (forced >= 1 && forced <= 4)  // at least S k-blocks per slice, so that no slice is empty
-    return (num_kb >= forced * forced && resident(forced, false, rz, dtype, dev) > 0) ? SplitPlan{forced, false}
-                                                                                         : none;
-  int S_cluster = 0;
+    return (num_kb >= forced * forced && resident(forced, rz, dtype, dev) > 0) ? forced : 0;
   for (int S : {4, 3, 2}) {
     if (tiles * 2 * S > num_sms || num_kb < 8 * S) continue;
-    if (tiles > resident(S, false, rz, dtype, dev)) continue;
-    S_cluster = S;
-    break;
+    if (tiles > resident(S, rz, dtype, dev)) continue;
+    return S;
   }
-  if (tiles <= kGbMaxTiles) {
-    for (int S : {8, 6, 5, 4}) {
-      if (S <= S_cluster || tiles * 2 * S > num_sms || num_kb < 8 * S) continue;
-      if (tiles * S > resident(S, true, rz, dtype, dev)) continue;
-      return SplitPlan{S, true};
-    }
-  }
-  if (S_cluster > 0) return SplitPlan{S_cluster, false};
-  return (num_kb >= 8 && resident(1, false, rz, dtype, dev) > 0) ? SplitPlan{1, false} : none;
+  return (num_kb >= 8 && resident(1, rz, dtype, dev) > 0) ? 1 : 0;
 }
 
-template <int S, int RZ, bool GB, typename T>
+template <int S, int RZ, typename T>
 int launch_t(const CUtensorMap& tx, const CUtensorMap& tw, const CUtensorMap& ta, const SplitArgs& a, int tiles,
              cudaStream_t stream) {
-  auto kernel = gemm_split_pair_kernel<S, RZ, GB, T>;
+  auto kernel = gemm_split_pair_kernel<S, RZ, T>;
   if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SplitSmem<S, RZ>::kBytes) !=
       cudaSuccess)
     return LORA_ERR_CUDA;
   cudaLaunchAttribute attr[2];
-  cudaLaunchConfig_t cfg = make_config<S, RZ, GB, T>(tiles, stream, attr);
+  cudaLaunchConfig_t cfg = make_config<S, RZ, T>(tiles, stream, attr);
   attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[1].val.programmaticStreamSerializationAllowed = 1;
   cfg.numAttrs = pdl_enabled() ? 2 : 1;
@@ -657,42 +568,28 @@ int launch_t(const CUtensorMap& tx, const CUtensorMap& tw, const CUtensorMap& ta
 }
 
 template <int RZ, typename T>
-int launch_s(const SplitPlan& plan, const CUtensorMap& tx, const CUtensorMap& tw, const CUtensorMap& ta,
-             const SplitArgs& a, int tiles, cudaStream_t stream) {
-  if (plan.gb) {
-    if (plan.S == 8) return launch_t<8, RZ, true, T>(tx, tw, ta, a, tiles, stream);
-    if (plan.S == 6) return launch_t<6, RZ, true, T>(tx, tw, ta, a, tiles, stream);
-    if (plan.S == 5) return launch_t<5, RZ, true, T>(tx, tw, ta, a, tiles, stream);
-    return launch_t<4, RZ, true, T>(tx, tw, ta, a, tiles, stream);
-  }
-  if (plan.S == 4) return launch_t<4, RZ, false, T>(tx, tw, ta, a, tiles, stream);
-  if (plan.S == 3) return launch_t<3, RZ, false, T>(tx, tw, ta, a, tiles, stream);
-  if (plan.S == 2) return launch_t<2, RZ, false, T>(tx, tw, ta, a, tiles, stream);
-  return launch_t<1, RZ, false, T>(tx, tw, ta, a, tiles, stream);
+int launch_s(int S, const CUtensorMap& tx, const CUtensorMap& tw, const CUtensorMap& ta, const SplitArgs& a,
+             int tiles, cudaStream_t stream) {
+  if (S == 4) return launch_t<4, RZ, T>(tx, tw, ta, a, tiles, stream);
+  if (S == 3) return launch_t<3, RZ, T>(tx, tw, ta, a, tiles, stream);
+  if (S == 2) return launch_t<2, RZ, T>(tx, tw, ta, a, tiles, stream);
+  return launch_t<1, RZ, T>(tx, tw, ta, a, tiles, stream);
 }
 
 template <int RZ>
-int launch_rz(int dtype, const SplitPlan& plan, const CUtensorMap& tx, const CUtensorMap& tw, const CUtensorMap& ta,
+int launch_rz(int dtype, int S, const CUtensorMap& tx, const CUtensorMap& tw, const CUtensorMap& ta,
               const SplitArgs& a, int tiles, cudaStream_t stream) {
-  if (dtype == LORA_BF16) return launch_s<RZ, __nv_bfloat16>(plan, tx, tw, ta, a, tiles, stream);
-  return launch_s<RZ, __half>(plan, tx, tw, ta, a, tiles, stream);
+  if (dtype == LORA_BF16) return launch_s<RZ, __nv_bfloat16>(S, tx, tw, ta, a, tiles, stream);
+  return launch_s<RZ, __half>(S, tx, tw, ta, a, tiles, stream);
 }
 
 template <int S>
 size_t ws_bytes_s(int64_t tiles) {
-  return kGbCounterBytes + static_cast<size_t>(tiles * SplitWs<S>::kPerTile) * sizeof(float);
+  return static_cast<size_t>(tiles * SplitWs<S>::kPerTile) * sizeof(float);
 }
 
 size_t ws_bytes(int S, int64_t tiles) {
-  switch (S) {
-    case 8: return ws_bytes_s<8>(tiles);
-    case 6: return ws_bytes_s<6>(tiles);
-    case 5: return ws_bytes_s<5>(tiles);
-    case 4: return ws_bytes_s<4>(tiles);
-    case 3: return ws_bytes_s<3>(tiles);
-    case 2: return ws_bytes_s<2>(tiles);
-    default: return 0;
-  }
+  return S == 4 ? ws_bytes_s<4>(tiles) : (S == 3 ? ws_bytes_s<3>(tiles) : (S == 2 ? ws_bytes_s<2>(tiles) : 0));
 }
 
 int rz_for(int64_t R) { return R <= 0 ? 0 : (R <= 16 ? 16 : (R <= 32 ? 32 : 64)); }
@@ -702,8 +599,7 @@ int rz_for(int64_t R) { return R <= 0 ? 0 : (R <= 16 ? 16 : (R <= 32 ? 32 : 64))
 size_t split_pair_workspace_bytes(int64_t M, int64_t N, int64_t R) {
   if (M <= 0 || N <= 0 || R < 0 || R > kSplitMaxRank) return 0;
   const int64_t tiles = ((M + 255) / 256) * ((N + 255) / 256);
-  return std::max({ws_bytes(8, tiles), ws_bytes(6, tiles), ws_bytes(5, tiles), ws_bytes(4, tiles),
-                   ws_bytes(3, tiles), ws_bytes(2, tiles)});
+  return std::max({ws_bytes(4, tiles), ws_bytes(3, tiles), ws_bytes(2, tiles)});
 }
 
 int launch_linear_split(const void* x, int64_t ldx, const void* w, int64_t ldw, const void* a, int64_t lda,
@@ -719,8 +615,7 @@ int launch_linear_split(const void* x, int64_t ldx, const void* w, int64_t ldw, 
   const DeviceInfo& info = device_info(dev);
   const int rz = rz_for(R);
   const int64_t num_kb = (K + kSpBK - 1) / kSpBK;
-  const SplitPlan plan = plan_slices(M, N, num_kb, rz, dtype, dev, info.num_sms);
-  const int S = plan.S;
+  const int S = plan_slices(M, N, num_kb, rz, dtype, dev, info.num_sms);
   if (S == 0) return LORA_ERR_UNSUPPORTED;
   const int tiles = static_cast<int>(((M + 255) / 256) * ((N + 255) / 256));
   if (workspace_bytes < ws_bytes(S, tiles)) return LORA_ERR_UNSUPPORTED;
@@ -737,8 +632,7 @@ int launch_linear_split(const void* x, int64_t ldx, const void* w, int64_t ldw, 
   args.out = out;
   args.bias = bias;
   args.b = b;
-  args.counters = static_cast<unsigned*>(workspace);
-  args.ws = reinterpret_cast<float*>(static_cast<char*>(workspace) + kGbCounterBytes);
+  args.ws = static_cast<float*>(workspace);
   args.err = info.err_word;
   args.ldo = ldo;
   args.ldb = ldb;
@@ -750,10 +644,10 @@ int launch_linear_split(const void* x, int64_t ldx, const void* w, int64_t ldw, 
   args.num_n_tiles = static_cast<int>((N + 255) / 256);
   args.num_tiles = tiles;
   args.scale = scale;
-  if (rz == 0) return launch_rz<0>(dtype, plan, tx, tw, ta, args, tiles, stream);
-  if (rz == 16) return launch_rz<16>(dtype, plan, tx, tw, ta, args, tiles, stream);
-  if (rz == 32) return launch_rz<32>(dtype, plan, tx, tw, ta, args, tiles, stream);
-  return launch_rz<64>(dtype, plan, tx, tw, ta, args, tiles, stream);
+  if (rz == 0) return launch_rz<0>(dtype, S, tx, tw, ta, args, tiles, stream);
+  if (rz == 16) return launch_rz<16>(dtype, S, tx, tw, ta, args, tiles, stream);
+  if (rz == 32) return launch_rz<32>(dtype, S, tx, tw, ta, args, tiles, stream);
+  return launch_rz<64>(dtype, S, tx, tw, ta, args, tiles, stream);
 }
 
 }  // namespace lora

@@ -4,9 +4,7 @@ Reached through lora_linear_small for 128 < M <= 256 with rank <= 64 (the
 shrink accumulated beside the base tile, the partial tiles exchanged through
 the caller's workspace).  Each case is checked against the float64 oracle
 (oracle/lora_oracle.py); the slice count is forced both ways through
-LORA_B200_SPLIT_PAIR so that the 2-, 3- and 4-slice reductions over a
-cluster, the grid form with 4, 5, 6 and 8 slices meeting at a workspace
-counter (where the shape allows it; else the W-streaming kernel runs), and the
+LORA_B200_SPLIT_PAIR so that the 2-, 3- and 4-slice reductions and the
 single-slice form (no exchange; chosen on its own for wide outputs) all run.  Shapes
 cover partial token tiles (M not a multiple of 256), output widths that are
 not multiples of 256 or of 8, ranks 1, 16, 17, 32, 48 and 64 (the wider
@@ -34,7 +32,7 @@ def _case(m, n, k, r, dtype, seed):
     return x, w, bias, a, b
 
 
-@pytest.mark.parametrize("slices", ["1", "2", "3", "4", "g4", "g5", "g6", "g8", ""])
+@pytest.mark.parametrize("slices", ["1", "2", "3", "4", ""])
 @pytest.mark.parametrize("m,n,k,r", [(256, 4096, 4096, 16), (129, 1000, 2048, 1), (200, 1002, 1024, 17),
                                      (256, 512, 4096, 32), (160, 4096, 1536, 0), (256, 4096, 4096, 64),
                                      (231, 1000, 2048, 48), (129, 4096, 1024, 33), (256, 12288, 1024, 48)])
