@@ -323,7 +323,9 @@ LORA_API int lora_sgmv_branch(const void* x, int64_t ldx, const void* y, int64_t
  * output is written once, with the adapters in it; no y is read or written.
  * Launches: the tile's pieces (one CTA), the unit shrink, the slot fill, the
  * GEMM.  Workspace: lora_sgmv_linear_workspace_size(T, S, K, r_max) bytes
- * (256-byte aligned, no zeroing; one buffer per stream).  S: the segment
+ * (256-byte aligned, no zeroing; one buffer per stream); 0 when the batch's
+ * worst case needs more than 512 MiB (per-token ids over ~8000 tokens): then
+ * the call returns LORA_ERR_UNSUPPORTED.  S: the segment
  * count the tiles were scheduled from (0 for per-token ids).  Serves
  * r_max <= 64, K and N multiples of 64, leading dimensions multiples of 8,
  * 16-byte aligned rows; LORA_ERR_UNSUPPORTED otherwise (use lora_gemm +

@@ -626,8 +626,15 @@ int launch_sl_pair(const SlMaps& maps, const GemmArgs& a, const SlArgs& sl, int 
 
 }  // namespace
 
+// The slot region is sized for the worst case the schedule allows (every
+// schedule tile its own piece of two slots), 32 KB a slot.  Batches whose
+// worst case exceeds this (per-token ids over more than ~8000 tokens) are
+// declined: the base GEMM + branch path serves them.
+constexpr size_t kSlMaxWorkspace = size_t{512} << 20;
+
 size_t sgmv_linear_workspace(int64_t T, int64_t S, int64_t K, int64_t r_max, int num_sms) {
-  return sl_layout(T, S, K, r_max, num_sms).bytes;
+  const size_t bytes = sl_layout(T, S, K, r_max, num_sms).bytes;
+  return bytes <= kSlMaxWorkspace ? bytes : 0;
 }
 
 int launch_sgmv_linear(const void* x, int64_t ldx, const void* w, int64_t ldw, const void* bias, const void* a_flat,
@@ -644,8 +651,8 @@ int launch_sgmv_linear(const void* x, int64_t ldx, const void* w, int64_t ldw, c
       N > INT32_MAX / 2 || K > INT32_MAX)
     return LORA_ERR_UNSUPPORTED;
   const SlLayout l = sl_layout(T, S, K, r_max, num_sms);
-  if (l.cap * kSlTile > INT32_MAX || workspace == nullptr || (reinterpret_cast<uintptr_t>(workspace) & 255u) != 0 ||
-      workspace_bytes < l.bytes)
+  if (l.cap * kSlTile > INT32_MAX || l.bytes > kSlMaxWorkspace || workspace == nullptr ||
+      (reinterpret_cast<uintptr_t>(workspace) & 255u) != 0 || workspace_bytes < l.bytes)
     return LORA_ERR_UNSUPPORTED;
   const int dev = current_device();
   if (dev < 0) return LORA_ERR_DEVICE;

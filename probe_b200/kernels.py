@@ -375,6 +375,8 @@ def sgmv_linear(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None
         out = torch.empty((t, n), device=x.device, dtype=x.dtype)
     lib = _lib.load()
     ws_bytes = lib.lora_sgmv_linear_workspace_size(t, s, k, int(r_max))
+    if ws_bytes == 0:  # beyond the fused kernel's workspace cap (per-token ids over many tokens)
+        return None
     ws = _lib.WORKSPACE.get(ws_bytes, x.device, "sgmv_linear")
     offsets = _i64(offsets, x.device)
     ranks = _i64(ranks, x.device)

@@ -169,3 +169,21 @@ def test_sgmv_linear_fp16():
     assert rep["ok"], rep
     ok, worst = _fp32_close(got, x, w, bias, a, b, offs, rk, ids)
     assert ok, worst
+
+
+def test_sgmv_linear_declines_batches_beyond_its_workspace_cap():
+    """Per-token ids over 9000 tokens: the slot region's worst case (every token
+    its own piece) is above the cap, so the fused kernel declines and the surface
+    runs base GEMM + branch."""
+    t, k, n = 9000, 256, 256
+    a, b, offs, rk = _tables([16, 8], k, n, seed=21)
+    ids = np.random.default_rng(22).integers(0, 2, size=t)
+    x = randn((t, k), 1.0, seed=23)
+    w = randn((n, k), 1 / math.sqrt(k), seed=24)
+    idt = torch.as_tensor(ids, device=DEV)
+    assert _lib.load().lora_sgmv_linear_workspace_size(t, 0, k, 16) == 0
+    tiles, s = kernels.sgmv_schedule(t, 2, ids=idt)
+    assert kernels.sgmv_linear(x, w, None, a, b, offs, rk, tiles, s, 16) is None
+    got = ragged_branch.linear(x, w, None, a, b, offs, rk, idt, 16)
+    rep = checks.seg_linear_report(got, x, w, None, a, b, offs, rk, ids)
+    assert rep["ok"], rep
