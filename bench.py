@@ -616,31 +616,45 @@ def _time_chain(fns, iters, dev, launches=20):
     126 MB L2 every call reads its operands from HBM, and the graph-launch
     floor (about 6 us per replay) is spread over the whole chain.  Median over
     ``iters`` replays."""
+    return _time_chains([fns], iters, dev, launches)[0]
+
+
+def _time_chains(fn_lists, iters, dev, launches=20):
+    """``_time_chain`` for several calls compared with one another: one graph per
+    entry of ``fn_lists``, their replays interleaved (A B A B ...), so that the
+    clock and power state of the part (which drifts after a heavy shape under the
+    power cap) is shared by every arm instead of favouring whichever ran last."""
     import torch
 
     side = torch.cuda.Stream(dev)  # warm up on the capture stream: per-stream workspaces exist before capture
     side.wait_stream(torch.cuda.current_stream(dev))
     with torch.cuda.stream(side):
-        for f in fns:
-            f()
+        for fns in fn_lists:
+            for f in fns:
+                f()
     torch.cuda.synchronize()
-    g = torch.cuda.CUDAGraph()
-    with torch.cuda.graph(g, stream=side):
-        for i in range(launches):
-            fns[i % len(fns)]()
+    graphs = []
+    for fns in fn_lists:
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=side):
+            for i in range(launches):
+                fns[i % len(fns)]()
+        graphs.append(g)
     for _ in range(3):
-        g.replay()
+        for g in graphs:
+            g.replay()
     torch.cuda.synchronize()
-    times = []
+    times = [[] for _ in graphs]
     for _ in range(iters):
-        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        a.record()
-        g.replay()
-        b.record()
-        b.synchronize()
-        times.append(a.elapsed_time(b) / launches)
-    del g
-    return statistics.median(times)
+        for g, ts in zip(graphs, times):
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            g.replay()
+            b.record()
+            b.synchronize()
+            ts.append(a.elapsed_time(b) / launches)
+    del graphs
+    return [statistics.median(ts) for ts in times]
 
 
 def _copies_for(nbytes, floor=3, l2_multiple=3.0):
@@ -723,8 +737,7 @@ def _config_c3(steps):
                for x, _, tabs in copies]
     fused = [lambda x=x, tabs=tabs: segmented_branch.segmented_linear_varlen(x, w, None, *tabs, c.r_max)
              for x, _, tabs in copies]
-    ms_unfused = _time_chain(unfused, max(steps, 10), dev)
-    ms_fused = _time_chain(fused, max(steps, 10), dev)
+    ms_unfused, ms_fused = _time_chains([unfused, fused], max(steps, 10), dev)
     got = fused[0]()
     rep_f = checks.seg_linear_report(got, x, w, None, tabs[0], tabs[1], c.offsets, c.ranks, c.token_ids())
     flops_f = flops + 2.0 * c.x.shape[0] * c.x.shape[1] * c.w.shape[0]
@@ -823,7 +836,7 @@ def _config_gate(steps):
                    torch.empty((m, n), device=dev, dtype=bf)) for _ in range(_copies_for(nbytes))]
         ours = [lambda c=c: kernels.gemm(c[0], c[1], out=c[2]) for c in copies]
         ref = [lambda c=c: torch.matmul(c[0], c[1].t(), out=c[2]) for c in copies]
-        ms_ours, ms_ref = _time_chain(ours, max(steps, 10), dev), _time_chain(ref, max(steps, 10), dev)
+        ms_ours, ms_ref = _time_chains([ours, ref], max(steps, 10), dev)
         x, w, o = copies[0]
         got = kernels.gemm(x, w)
         want = torch.matmul(x, w.t())

@@ -40,6 +40,7 @@
 // Reference semantics: ragged_branch.py:6-40 (per-token shrink / expand,
 // rank-0 skip), segmented_branch.py:12-60, multilora.py:128-182, :295-347.
 #include <algorithm>
+#include <cstdlib>
 #include <type_traits>
 
 #include "common.cuh"
@@ -445,27 +446,41 @@ __global__ void __launch_bounds__(256) sgmv_reduce_kernel(const RedArgs p) {
 // =================================================================== expand
 namespace {
 
-constexpr int kExDrainWarps = 8;  // warps 0..7 drain (two per TMEM lane quadrant)
-constexpr int kExProducer = 8;
-constexpr int kExIssuer = 9;
-constexpr int kExThreads = 320;
+// Warps: eight drain warps on TMEM lane quadrants 0 and 1 (the accumulator's
+// 64 token rows), the TMA producer, the MMA issuer; warps 6, 7, 10 and 11
+// have no role (a warp may only read the lane quadrant warp_id % 4).
+constexpr int kExDrainWarps = 8;
+constexpr int kExProducer = 2;
+constexpr int kExIssuer = 3;
+constexpr int kExThreads = 14 * 32;
 constexpr int kExBN = 256;        // output columns per unit
 constexpr int kExZW = 64;         // z_hl: [T, 2 * 64] (hi | lo), r_max <= 64
-constexpr int kExSlots = 8;       // units in flight at most
-constexpr int kExRing = 208 * 1024;
-constexpr int kExOffBar = kExRing;
-constexpr int kExSmem = kExOffBar + 256 + 1024;
+constexpr int kExSlots = 12;      // units in flight at most
+constexpr int kExGroup = 2;       // column chunks of one tile walked together (one z load), default
+// Shared memory: [identity 8 KB][z buffer 0][z buffer 1][stage ring][barriers].
+// An M = 128 operand read from the identity or a z buffer spans 16 KB: its
+// rows 64..127 are whatever follows (never drained), always inside the block.
+constexpr int kExOffId = 0;                          // 64 x 64 identity, K-major, 128-byte swizzle
+constexpr int kExZBytes = 2 * 64 * 128;              // one z buffer: 64 token rows of hi, then of lo
+constexpr int kExOffZ = 64 * 128;
+constexpr int kExOffRing = kExOffZ + 2 * kExZBytes;
+constexpr int kExRing = 184 * 1024;
+constexpr int kExOffBar = kExOffRing + kExRing;
+constexpr int kExSmem = kExOffBar + 512 + 1024;
 constexpr uint32_t kExTmemCols = 2 * kExBN;
 
-// A unit's stage: [B rows: 4 chunks x r16 x 128 B]
-// [z: hi rows | hi rows again | lo rows | lo rows again, 64 x 128 B each]
-// [y: 4 chunks x n16 x 128 B], packed into a ring in unit order (a stage that
-// would cross the end starts at 0).  The z rows are loaded twice so that
-// operand rows 0..63 and 64..127 both hold the tile's tokens: the accumulator
-// then has every token in two TMEM lane quadrants and all four quadrants'
-// drain warps have work.  The producer places, the MMA issuer and the drain
-// recompute the same offsets; the drain frees a stage once it has read its y
-// and its accumulator.
+__device__ __forceinline__ int ex_drain_index(int warp) {  // -1: not a drain warp
+  return ((warp & 3) < 2 && warp < 14) ? (warp >> 2) * 2 + (warp & 1) : -1;
+}
+
+// A unit's stage: [B rows: 4 chunks x r16 x 128 B][y: 4 chunks x n16 x 128 B],
+// packed into a ring in unit order (a stage that would cross the end starts
+// at 0).  The producer places, the MMA issuer recomputes the same offsets; the
+// drain frees a stage once the unit's MMAs (which read all of it) have
+// completed.  z is not part of a stage: CTAs stride over groups of kExGroup
+// consecutive column chunks of a tile, and a group's z rows are loaded once
+// into one of two z buffers.  Neighbouring CTAs take neighbouring groups, so
+// the CTAs in flight cover whole rows of y and out.
 struct ExRing {
   uint32_t head = 0;
   __device__ uint32_t place(uint32_t size, uint32_t& footprint) {
@@ -478,7 +493,7 @@ struct ExRing {
 };
 
 __device__ __forceinline__ uint32_t ex_stage_bytes(int r16, int n16) {
-  return static_cast<uint32_t>((4 * r16 + 256 + 4 * n16) * 128);
+  return static_cast<uint32_t>((4 * r16 + 4 * n16) * 128);
 }
 
 struct ExMaps {
@@ -495,7 +510,7 @@ struct ExArgs {
   const int32_t* tiles;
   int* err;
   int64_t ldo, ldy;
-  int T, N, R, n_chunks;
+  int T, N, R, n_chunks, group;
 };
 
 // Shared-memory descriptor of an MN-major operand written by TMA as 64-element
@@ -513,24 +528,35 @@ __device__ __forceinline__ uint64_t umma_desc_sw128_mn(uint32_t smem_addr, uint3
 
 }  // namespace
 
+// Per unit, with the tile's tokens as the M = 128 rows (rows 64..127 unused):
+//   D[tok, col] = sum_j z_hi[tok, j] B[off + j, col] + sum_j z_lo[tok, j] B[off + j, col]
+//               + sum_k I[tok, k] y[k, col]
+// A = the z rows or a 64 x 64 identity (K-major), B = the adapter's B rows or
+// the tile's y rows (MN-major, straight from the TMA chunk boxes), N = 256.
+// The identity pass adds y exactly (one nonzero product per output), so the
+// drain only converts and stores.
 template <typename T>
 __global__ void __launch_bounds__(kExThreads, 1) sgmv_expand_unit_kernel(const __grid_constant__ ExMaps maps,
                                                                          const ExArgs p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
-  if (static_cast<uint32_t>(smem - smem_raw) + static_cast<uint32_t>(kExOffBar) + 256u > dynamic_smem_bytes()) {
+  if (static_cast<uint32_t>(smem - smem_raw) + static_cast<uint32_t>(kExOffBar) + 512u > dynamic_smem_bytes()) {
     if (threadIdx.x == 0) record_error(p.err, kDevErrSmemLayout);
     return;
   }
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kExOffBar);  // B rows, z, y of a stage landed
-  uint64_t* freed = full + kExSlots;                               // the drain is done with a stage
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kExOffBar);  // B rows and y of a stage landed
+  uint64_t* freed = full + kExSlots;                               // the unit's MMAs are done, stage reusable
   uint64_t* afull = freed + kExSlots;
   uint64_t* aempty = afull + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(aempty + 2);
+  uint64_t* zfull = aempty + 2;
+  uint64_t* zfree = zfull + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(zfree + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  uint8_t* ring_base = smem + kExOffRing;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int dw = ex_drain_index(warp);
   const bool has_y = p.y != nullptr;
   if (threadIdx.x == 0) {
     for (int b = 0; b < kExSlots; ++b) {
@@ -540,9 +566,22 @@ __global__ void __launch_bounds__(kExThreads, 1) sgmv_expand_unit_kernel(const _
     for (int b = 0; b < 2; ++b) {
       mbar_init(&afull[b], 1);
       mbar_init(&aempty[b], kExDrainWarps);
+      mbar_init(&zfull[b], 1);
+      mbar_init(&zfree[b], 1);
     }
     *abort_flag = 0;
     fence_mbar_init();
+  }
+  if (dw >= 0) {
+    // identity rows: row t holds 1 at K = t (16-byte granule t / 8, swizzled by t % 8)
+    const uint32_t one_lo = pack2<T>(1.f, 0.f), one_hi = pack2<T>(0.f, 1.f);
+    for (int g = dw * 32 + lane; g < 64 * 8; g += kExDrainWarps * 32) {
+      const int t = g >> 3, logical = (g & 7) ^ (t & 7);
+      uint32_t w[4] = {0u, 0u, 0u, 0u};
+      if (logical == (t >> 3)) w[(t & 7) >> 1] = (t & 1) ? one_hi : one_lo;
+      *reinterpret_cast<uint4*>(smem + kExOffId + g * 16) = make_uint4(w[0], w[1], w[2], w[3]);
+    }
+    fence_proxy_async_smem();
   }
   if (warp == kExProducer && lane == 0) {
     tma_prefetch_desc(&maps.z);
@@ -563,149 +602,172 @@ __global__ void __launch_bounds__(kExThreads, 1) sgmv_expand_unit_kernel(const _
   // z_hl comes from the reduce launched just before: wait before any global read.
   pdl_wait();
   if (threadIdx.x == 0) pdl_launch_dependents();
-  const int n_units = sgmv_num_tiles(p.tiles) * p.n_chunks;
+  const int gpt = (p.n_chunks + p.group - 1) / p.group;  // groups per tile
+  const int n_groups = sgmv_num_tiles(p.tiles) * gpt;
 
   if (warp == kExProducer) {
     // ------------------------------------------------------------ producer
-    UnitWalk walk(blockIdx.x, gridDim.x, n_units, p.n_chunks, lane);
+    UnitWalk walk(blockIdx.x, gridDim.x, n_groups, gpt, lane);
     TileInfo u;
-    int chunk, issued = 0, released = 0;
+    int grp, issued = 0, released = 0, runs = 0;
     uint32_t freed_bytes = 0;
     uint32_t foot[kExSlots];
     ExRing ring;
     bool ok = true;
-    while (ok && walk.next(p, u, chunk)) {
+    while (ok && walk.next(p, u, grp)) {
       if (u.ntok <= 0 || u.r <= 0) continue;
       const int r16 = (u.r + 15) & ~15, n16 = (u.ntok + 15) & ~15;
-      const int c0 = chunk * (kExBN / 64);  // first 64-column chunk of the unit
-      uint32_t footprint;
-      const uint32_t start = ring.place(ex_stage_bytes(r16, n16), footprint);
-      if (lane == 0) {
-        while (ok && (issued - released == kExSlots || ring.head - freed_bytes > static_cast<uint32_t>(kExRing))) {
-          const int rs = released % kExSlots;
-          ok = mbar_wait_bounded(&freed[rs], static_cast<uint32_t>((released / kExSlots) & 1), abort_flag, p.err,
-                                 kDevErrTimeoutEmpty);
-          freed_bytes += foot[rs];
-          ++released;
-        }
+      if (lane == 0) {  // the tile's z rows, once per group (the buffer's group before last has finished its MMAs)
+        const int zb = runs & 1;
+        ok = mbar_wait_bounded(&zfree[zb], static_cast<uint32_t>(((runs >> 1) & 1) ^ 1), abort_flag, p.err,
+                               kDevErrTimeoutEmpty);
         if (ok) {
-          const int s = issued % kExSlots;
-          foot[s] = footprint;
-          uint8_t* st = smem + start;
-          uint8_t* zs = st + 4 * r16 * 128;
-          mbar_arrive_expect_tx(&full[s], (4 * r16 + 256 + (has_y ? 4 * n16 : 0)) * 128);
-          tma_load_3d(&maps.b[(r16 >> 4) - 1], st, &full[s], 0, static_cast<int32_t>(u.arow), c0);
-          for (int q = 0; q < 4; ++q)  // hi, hi, lo, lo
-            tma_load_2d(&maps.z, zs + q * 64 * 128, &full[s], (q >> 1) * kExZW, u.ts);
-          if (has_y) tma_load_3d(&maps.y[(n16 >> 4) - 1], zs + 256 * 128, &full[s], 0, u.ts, c0);
+          uint8_t* zs = smem + kExOffZ + zb * kExZBytes;
+          mbar_arrive_expect_tx(&zfull[zb], kExZBytes);
+          tma_load_2d(&maps.z, zs, &zfull[zb], 0, u.ts);                // hi
+          tma_load_2d(&maps.z, zs + 64 * 128, &zfull[zb], kExZW, u.ts);  // lo
         }
       }
-      ++issued;
+      ++runs;
+      const int c_end = min(p.n_chunks, (grp + 1) * p.group);
+      for (int chunk = grp * p.group; ok && chunk < c_end; ++chunk) {
+        uint32_t footprint;
+        const uint32_t start = ring.place(ex_stage_bytes(r16, n16), footprint);
+        if (lane == 0) {
+          while (ok && (issued - released == kExSlots || ring.head - freed_bytes > static_cast<uint32_t>(kExRing))) {
+            const int rs = released % kExSlots;
+            ok = mbar_wait_bounded(&freed[rs], static_cast<uint32_t>((released / kExSlots) & 1), abort_flag, p.err,
+                                   kDevErrTimeoutEmpty);
+            freed_bytes += foot[rs];
+            ++released;
+          }
+          if (ok) {
+            const int s = issued % kExSlots;
+            const int c0 = chunk * (kExBN / 64);  // first 64-column chunk of the unit
+            foot[s] = footprint;
+            uint8_t* st = ring_base + start;
+            mbar_arrive_expect_tx(&full[s], (4 * r16 + (has_y ? 4 * n16 : 0)) * 128);
+            tma_load_3d(&maps.b[(r16 >> 4) - 1], st, &full[s], 0, static_cast<int32_t>(u.arow), c0);
+            if (has_y) tma_load_3d(&maps.y[(n16 >> 4) - 1], st + 4 * r16 * 128, &full[s], 0, u.ts, c0);
+          }
+        }
+        ++issued;
+        ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+      }
       ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
     }
   } else if (warp == kExIssuer) {
     // ---------------------------------------------------------- MMA issuer
-    UnitWalk walk(blockIdx.x, gridDim.x, n_units, p.n_chunks, lane);
+    UnitWalk walk(blockIdx.x, gridDim.x, n_groups, gpt, lane);
     TileInfo u;
-    int chunk, i = 0;
+    int grp, i = 0, runs = 0;
     ExRing ring;
     bool ok = true;
-    // M = 128, N = 256, A (z) K-major, B (adapter rows) MN-major (transpose-B bit 16)
+    // M = 128 (tokens), N = 256 columns; A K-major, B MN-major (transpose-B bit 16)
     const uint32_t idesc = umma_idesc_f16(128, kExBN, std::is_same<T, __nv_bfloat16>::value ? 1 : 0) | (1u << 16);
-    while (ok && walk.next(p, u, chunk)) {
+    const uint32_t zbase = smem_u32(smem + kExOffZ), ring_u32 = smem_u32(ring_base);
+    const uint64_t id_desc = umma_desc_sw128(smem_u32(smem + kExOffId));
+    while (ok && walk.next(p, u, grp)) {
       if (u.ntok <= 0 || u.r <= 0) continue;
       const int r16 = (u.r + 15) & ~15, n16 = (u.ntok + 15) & ~15;
-      uint32_t footprint;
-      const uint32_t start = ring.place(ex_stage_bytes(r16, n16), footprint);
-      const int s = i % kExSlots, buf = i & 1;
-      const uint32_t ph = static_cast<uint32_t>((i / kExSlots) & 1), aph = static_cast<uint32_t>((i >> 1) & 1);
-      ++i;
+      const int zb = runs & 1;
       if (lane == 0) {
-        ok = mbar_wait_bounded(&full[s], ph, abort_flag, p.err, kDevErrTimeoutFull) &&
-             mbar_wait_bounded(&aempty[buf], aph ^ 1, abort_flag, p.err, kDevErrTimeoutAccEmpty);
-        if (ok) {
-          tc_fence_after();
-          const uint32_t d = tmem_base + static_cast<uint32_t>(buf * kExBN);
-          const uint32_t bs = smem_u32(smem + start);
-          const uint32_t zs = bs + static_cast<uint32_t>(4 * r16 * 128);
-          for (int h = 0; h < 2; ++h) {  // hi, then lo: 128 operand rows = the tile's tokens twice
-            const uint64_t ad = umma_desc_sw128(zs + static_cast<uint32_t>(h * 128 * 128));
-            for (int ks = 0; ks < r16 / 16; ++ks) {
-              const uint64_t bd = umma_desc_sw128_mn(bs + static_cast<uint32_t>(ks * 2048),
-                                                     static_cast<uint32_t>(r16 * 128));
-              tc_mma_f16(d, ad + static_cast<uint64_t>(2 * ks), bd, idesc, (h > 0 || ks > 0) ? 1u : 0u);
-            }
-          }
-          tc_commit(&afull[buf]);
-        }
+        if (runs > 0) tc_commit(&zfree[zb ^ 1]);  // every MMA of the previous group is issued
+        ok = mbar_wait_bounded(&zfull[zb], static_cast<uint32_t>((runs >> 1) & 1), abort_flag, p.err,
+                               kDevErrTimeoutFull);
       }
+      ++runs;
       ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+      const uint32_t zs = zbase + static_cast<uint32_t>(zb * kExZBytes);
+      const int c_end = min(p.n_chunks, (grp + 1) * p.group);
+      for (int chunk = grp * p.group; ok && chunk < c_end; ++chunk) {
+        uint32_t footprint;
+        const uint32_t start = ring.place(ex_stage_bytes(r16, n16), footprint);
+        const int s = i % kExSlots, buf = i & 1;
+        const uint32_t ph = static_cast<uint32_t>((i / kExSlots) & 1), aph = static_cast<uint32_t>((i >> 1) & 1);
+        ++i;
+        if (lane == 0) {
+          ok = mbar_wait_bounded(&full[s], ph, abort_flag, p.err, kDevErrTimeoutFull) &&
+               mbar_wait_bounded(&aempty[buf], aph ^ 1, abort_flag, p.err, kDevErrTimeoutAccEmpty);
+          if (ok) {
+            tc_fence_after();
+            const uint32_t d = tmem_base + static_cast<uint32_t>(buf * kExBN);
+            const uint32_t bs = ring_u32 + start;
+            for (int part = 0; part < 2; ++part) {  // z hi, then z lo
+              const uint64_t zd = umma_desc_sw128(zs + static_cast<uint32_t>(part * 64 * 128));
+              for (int ks = 0; ks < r16 / 16; ++ks)
+                tc_mma_f16(d, zd + static_cast<uint64_t>(2 * ks),
+                           umma_desc_sw128_mn(bs + static_cast<uint32_t>(ks * 2048), static_cast<uint32_t>(r16 * 128)),
+                           idesc, (part > 0 || ks > 0) ? 1u : 0u);
+            }
+            if (has_y) {  // + y: identity x the tile's y rows (K = its tokens)
+              const uint32_t ys = bs + static_cast<uint32_t>(4 * r16 * 128);
+              for (int ks = 0; ks < n16 / 16; ++ks)
+                tc_mma_f16(d, id_desc + static_cast<uint64_t>(2 * ks),
+                           umma_desc_sw128_mn(ys + static_cast<uint32_t>(ks * 2048), static_cast<uint32_t>(n16 * 128)),
+                           idesc, 1u);
+            }
+            tc_commit(&afull[buf]);
+          }
+        }
+        ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+      }
     }
-  } else {
-    // ------------------------------------------------ drain (warps 0..7)
-    const int quad = warp & 3;                            // TMEM lane quadrant this warp may read
-    const int t = (quad * 32 + lane) & 63;                // lanes 64..127 hold tokens 0..63 again
-    const int cb = (quad >> 1) * 128 + (warp >> 2) * 64;  // this warp's 64-column chunk of the unit
-    UnitWalk walk(blockIdx.x, gridDim.x, n_units, p.n_chunks, lane);
+  } else if (dw >= 0) {
+    // ------------------------------------------------ drain (8 warps)
+    const int quad = dw & 1;        // == warp % 4: TMEM lanes quad*32.. hold tokens quad*32..
+    const int cb = (dw >> 1) * 64;  // this warp's 64-column block of the unit
+    const int t = quad * 32 + lane;
+    UnitWalk walk(blockIdx.x, gridDim.x, n_groups, gpt, lane);
     TileInfo u;
-    int chunk, i = 0;
-    ExRing ring;
+    int grp, i = 0;
     bool ok = true;
-    while (walk.next(p, u, chunk)) {
-      const int n0 = chunk * kExBN;
+    while (walk.next(p, u, grp)) {
+      const int c_end = min(p.n_chunks, (grp + 1) * p.group);
       if (u.ntok <= 0 || u.r <= 0) {
-        // rank 0 / unknown adapter: out = y (zeros without y); warp covers 32 tokens x 64 columns
-        for (int rr = 0; rr < 32; ++rr) {
-          const int tt = (quad & 1) * 32 + rr;
-          if (tt >= u.ntok) break;
-          const int col = n0 + cb + lane * 2;
-          if (col >= p.N) continue;  // N is a multiple of 64
-          T* o = static_cast<T*>(p.out) + static_cast<int64_t>(u.ts + tt) * p.ldo + col;
-          const T* yy = has_y ? static_cast<const T*>(p.y) + static_cast<int64_t>(u.ts + tt) * p.ldy + col : nullptr;
-          *reinterpret_cast<uint32_t*>(o) = has_y ? *reinterpret_cast<const uint32_t*>(yy) : 0u;
+        // rank 0 / unknown adapter: out = y (zeros without y); warp dw copies tokens dw, dw + 8, ...
+        for (int tt = dw; tt < u.ntok; tt += kExDrainWarps) {
+          for (int col = grp * p.group * kExBN + lane * 2; col < c_end * kExBN && col < p.N; col += 64) {
+            T* o = static_cast<T*>(p.out) + static_cast<int64_t>(u.ts + tt) * p.ldo + col;
+            const T* yy = has_y ? static_cast<const T*>(p.y) + static_cast<int64_t>(u.ts + tt) * p.ldy + col : nullptr;
+            *reinterpret_cast<uint32_t*>(o) = has_y ? *reinterpret_cast<const uint32_t*>(yy) : 0u;
+          }
         }
         continue;
       }
-      const int r16 = (u.r + 15) & ~15, n16 = (u.ntok + 15) & ~15;
-      uint32_t footprint;
-      const uint32_t start = ring.place(ex_stage_bytes(r16, n16), footprint);
-      const int s = i % kExSlots, buf = i & 1;
-      const uint32_t ph = static_cast<uint32_t>((i / kExSlots) & 1), aph = static_cast<uint32_t>((i >> 1) & 1);
-      ++i;
-      if (ok) ok = mbar_wait_bounded(&afull[buf], aph, abort_flag, p.err, kDevErrTimeoutAccFull);
-      if (ok) ok = mbar_wait_bounded(&full[s], ph, abort_flag, p.err, kDevErrTimeoutFull);  // y landed
-      tc_fence_after();
-      __syncwarp();
-      if (ok) {
+      for (int chunk = grp * p.group; chunk < c_end; ++chunk) {
+        const int n0 = chunk * kExBN;
+        const int s = i % kExSlots, buf = i & 1;
+        const uint32_t aph = static_cast<uint32_t>((i >> 1) & 1);
+        ++i;
+        if (ok) ok = mbar_wait_bounded(&afull[buf], aph, abort_flag, p.err, kDevErrTimeoutAccFull);
+        tc_fence_after();
+        __syncwarp();
         uint32_t v[64];
-        const uint32_t ta =
-            tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + static_cast<uint32_t>(buf * kExBN + cb);
-        tmem_ld_32x32b_x32(ta, v);
-        tmem_ld_32x32b_x32(ta + 32, v + 32);
-        tmem_wait_ld();
-        if (t < u.ntok && n0 + cb < p.N) {  // N is a multiple of 64
-          const uint8_t* ys = smem + start + (4 * r16 + 256) * 128 + (cb >> 6) * n16 * 128 + t * 128;
+        if (ok) {
+          const uint32_t ta =
+              tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + static_cast<uint32_t>(buf * kExBN + cb);
+          tmem_ld_32x32b_x32(ta, v);
+          tmem_ld_32x32b_x32(ta + 32, v + 32);
+          tmem_wait_ld();
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) {  // accumulator read and the unit's MMAs done: both can be reused
+          mbar_arrive(&aempty[buf]);
+          mbar_arrive(&freed[s]);
+        }
+        if (ok && t < u.ntok && n0 + cb < p.N) {  // N is a multiple of 64
           T* orow = static_cast<T*>(p.out) + static_cast<int64_t>(u.ts + t) * p.ldo + n0 + cb;
 #pragma unroll
-          for (int c = 0; c < 8; ++c) {  // 8 columns (16 bytes) per step
-            uint4 yv = make_uint4(0u, 0u, 0u, 0u);
-            if (has_y) yv = *reinterpret_cast<const uint4*>(ys + ((c ^ (t & 7)) << 4));
-            const uint32_t* yw = reinterpret_cast<const uint32_t*>(&yv);
+          for (int c = 0; c < 8; ++c) {  // 8 columns (16 bytes) per store
             uint32_t ow[4];
 #pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              const float2 yf = unpack2<T>(yw[e]);
-              ow[e] = pack2<T>(yf.x + __uint_as_float(v[8 * c + 2 * e]), yf.y + __uint_as_float(v[8 * c + 2 * e + 1]));
-            }
+            for (int e = 0; e < 4; ++e)
+              ow[e] = pack2<T>(__uint_as_float(v[8 * c + 2 * e]), __uint_as_float(v[8 * c + 2 * e + 1]));
             *reinterpret_cast<uint4*>(orow + 8 * c) = make_uint4(ow[0], ow[1], ow[2], ow[3]);
           }
         }
-      }
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) {
-        mbar_arrive(&aempty[buf]);
-        mbar_arrive(&freed[s]);
       }
     }
   }
@@ -803,6 +865,17 @@ int launch_reduce(const float* partial, int S, int64_t T, int64_t RP, void* z, i
   return cudaLaunchKernelEx(&cfg, sgmv_reduce_kernel<__half>, r) == cudaSuccess ? LORA_OK : LORA_ERR_CUDA;
 }
 
+// Column chunks per expand group: LORA_B200_EX_GROUP overrides the default
+// (read once; tuning sweeps).
+int expand_group(int64_t n_chunks) {
+  static const int g = [] {
+    const char* v = std::getenv("LORA_B200_EX_GROUP");
+    const int parsed = v != nullptr ? std::atoi(v) : 0;
+    return parsed > 0 ? parsed : kExGroup;
+  }();
+  return static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(g, n_chunks)));
+}
+
 int launch_expand_units(const void* y, int64_t ldy, const void* z_hl, const void* b, int64_t b_rows, int64_t ldb,
                         const int64_t* offsets, const int64_t* ranks, const int32_t* tiles, int64_t max_tiles,
                         void* out, int64_t ldo, int64_t T, int64_t N, int64_t r_max, int dtype, int num_sms, int* err,
@@ -837,7 +910,9 @@ int launch_expand_units(const void* y, int64_t ldy, const void* z_hl, const void
   a.N = static_cast<int>(N);
   a.R = static_cast<int>(r_max);
   a.n_chunks = static_cast<int>(n_chunks);
-  const int grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(max_tiles * n_chunks, num_sms)));
+  a.group = expand_group(n_chunks);
+  const int64_t groups = max_tiles * ((n_chunks + a.group - 1) / a.group);
+  const int grid = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(groups, num_sms)));
   cudaLaunchAttribute attr[1];
   cudaLaunchConfig_t cfg = pdl_config(grid, kExThreads, kExSmem, stream, attr);
   if (dtype == LORA_BF16) {
