@@ -21,16 +21,19 @@
 //    order (results do not depend on timing) and writes z: fp32 or 16-bit
 //    [T, z_width], or, for the expand, the 16-bit pair
 //    hi = round(s.z), lo = round(s.z - hi) as [T, 2 W] (W = 64).
-// 3. Expand.  Work units = (tile, 256-column chunk).  The producer loads by
-//    TMA the adapter's B rows [r16 x 256] (rank-major table: an MN-major MMA
-//    operand) and the tile's y rows, each in ONE TMA operation (3-D chunk
-//    boxes: on B200 the operation count, not the bytes, limits a pipeline of
-//    small boxes), and the tile's [hi | lo] z rows twice, to operand rows
-//    0..63 and 64..127; one thread issues M = 128, N = 256 MMAs over
-//    K = r16 (hi) + r16 (lo) into a double-buffered accumulator (2 x 256
-//    TMEM columns) that holds every token in two lane quadrants; eight drain
-//    warps (two per quadrant, 64 columns each) add y from shared memory and
-//    store out with 16-byte stores.
+// 3. Expand.  Work units = (tile, 256-column chunk); CTAs stride over groups
+//    of two consecutive units of a tile.  The producer loads a group's
+//    [hi | lo] z rows once, into one of two z buffers, and for every unit the
+//    adapter's B rows [r16 x 256] (rank-major table: an MN-major MMA operand)
+//    and the tile's y rows, each in ONE TMA operation (3-D chunk boxes: on
+//    B200 the operation count, not the bytes, limits a pipeline of small
+//    boxes).  One thread issues M = 128 (the tile's tokens), N = 256 MMAs over
+//    K = r16 (hi) + r16 (lo), then adds y with an identity MMA (K = the tile's
+//    tokens, one nonzero product per output: exact), into a double-buffered
+//    accumulator (2 x 256 TMEM columns).  Eight drain warps on the two lane
+//    quadrants that hold the tokens convert and store out with 16-byte
+//    stores, releasing the accumulator and the stage as soon as they have
+//    read it.
 //    Tiles of rank 0 or with an unknown adapter copy y to out.
 //
 // Roles per CTA: one TMA producer warp, one warp that owns TMEM and issues the
