@@ -79,55 +79,10 @@ struct AdapterLookup {
   }
 };
 
-}  // namespace
-
-__global__ void __launch_bounds__(1024) sgmv_schedule_kernel(AdapterLookup look, int32_t* tiles, int max_tiles) {
-  __shared__ int warp_sum[32];
-  __shared__ int s_start[kSchedSmemSegs + 1];
-  __shared__ int s_adapter[kSchedSmemSegs];
-  const int tid = threadIdx.x, nth = blockDim.x;
-  const int lane = tid & 31, warp = tid >> 5, nwarps = nth >> 5;
-  const int T = look.T;
-  // Launched with programmatic serialization: the segment table (and the tile
-  // buffer, which the kernel before may still read) wait for that kernel.  The
-  // segmented shrink launched next may set up (barriers, TMEM) meanwhile; it
-  // waits for this grid before reading the table.
-  pdl_wait();
-  if (tid == 0) pdl_launch_dependents();
-  if (look.ids == nullptr && look.S <= kSchedSmemSegs) {
-    for (int i = tid; i <= look.S; i += nth) {
-      s_start[i] = clamp_start(look.seg_start[i], T);
-      if (i < look.S) {
-        const int64_t a = look.seg_adapter[i];
-        s_adapter[i] = (a < 0 || a >= look.n_adapters) ? -1 : static_cast<int>(a);
-      }
-    }
-    look.s_start = s_start;
-    look.s_adapter = s_adapter;
-  }
-  __syncthreads();
-  const int chunk = (T + nth - 1) / nth;
-  const int c0 = min(T, tid * chunk), c1 = min(T, c0 + chunk);
-
-  int seg = -1;
-  if (look.ids == nullptr && c0 < c1) seg = look.find_segment(c0 > 0 ? c0 - 1 : 0);
-  int prev = -2;
-  if (c0 > 0 && c0 < c1) {
-    int s2 = seg;
-    prev = look(c0 - 1, s2);
-    seg = s2;
-  }
-  int count = 0;
-  {
-    int s = seg, pv = prev;
-    for (int t = c0; t < c1; ++t) {
-      const int a = look(t, s);
-      if ((t % kSgmvTileTokens) == 0 || a != pv) ++count;
-      pv = a;
-    }
-  }
-  // exclusive scan of the counts: within each warp by shuffles, then over the
-  // warp totals by warp 0 (two block barriers)
+// Exclusive prefix sum of `count` over the block, in thread order; `total`
+// receives the sum.  Two block barriers; every thread of the block calls it.
+__device__ int block_exclusive_scan(int count, int* warp_sum, int& total) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nwarps = blockDim.x >> 5;
   int incl = count;
 #pragma unroll
   for (int off = 1; off < 32; off <<= 1) {
@@ -146,23 +101,128 @@ __global__ void __launch_bounds__(1024) sgmv_schedule_kernel(AdapterLookup look,
     warp_sum[lane] = w;  // inclusive over warps
   }
   __syncthreads();
-  const int total = warp_sum[nwarps - 1];
-  int base = incl - count + (warp > 0 ? warp_sum[warp - 1] : 0);
-  int32_t* starts = tiles + 2;
-  int32_t* adapters = tiles + 3 + max_tiles;
-  int32_t* block_first = tiles + 3 + 2 * max_tiles;
-  {
+  total = warp_sum[nwarps - 1];
+  return incl - count + (warp > 0 ? warp_sum[warp - 1] : 0);
+}
+
+// Segment i of a table that covers [0, T) in order: its tokens [a, b), its
+// adapter (-1 if out of range) and whether a tile starts at a (a is a
+// multiple of 64, or the token before it -- in the last non-empty segment
+// before i -- has another adapter).  Tiles also start at every multiple of 64
+// inside (a, b).
+struct SegTiles {
+  int a, b, ad;
+  bool first;
+  __device__ int count() const {
+    return b > a ? (first ? 1 : 0) + (b - 1) / kSgmvTileTokens - a / kSgmvTileTokens : 0;
+  }
+};
+
+__device__ SegTiles seg_tiles(int i, const int* s_start, const int* s_adapter) {
+  SegTiles g{s_start[i], s_start[i + 1], s_adapter[i], false};
+  if (g.b > g.a) {
+    if (g.a % kSgmvTileTokens == 0) {
+      g.first = true;
+    } else {
+      int j = i - 1;
+      while (j >= 0 && s_start[j] == g.a) --j;  // skip empty segments
+      g.first = j < 0 || s_adapter[j] != g.ad;
+    }
+  }
+  return g;
+}
+
+// One tile entry: start token t, adapter ad, index idx (entries past
+// max_tiles are counted but not stored).
+__device__ __forceinline__ void put_tile(int32_t* tiles, int max_tiles, int idx, int t, int ad) {
+  if (t % kSgmvTileTokens == 0) tiles[3 + 2 * max_tiles + t / kSgmvTileTokens] = min(idx, max_tiles);
+  if (idx < max_tiles) {
+    tiles[2 + idx] = t;
+    tiles[3 + max_tiles + idx] = ad;
+  }
+}
+
+}  // namespace
+
+__global__ void __launch_bounds__(1024) sgmv_schedule_kernel(AdapterLookup look, int32_t* tiles, int max_tiles) {
+  __shared__ int warp_sum[32];
+  __shared__ int s_start[kSchedSmemSegs + 1];
+  __shared__ int s_adapter[kSchedSmemSegs];
+  const int tid = threadIdx.x, nth = blockDim.x;
+  const int T = look.T;
+  // Launched with programmatic serialization: the segment table (and the tile
+  // buffer, which the kernel before may still read) wait for that kernel.  The
+  // segmented shrink launched next may set up (barriers, TMEM) meanwhile; it
+  // waits for this grid before reading the table.
+  pdl_wait();
+  if (tid == 0) pdl_launch_dependents();
+  const bool staged = look.ids == nullptr && look.S <= kSchedSmemSegs;
+  if (staged) {
+    for (int i = tid; i <= look.S; i += nth) {
+      s_start[i] = clamp_start(look.seg_start[i], T);
+      if (i < look.S) {
+        const int64_t a = look.seg_adapter[i];
+        s_adapter[i] = (a < 0 || a >= look.n_adapters) ? -1 : static_cast<int>(a);
+      }
+    }
+    look.s_start = s_start;
+    look.s_adapter = s_adapter;
+  }
+  __syncthreads();
+  // A staged table that covers [0, T) in order (the usual serving batch) is
+  // tiled segment by segment: O(S) work instead of a walk over every token.
+  bool by_segment = false;
+  if (staged) {
+    int ordered = 1;
+    for (int i = tid; i < look.S; i += nth) ordered &= s_start[i] <= s_start[i + 1] ? 1 : 0;
+    if (tid == 0) ordered &= (s_start[0] == 0 && s_start[look.S] == T) ? 1 : 0;
+    by_segment = __syncthreads_and(ordered) != 0;
+  }
+  int total = 0;
+  if (by_segment) {
+    const int per = (look.S + nth - 1) / nth;  // contiguous segments per thread, in order
+    const int s0 = min(look.S, tid * per), s1 = min(look.S, s0 + per);
+    int count = 0;
+    for (int i = s0; i < s1; ++i) {
+      const SegTiles g = seg_tiles(i, s_start, s_adapter);
+      if (g.b > g.a && g.ad < 0) record_error(look.err, kDevErrBadIndex);
+      count += g.count();
+    }
+    int idx = block_exclusive_scan(count, warp_sum, total);
+    for (int i = s0; i < s1; ++i) {
+      const SegTiles g = seg_tiles(i, s_start, s_adapter);
+      if (g.b <= g.a) continue;
+      if (g.first) put_tile(tiles, max_tiles, idx++, g.a, g.ad);
+      for (int m = (g.a / kSgmvTileTokens + 1) * kSgmvTileTokens; m < g.b; m += kSgmvTileTokens)
+        put_tile(tiles, max_tiles, idx++, m, g.ad);
+    }
+  } else {
+    // token by token: per-token ids, or a table with gaps, overlaps or more
+    // than kSchedSmemSegs entries
+    const int chunk = (T + nth - 1) / nth;
+    const int c0 = min(T, tid * chunk), c1 = min(T, c0 + chunk);
+    int seg = -1;
+    if (look.ids == nullptr && c0 < c1) seg = look.find_segment(c0 > 0 ? c0 - 1 : 0);
+    int prev = -2;
+    if (c0 > 0 && c0 < c1) {
+      int s2 = seg;
+      prev = look(c0 - 1, s2);
+      seg = s2;
+    }
+    int count = 0;
+    {
+      int s = seg, pv = prev;
+      for (int t = c0; t < c1; ++t) {
+        const int a = look(t, s);
+        if ((t % kSgmvTileTokens) == 0 || a != pv) ++count;
+        pv = a;
+      }
+    }
+    int idx = block_exclusive_scan(count, warp_sum, total);
     int s = seg, pv = prev;
     for (int t = c0; t < c1; ++t) {
       const int a = look(t, s);
-      if ((t % kSgmvTileTokens) == 0 || a != pv) {
-        if ((t % kSgmvTileTokens) == 0) block_first[t / kSgmvTileTokens] = min(base, max_tiles);
-        if (base < max_tiles) {
-          starts[base] = t;
-          adapters[base] = a;
-        }
-        ++base;
-      }
+      if ((t % kSgmvTileTokens) == 0 || a != pv) put_tile(tiles, max_tiles, idx++, t, a);
       pv = a;
     }
   }
@@ -171,8 +231,8 @@ __global__ void __launch_bounds__(1024) sgmv_schedule_kernel(AdapterLookup look,
     if (total > max_tiles) record_error(look.err, kDevErrBadIndex);
     tiles[0] = n;
     tiles[1] = max_tiles;
-    starts[n] = T;
-    block_first[(T + kSgmvTileTokens - 1) / kSgmvTileTokens] = n;
+    tiles[2 + n] = T;
+    tiles[3 + 2 * max_tiles + (T + kSgmvTileTokens - 1) / kSgmvTileTokens] = n;
   }
 }
 

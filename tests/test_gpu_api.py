@@ -338,6 +338,50 @@ def test_schedule_matches_oracle():
     assert _lib.device_error() == 0
 
 
+def _schedule(tiles):
+    n, mt = int(tiles[0]), int(tiles[1])
+    return tiles[2:3 + n].tolist(), tiles[3 + mt:3 + mt + n].tolist(), tiles[3 + 2 * mt:].tolist()
+
+
+@pytest.mark.parametrize("seed", range(6))
+def test_schedule_segments_match_oracle(seed):
+    """Segment tables that cover the batch in order (tiled segment by segment on
+    the device): empty segments, neighbours with the same adapter, out-of-range
+    adapters, long segments, T not a multiple of 64.  Tile starts, adapters and
+    the first tile of every 64-token block match the oracle."""
+    rng = np.random.default_rng(seed)
+    t = int(rng.integers(1, 3000))
+    n_seg = int(rng.integers(1, 300))
+    seg_start = np.concatenate([[0], np.sort(rng.integers(0, t + 1, size=n_seg - 1)), [t]])
+    n_ad = 6
+    seg_ad = rng.integers(-1, n_ad + 1, size=n_seg)  # -1 and n_ad are out of range
+    seg_ad[rng.random(n_seg) < 0.3] = 2              # runs of neighbours sharing an adapter
+    tiles, _ = kernels.sgmv_schedule(t, n_ad, seg_start=torch.as_tensor(seg_start, device=DEV),
+                                     seg_adapter=torch.as_tensor(seg_ad, device=DEV))
+    starts, adapters, first = _schedule(tiles)
+    want_s, want_a = orc.tile_schedule(seg_start=seg_start.tolist(), seg_adapter=seg_ad.tolist(), n_adapters=n_ad)
+    assert starts == want_s and adapters == want_a
+    blocks = (t + 63) // 64
+    assert first[:blocks + 1] == [want_s.index(64 * b) for b in range(blocks)] + [len(want_a)]
+    bad = any((seg_ad[i] < 0 or seg_ad[i] >= n_ad) and seg_start[i + 1] > seg_start[i] for i in range(n_seg))
+    assert _lib.device_error() == (110 if bad else 0)
+
+
+def test_schedule_segments_with_gaps():
+    """A table that leaves tokens uncovered takes the token-by-token walk: those
+    tokens get no adapter (-1) and the error is recorded."""
+    seg_start = [5, 70, 200]
+    seg_ad = [1, 3]
+    t = 250
+    tiles, _ = kernels.sgmv_schedule(t, 4, seg_start=torch.tensor(seg_start, device=DEV),
+                                     seg_adapter=torch.tensor(seg_ad, device=DEV))
+    starts, adapters, _ = _schedule(tiles)
+    ids = [-1] * 5 + [1] * 65 + [3] * 130 + [-1] * 50
+    want_s, want_a = orc.tile_schedule(ids=ids, n_adapters=4)
+    assert starts == want_s and adapters == want_a
+    assert _lib.device_error() == 110
+
+
 def test_routing_bit_exact():
     """Exactly representable probe: out - y == adapter id + 1 for every token."""
     n_ad, k, n = 12, 64, 48
