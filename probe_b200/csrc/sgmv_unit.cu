@@ -786,15 +786,23 @@ __global__ void __launch_bounds__(kExThreads, 1) sgmv_expand_unit_kernel(const _
 // ===================================================================== host
 namespace {
 
-// K slices of the shrink: about four units per SM counting one tile per 64
-// tokens (the fewest any schedule of T tokens has), at least 4 k-blocks per
-// slice, at most 16 slices.  It depends on T and K only, so per-token ids
+// K slices of the shrink: about `per_sm` units per SM counting one tile per
+// 64 tokens (the fewest any schedule of T tokens has), at least 4 k-blocks
+// per slice, at most 16 slices.  It depends on T and K only, so per-token ids
 // and segment tables describing the same batch sum their partials alike and
 // give bit-identical results.
-int unit_slices(int64_t T, int64_t K, int num_sms) {
+// per_sm: 4 for the standalone shrink and the fused linear's slot fill;
+// 1 for the one-call branch, whose reduce and expand follow at once: fewer,
+// longer units keep more of a CTA's stages in flight and leave fewer partial
+// slices to sum (C3: 64.7 against 67.8 us per branch call; the fused linear
+// measured 158.2 against 155.4 us the other way round).
+constexpr int kUnitsPerSm = 4;
+constexpr int kBranchUnitsPerSm = 1;
+
+int unit_slices(int64_t T, int64_t K, int num_sms, int per_sm) {
   const int64_t kb = std::max<int64_t>((K + kUnitBK - 1) / kUnitBK, 1);
   const int64_t blocks = std::max<int64_t>((T + 63) / 64, 1);
-  int64_t s = (4 * static_cast<int64_t>(num_sms) + blocks - 1) / blocks;
+  int64_t s = (per_sm * static_cast<int64_t>(num_sms) + blocks - 1) / blocks;
   s = std::max<int64_t>(1, std::min<int64_t>({s, 16, std::max<int64_t>(kb / 4, 1)}));
   const int64_t per = ((kb + s - 1) / s + kShKC - 1) / kShKC * kShKC;
   return static_cast<int>((kb + per - 1) / per);
@@ -938,11 +946,16 @@ bool shrink_units_ok(const void* x, int64_t ldx, const void* a_flat, int64_t lda
   return T <= INT32_MAX / 2 && K <= INT32_MAX && max_tiles * 16 <= INT32_MAX;
 }
 
+// Bytes of the fp32 partials [S][T][rpad(r_max)], rounded up to 256.
+size_t partial_bytes(int S, int64_t T, int64_t r_max) {
+  return (static_cast<size_t>(S) * static_cast<size_t>(T) * static_cast<size_t>(rpad(r_max)) * sizeof(float) + 255) /
+         256 * 256;
+}
+
 }  // namespace
 
 size_t sgmv_unit_shrink_workspace(int64_t T, int64_t K, int64_t r_max, int64_t max_tiles, int num_sms) {
-  return static_cast<size_t>(unit_slices(T, K, num_sms)) * static_cast<size_t>(T) *
-         static_cast<size_t>(rpad(r_max)) * sizeof(float);
+  return partial_bytes(unit_slices(T, K, num_sms, kUnitsPerSm), T, r_max);
 }
 
 int launch_sgmv_shrink_unit(const void* x, int64_t ldx, const void* a_flat, int64_t lda, int64_t a_rows,
@@ -952,7 +965,7 @@ int launch_sgmv_shrink_unit(const void* x, int64_t ldx, const void* a_flat, int6
                             void* stream) {
   if (!shrink_units_ok(x, ldx, a_flat, lda, a_rows, T, K, r_max, max_tiles)) return LORA_ERR_UNSUPPORTED;
   if (z_dtype != LORA_F32 && z_dtype != dtype) return LORA_ERR_DTYPE;
-  const int S = unit_slices(T, K, num_sms);
+  const int S = unit_slices(T, K, num_sms, kUnitsPerSm);
   if (workspace == nullptr || !unit_al16(workspace) ||
       workspace_bytes < sgmv_unit_shrink_workspace(T, K, r_max, max_tiles, num_sms))
     return LORA_ERR_UNSUPPORTED;
@@ -965,8 +978,8 @@ int launch_sgmv_shrink_unit(const void* x, int64_t ldx, const void* a_flat, int6
 }
 
 size_t sgmv_unit_branch_workspace(int64_t T, int64_t K, int64_t r_max, int64_t max_tiles, int num_sms) {
-  const size_t part = (sgmv_unit_shrink_workspace(T, K, r_max, max_tiles, num_sms) + 255) / 256 * 256;
-  return part + static_cast<size_t>(T) * 2 * kExZW * 2;
+  return partial_bytes(unit_slices(T, K, num_sms, kBranchUnitsPerSm), T, r_max) +
+         static_cast<size_t>(T) * 2 * kExZW * 2;
 }
 
 int launch_sgmv_branch_unit(const void* x, int64_t ldx, const void* y, int64_t ldy, const void* a_flat, int64_t lda,
@@ -984,10 +997,9 @@ int launch_sgmv_branch_unit(const void* x, int64_t ldx, const void* y, int64_t l
   if (workspace == nullptr || !unit_al16(workspace) ||
       workspace_bytes < sgmv_unit_branch_workspace(T, K, r_max, max_tiles, num_sms))
     return LORA_ERR_UNSUPPORTED;
-  const int S = unit_slices(T, K, num_sms);
+  const int S = unit_slices(T, K, num_sms, kBranchUnitsPerSm);
   float* partial = static_cast<float*>(workspace);
-  const size_t part = (sgmv_unit_shrink_workspace(T, K, r_max, max_tiles, num_sms) + 255) / 256 * 256;
-  void* z_hl = static_cast<char*>(workspace) + part;
+  void* z_hl = static_cast<char*>(workspace) + partial_bytes(S, T, r_max);
   int rc = launch_shrink_units(x, ldx, a_flat, lda, a_rows, offsets, ranks, tiles, max_tiles, partial, T, K, r_max, S,
                                dtype, num_sms, err, stream);
   if (rc != LORA_OK) return rc;
@@ -997,7 +1009,7 @@ int launch_sgmv_branch_unit(const void* x, int64_t ldx, const void* y, int64_t l
                              r_max, dtype, num_sms, err, stream);
 }
 
-int sgmv_unit_slices(int64_t T, int64_t K, int num_sms) { return unit_slices(T, K, num_sms); }
+int sgmv_unit_slices(int64_t T, int64_t K, int num_sms) { return unit_slices(T, K, num_sms, kUnitsPerSm); }
 
 int launch_sgmv_shrink_partials(const void* x, int64_t ldx, const void* a_flat, int64_t lda, int64_t a_rows,
                                 const int64_t* offsets, const int64_t* ranks, const int32_t* tiles, int64_t max_tiles,
