@@ -8,9 +8,9 @@
 // Three kernels, chained with programmatic dependent launch:
 //
 // 1. Shrink.  Work units = (tile, K slice).  Every x row is read once per
-//    call and every adapter row once per tile; units are alike (~100 KB of
-//    operands) so persistent CTAs striding over them stay balanced whatever
-//    the segment lengths.  Swap-AB MMA: the adapter rows are the M = 128
+//    call and every adapter row once per tile; persistent CTAs take the units
+//    in a snake over a cost-sorted tile order (order_tiles), so they stay
+//    balanced whatever the segment lengths and ranks.  Swap-AB MMA: the adapter rows are the M = 128
 //    operand (only the first r16 rows are loaded; the other accumulator lanes
 //    are never read), the tile's tokens the N = 16..64 operand, both K-major
 //    tiles written by TMA with 128-byte swizzle; a double-buffered TMEM
@@ -21,8 +21,8 @@
 //    order (results do not depend on timing) and writes z: fp32 or 16-bit
 //    [T, z_width], or, for the expand, the 16-bit pair
 //    hi = round(s.z), lo = round(s.z - hi) as [T, 2 W] (W = 64).
-// 3. Expand.  Work units = (tile, 256-column chunk); CTAs stride over groups
-//    of two consecutive units of a tile.  The producer loads a group's
+// 3. Expand.  Work units = (tile, 256-column chunk); CTAs walk groups of two
+//    consecutive units of a tile.  The producer loads a group's
 //    [hi | lo] z rows once, into one of two z buffers, and for every unit the
 //    adapter's B rows [r16 x 256] (rank-major table: an MN-major MMA operand)
 //    and the tile's y rows, each in ONE TMA operation (3-D chunk boxes: on
@@ -127,21 +127,109 @@ __device__ __forceinline__ TileInfo read_tile(const int32_t* tiles, const int64_
   return ti;
 }
 
-// Walks this CTA's units u = first, first + stride, ... (< n); unit u is tile
-// u / per_tile, part u % per_tile.  Warp-collective (lane l prefetches the
-// tile of the (j + l)-th unit); every role walks the same sequence.
+// Unit order.  A unit's time is about its operand bytes, (r16 + n16) rows per
+// K chunk or column chunk, and tiles range from 16 to 128 such rows: striding
+// over the tiles in schedule order leaves the costliest CTA with ~1.4-1.7x the
+// mean on C3.  So every CTA first computes the same order of the tile list --
+// descending (r16 + n16), ties in schedule order: a stable counting sort by
+// warp ballots, in shared memory -- and takes its units in a snake over the
+// grid along that order (b, 2G-1-b, 2G+b, ...).  Which CTA runs a unit does not
+// change any result.  Past kOrderMax tiles the tiles keep schedule order.
+constexpr int kOrderMax = 1024;
+constexpr int kOrderKeys = 12;  // buckets 0..10: (r16 + n16) / 16 = 12..2 (r <= 128, <= 64 tokens); 11: no work
+constexpr int kOrderBytes = kOrderMax * 4 + kOrderMax + kOrderKeys * 33 * 4 + 16;  // order, keys, counters
+
+__device__ int tile_bucket(const int32_t* tiles, const int64_t* ranks, int i, int T, int R) {
+  const int ntok = min(sgmv_tile_start(tiles, i + 1), T) - sgmv_tile_start(tiles, i);
+  const int ad = sgmv_tile_adapter(tiles, i);
+  int r = 0;
+  if (ad >= 0) {
+    const int64_t rr = ranks[ad];
+    r = rr <= 0 ? 0 : static_cast<int>(rr < R ? rr : R);
+  }
+  if (ntok <= 0 || r <= 0) return kOrderKeys - 1;
+  const int b = 12 - ((r + 15) / 16 + (ntok + 15) / 16);
+  return b < 0 ? 0 : (b > kOrderKeys - 2 ? kOrderKeys - 2 : b);
+}
+
+// All threads of the block call it; returns the order (shared memory) or
+// nullptr past kOrderMax tiles.
+__device__ const int* order_tiles(const int32_t* tiles, const int64_t* ranks, int T, int R, uint8_t* region) {
+  const int n = sgmv_num_tiles(tiles);
+  if (n > kOrderMax) return nullptr;
+  int* order = reinterpret_cast<int*>(region);
+  uint8_t* key = region + kOrderMax * 4;
+  int* cursor = reinterpret_cast<int*>(region + kOrderMax * 5);  // [kOrderKeys], then [warp][kOrderKeys]
+  int* wc = cursor + kOrderKeys;
+  const int tid = threadIdx.x, nth = blockDim.x, lane = tid & 31, warp = tid >> 5, nwarps = nth >> 5;
+  if (tid < kOrderKeys) cursor[tid] = 0;
+  __syncthreads();
+  for (int i = tid; i < n; i += nth) {
+    const int b = tile_bucket(tiles, ranks, i, T, R);
+    key[i] = static_cast<uint8_t>(b);
+    atomicAdd(&cursor[b], 1);
+  }
+  __syncthreads();
+  if (tid == 0) {
+    int acc = 0;
+    for (int b = 0; b < kOrderKeys; ++b) {
+      const int c = cursor[b];
+      cursor[b] = acc;
+      acc += c;
+    }
+  }
+  __syncthreads();
+  for (int base = 0; base < n; base += nth) {  // stable placement, one block-wide chunk at a time
+    const int i = base + tid;
+    const int b = i < n ? key[i] : -1;
+    int below = 0;
+    for (int k = 0; k < kOrderKeys; ++k) {
+      const unsigned m = __ballot_sync(0xffffffffu, b == k);
+      if (b == k) below = __popc(m & ((1u << lane) - 1u));
+      if (lane == 0) wc[warp * kOrderKeys + k] = __popc(m);
+    }
+    __syncthreads();
+    if (b >= 0) {
+      int pos = cursor[b] + below;
+      for (int w = 0; w < warp; ++w) pos += wc[w * kOrderKeys + b];
+      order[pos] = i;
+    }
+    __syncthreads();
+    if (tid < kOrderKeys) {
+      int add = 0;
+      for (int w = 0; w < nwarps; ++w) add += wc[w * kOrderKeys + tid];
+      cursor[tid] += add;
+    }
+    __syncthreads();
+  }
+  return order;
+}
+
+// Walks this CTA's share of n units: unit k is the tile order[k / per_tile]
+// (k / per_tile without an order), part k % per_tile.  With an order, CTA b
+// takes positions b, 2G-1-b, 2G+b, ... (G CTAs); without, b, b + G, ...
+// Warp-collective (lane l prefetches the tile of the (j + l)-th unit); every
+// role walks the same sequence.
 struct UnitWalk {
-  int first, stride, n, per_tile, lane, j = 0;
+  int cta, ctas, n, per_tile, lane, j = 0;
+  const int* order;
   TileInfo c;
-  __device__ UnitWalk(int f, int s, int n_, int per, int l) : first(f), stride(s), n(n_), per_tile(per), lane(l) {}
+  __device__ UnitWalk(int b, int g, int n_, int per, int l, const int* ord)
+      : cta(b), ctas(g), n(n_), per_tile(per), lane(l), order(ord) {}
+  __device__ int pos(int jj) const {
+    return order != nullptr ? jj * ctas + ((jj & 1) ? ctas - 1 - cta : cta) : cta + jj * ctas;
+  }
   template <typename Args>
   __device__ bool next(const Args& p, TileInfo& t, int& part) {
-    const int u = first + j * stride;
+    const int u = pos(j);
     if (u >= n) return false;
     if ((j & 31) == 0) {
-      const int uu = first + (j + lane) * stride;
+      const int uu = pos(j + lane);
       c = TileInfo{0, 0, 0, 0};
-      if (uu < n) c = read_tile(p.tiles, p.offsets, p.ranks, uu / per_tile, p.T, p.R);
+      if (uu < n) {
+        const int tile = order != nullptr ? order[uu / per_tile] : uu / per_tile;
+        c = read_tile(p.tiles, p.offsets, p.ranks, tile, p.T, p.R);
+      }
     }
     const int src = j & 31;
     t.ts = __shfl_sync(0xffffffffu, c.ts, src);
@@ -203,7 +291,7 @@ __global__ void __launch_bounds__(kShThreads, 1) sgmv_shrink_unit_kernel(const _
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
   const uint32_t bar_off = static_cast<uint32_t>(kShRing + kShSlack);
-  if (static_cast<uint32_t>(smem - smem_raw) + bar_off + 512u > dynamic_smem_bytes()) {
+  if (static_cast<uint32_t>(smem - smem_raw) + bar_off + 512u + kOrderBytes > dynamic_smem_bytes()) {
     if (threadIdx.x == 0) record_error(p.err, kDevErrSmemLayout);
     return;
   }
@@ -246,10 +334,11 @@ __global__ void __launch_bounds__(kShThreads, 1) sgmv_shrink_unit_kernel(const _
   pdl_wait();
   if (threadIdx.x == 0) pdl_launch_dependents();
   const int n_units = sgmv_num_tiles(p.tiles) * p.S;
+  const int* order = order_tiles(p.tiles, p.ranks, p.T, p.R, smem + bar_off + 512);
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
-    UnitWalk walk(blockIdx.x, gridDim.x, n_units, p.S, lane);
+    UnitWalk walk(blockIdx.x, gridDim.x, n_units, p.S, lane, order);
     TileInfo u;
     int slice, issued = 0, released = 0;
     uint32_t freed = 0;
@@ -289,7 +378,7 @@ __global__ void __launch_bounds__(kShThreads, 1) sgmv_shrink_unit_kernel(const _
     }
   } else if (warp == 1) {
     // ---------------------------------------------------------- MMA issuer
-    UnitWalk walk(blockIdx.x, gridDim.x, n_units, p.S, lane);
+    UnitWalk walk(blockIdx.x, gridDim.x, n_units, p.S, lane, order);
     TileInfo u;
     int slice, cnt = 0, i = 0;
     ShRing ring;
@@ -342,7 +431,7 @@ __global__ void __launch_bounds__(kShThreads, 1) sgmv_shrink_unit_kernel(const _
     const int quad = warp & 3;  // TMEM lanes 32*quad .. 32*quad+31 = ranks
     const int j = quad * 32 + lane;
     const int et = threadIdx.x - 64;
-    UnitWalk walk(blockIdx.x, gridDim.x, n_units, p.S, lane);
+    UnitWalk walk(blockIdx.x, gridDim.x, n_units, p.S, lane, order);
     TileInfo u;
     int slice, i = 0;
     bool ok = true;
@@ -467,9 +556,10 @@ constexpr int kExOffId = 0;                          // 64 x 64 identity, K-majo
 constexpr int kExZBytes = 2 * 64 * 128;              // one z buffer: 64 token rows of hi, then of lo
 constexpr int kExOffZ = 64 * 128;
 constexpr int kExOffRing = kExOffZ + 2 * kExZBytes;
-constexpr int kExRing = 184 * 1024;
+constexpr int kExRing = 176 * 1024;
 constexpr int kExOffBar = kExOffRing + kExRing;
-constexpr int kExSmem = kExOffBar + 512 + 1024;
+constexpr int kExOffOrder = kExOffBar + 512;  // the tile order (order_tiles)
+constexpr int kExSmem = kExOffOrder + kOrderBytes + 1024;
 constexpr uint32_t kExTmemCols = 2 * kExBN;
 
 __device__ __forceinline__ int ex_drain_index(int warp) {  // -1: not a drain warp
@@ -480,10 +570,10 @@ __device__ __forceinline__ int ex_drain_index(int warp) {  // -1: not a drain wa
 // packed into a ring in unit order (a stage that would cross the end starts
 // at 0).  The producer places, the MMA issuer recomputes the same offsets; the
 // drain frees a stage once the unit's MMAs (which read all of it) have
-// completed.  z is not part of a stage: CTAs stride over groups of kExGroup
-// consecutive column chunks of a tile, and a group's z rows are loaded once
-// into one of two z buffers.  Neighbouring CTAs take neighbouring groups, so
-// the CTAs in flight cover whole rows of y and out.
+// completed.  z is not part of a stage: CTAs walk groups of kExGroup
+// consecutive column chunks of a tile (in the cost order of order_tiles), and a
+// group's z rows are loaded once into one of two z buffers.  Neighbouring CTAs
+// take neighbouring groups, so the CTAs in flight cover whole rows of y and out.
 struct ExRing {
   uint32_t head = 0;
   __device__ uint32_t place(uint32_t size, uint32_t& footprint) {
@@ -544,7 +634,7 @@ __global__ void __launch_bounds__(kExThreads, 1) sgmv_expand_unit_kernel(const _
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
-  if (static_cast<uint32_t>(smem - smem_raw) + static_cast<uint32_t>(kExOffBar) + 512u > dynamic_smem_bytes()) {
+  if (static_cast<uint32_t>(smem - smem_raw) + static_cast<uint32_t>(kExOffOrder + kOrderBytes) > dynamic_smem_bytes()) {
     if (threadIdx.x == 0) record_error(p.err, kDevErrSmemLayout);
     return;
   }
@@ -607,10 +697,11 @@ __global__ void __launch_bounds__(kExThreads, 1) sgmv_expand_unit_kernel(const _
   if (threadIdx.x == 0) pdl_launch_dependents();
   const int gpt = (p.n_chunks + p.group - 1) / p.group;  // groups per tile
   const int n_groups = sgmv_num_tiles(p.tiles) * gpt;
+  const int* order = order_tiles(p.tiles, p.ranks, p.T, p.R, smem + kExOffOrder);
 
   if (warp == kExProducer) {
     // ------------------------------------------------------------ producer
-    UnitWalk walk(blockIdx.x, gridDim.x, n_groups, gpt, lane);
+    UnitWalk walk(blockIdx.x, gridDim.x, n_groups, gpt, lane, order);
     TileInfo u;
     int grp, issued = 0, released = 0, runs = 0;
     uint32_t freed_bytes = 0;
@@ -661,7 +752,7 @@ __global__ void __launch_bounds__(kExThreads, 1) sgmv_expand_unit_kernel(const _
     }
   } else if (warp == kExIssuer) {
     // ---------------------------------------------------------- MMA issuer
-    UnitWalk walk(blockIdx.x, gridDim.x, n_groups, gpt, lane);
+    UnitWalk walk(blockIdx.x, gridDim.x, n_groups, gpt, lane, order);
     TileInfo u;
     int grp, i = 0, runs = 0;
     ExRing ring;
@@ -721,7 +812,7 @@ __global__ void __launch_bounds__(kExThreads, 1) sgmv_expand_unit_kernel(const _
     const int quad = dw & 1;        // == warp % 4: TMEM lanes quad*32.. hold tokens quad*32..
     const int cb = (dw >> 1) * 64;  // this warp's 64-column block of the unit
     const int t = quad * 32 + lane;
-    UnitWalk walk(blockIdx.x, gridDim.x, n_groups, gpt, lane);
+    UnitWalk walk(blockIdx.x, gridDim.x, n_groups, gpt, lane, order);
     TileInfo u;
     int grp, i = 0;
     bool ok = true;
@@ -816,7 +907,7 @@ int launch_shrink_units(const void* x, int64_t ldx, const void* a_flat, int64_t 
                         void* stream) {
   const int num_kb = static_cast<int>((K + kUnitBK - 1) / kUnitBK);
   const int kb_per = ((num_kb + S - 1) / S + kShKC - 1) / kShKC * kShKC;
-  const size_t smem = static_cast<size_t>(kShRing + kShSlack) + 512 + 1024;
+  const size_t smem = static_cast<size_t>(kShRing + kShSlack) + 512 + kOrderBytes + 1024;
   ShMaps maps;
   for (int h = 0; h < 8; ++h)
     if (!encode_chunk_map(&maps.a[h], a_flat, dtype, static_cast<uint64_t>(a_rows), static_cast<uint64_t>(K),
