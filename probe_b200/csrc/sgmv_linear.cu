@@ -65,7 +65,7 @@ struct SlArgs {
 // output tile's slots into mt_first, a block-wide scan turns the counts into
 // first-slot offsets, pass 2 writes the slot records.  Every load of a pass is
 // independent of the others, so a pass costs a few memory latencies.
-constexpr int kSlPieceThreads = 256;
+constexpr int kSlPieceThreads = 1024;  // a warp per output tile up to 32 of them (8192 tokens): one walk each
 constexpr int kSlPieceWarps = kSlPieceThreads / 32;
 
 struct PieceWalk {
