@@ -882,13 +882,11 @@ namespace {
 // per slice, at most 16 slices.  It depends on T and K only, so per-token ids
 // and segment tables describing the same batch sum their partials alike and
 // give bit-identical results.
-// per_sm: 4 for the standalone shrink and the fused linear's slot fill;
-// 1 for the one-call branch, whose reduce and expand follow at once: fewer,
+// One unit per SM: with the units in cost order (order_tiles), fewer and
 // longer units keep more of a CTA's stages in flight and leave fewer partial
-// slices to sum (C3: 64.7 against 67.8 us per branch call; the fused linear
-// measured 158.2 against 155.4 us the other way round).
-constexpr int kUnitsPerSm = 4;
-constexpr int kBranchUnitsPerSm = 1;
+// slices to sum (C3: branch 64.9 against 67.6 us per call, fused linear
+// 152-154 against 155 us, than four per SM).
+constexpr int kUnitsPerSm = 1;
 
 int unit_slices(int64_t T, int64_t K, int num_sms, int per_sm) {
   const int64_t kb = std::max<int64_t>((K + kUnitBK - 1) / kUnitBK, 1);
@@ -1069,7 +1067,7 @@ int launch_sgmv_shrink_unit(const void* x, int64_t ldx, const void* a_flat, int6
 }
 
 size_t sgmv_unit_branch_workspace(int64_t T, int64_t K, int64_t r_max, int64_t max_tiles, int num_sms) {
-  return partial_bytes(unit_slices(T, K, num_sms, kBranchUnitsPerSm), T, r_max) +
+  return partial_bytes(unit_slices(T, K, num_sms, kUnitsPerSm), T, r_max) +
          static_cast<size_t>(T) * 2 * kExZW * 2;
 }
 
@@ -1088,7 +1086,7 @@ int launch_sgmv_branch_unit(const void* x, int64_t ldx, const void* y, int64_t l
   if (workspace == nullptr || !unit_al16(workspace) ||
       workspace_bytes < sgmv_unit_branch_workspace(T, K, r_max, max_tiles, num_sms))
     return LORA_ERR_UNSUPPORTED;
-  const int S = unit_slices(T, K, num_sms, kBranchUnitsPerSm);
+  const int S = unit_slices(T, K, num_sms, kUnitsPerSm);
   float* partial = static_cast<float*>(workspace);
   void* z_hl = static_cast<char*>(workspace) + partial_bytes(S, T, r_max);
   int rc = launch_shrink_units(x, ldx, a_flat, lda, a_rows, offsets, ranks, tiles, max_tiles, partial, T, K, r_max, S,
