@@ -1,5 +1,6 @@
-"""Unit-scheduled segmented shrink (GPU): (tile, K slice) units over persistent
-CTAs, split-K reduced by the last slice of each tile.
+"""Unit-scheduled segmented shrink and branch (GPU): (tile, K slice) units over
+persistent CTAs in a cost-sorted snake order (schedule order past 1024 tiles),
+partials summed in slice order.
 
 Cases reach its edges: one-token tiles (random per-token ids), a last tile cut
 by T, K not a multiple of 64, ranks 1..128 (stage layouts for r_max <= 64 and
@@ -42,6 +43,7 @@ def _run(x, a, offs, rk, ids, r_max, split_k, z_dtype=torch.float32, scale=0.7):
     (777, 520, [64, 13, 0, 33], "runs", 3),              # K % 64 != 0, rank 0, last tile cut by T
     (300, 1024, [128, 96, 1, 127], "runs", 16),          # r_max > 64: wider stages
     (64, 2048, [16], "runs", 2),                         # one tile
+    (3000, 512, [4, 8, 16, 32, 64], "random", 0),        # > 1024 tiles: units in schedule order, no sort
     (4096, 4096, [4, 8, 16, 32, 64] * 12 + [8] * 4, "zipf", 0),  # C3-like, default split
 ])
 def test_unit_shrink_matches_oracle(t, k, ranks, mode, split_k):
@@ -105,6 +107,7 @@ def _branch_case(t, k, n, ranks, ids, seed, with_y=True):
     (1000, 1024, 320, [4, 8, 16, 32, 64], "random", True),                # one-token tiles, N % 256 != 0
     (777, 576, 512, [64, 13, 0, 33], "runs", True),                      # rank 0, last tile cut by T
     (300, 256, 1024, [16, 48], "runs", False),                           # y = None
+    (3000, 512, 256, [4, 8, 16, 32, 64], "random", True),                # > 1024 tiles: schedule order, no sort
 ])
 def test_unit_branch_matches_oracle(t, k, n, ranks, mode, with_y):
     from oracle import checks
