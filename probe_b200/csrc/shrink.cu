@@ -414,8 +414,8 @@ extern "C" int lora_sgmv_pick_split_k(int64_t T, int64_t K, int64_t r_max) {
 extern "C" size_t lora_sgmv_shrink_workspace_size(int64_t T, int64_t S, int64_t z_width, int split_k) {
   if (T <= 0 || z_width <= 0) return 256;
   // the unit-scheduled tensor-core shrink keeps its partials after the
-  // counter region; its K split (<= 16, about four units per SM over the
-  // tile capacity) is bounded here without K
+  // counter region; its K split (<= 16, about one unit per SM over the tile
+  // capacity) is bounded here without K, by four units per SM
   const int dev = current_device();
   const int sms = dev >= 0 ? device_info(dev).num_sms : 148;
   const int64_t blocks = std::max<int64_t>((T + 63) / 64, 1);
