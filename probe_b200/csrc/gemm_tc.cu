@@ -727,7 +727,14 @@ int launch_gemm_pair(const void* x, int64_t ldx, const void* w, int64_t ldw, con
   a.num_n_tiles = static_cast<int>((N + 256 * NW - 1) / (256 * NW));
   a.num_tiles = a.num_m_tiles * a.num_n_tiles;
   a.group_m = env_int("LORA_B200_GROUP_M", 8);
-  a.l2_hints = env_int("LORA_B200_L2_HINTS", 0);
+  // W (and B_dup) with L2 evict_last when W is large: it is re-read by every
+  // band of M tiles while x streams through once (measured on B200 with the
+  // replays of both settings interleaved: 32760 x 5120 -> 13824 4193 -> 3971 us,
+  // 13824 -> 5120 3961 -> 3888, 5120 -> 5120 1530 -> 1505; 4096^3 unchanged,
+  // 1536 x 1536 1.3 % slower).  LORA_B200_L2_HINTS (bit 0: W evict_last, bit 1:
+  // x evict_first) overrides.
+  const int64_t w_bytes = (N * K + N * R) * 2;
+  a.l2_hints = env_int("LORA_B200_L2_HINTS", w_bytes >= (int64_t{48} << 20) ? 1 : 0);
   a.alpha = alpha;
 
   auto kernel = gemm_tc2_kernel<STAGES, NW, EW, T>;
