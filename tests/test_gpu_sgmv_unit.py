@@ -134,6 +134,26 @@ def test_unit_branch_matches_oracle(t, k, n, ranks, mode, with_y):
     assert _lib.device_error() == 0
 
 
+def test_unit_branch_fp16():
+    """fp16 operands through the one-call branch (the identity pass that adds y
+    and the hi/lo z pair in half precision), with and without y."""
+    from oracle import checks
+
+    t, k, n = 700, 512, 768
+    ranks = [16, 64, 8, 33]
+    ids = np.repeat(np.random.default_rng(3).integers(0, len(ranks), size=t // 50 + 1), 50)[:t]
+    x, y, a, b, offs, rk = _branch_case(t, k, n, ranks, ids, seed=31)
+    x, y, a, b = x.half(), y.half(), a.half(), b.half()
+    tiles, s = kernels.sgmv_schedule(t, offs.numel(), ids=torch.as_tensor(ids, device=DEV))
+    for yy in (y, None):
+        out = kernels.sgmv_branch(x, yy, a, b, offs, rk, tiles, s, max(ranks))
+        assert out is not None and out.dtype == torch.float16
+        ref_y = yy if yy is not None else torch.zeros((t, n), device=DEV, dtype=torch.float16)
+        rep = checks.branch_report(out, x, ref_y, a, b, offs, rk, ids, dtype="f16", n_random=64)
+        assert rep["ok"], rep
+    assert _lib.device_error() == 0
+
+
 def test_unit_branch_declines_outside_its_domain():
     """Ranks above 64, N or K not a multiple of 64: the one-call branch declines and
     the public branch surfaces take shrink + expand instead (same results)."""
