@@ -731,8 +731,8 @@ int launch_gemm_pair(const void* x, int64_t ldx, const void* w, int64_t ldw, con
   // band of M tiles while x streams through once (measured on B200 with the
   // replays of both settings interleaved: 32760 x 5120 -> 13824 4193 -> 3971 us,
   // 13824 -> 5120 3961 -> 3888, 5120 -> 5120 1530 -> 1505; 4096^3 unchanged,
-  // 1536 x 1536 1.3 % slower).  LORA_B200_L2_HINTS (bit 0: W evict_last, bit 1:
-  // x evict_first) overrides.
+  // 1536 x 1536 1.3 % slower).  LORA_B200_L2_HINTS overrides (1: W evict_last,
+  // 2: x evict_first, 4: output stores evict_first).
   const int64_t w_bytes = (N * K + N * R) * 2;
   a.l2_hints = env_int("LORA_B200_L2_HINTS", w_bytes >= (int64_t{48} << 20) ? 1 : 0);
   a.alpha = alpha;
